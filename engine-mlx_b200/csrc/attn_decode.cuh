@@ -1,0 +1,31 @@
+// attn_decode.cuh — batch-1 decode attention (flash-decode, split KV).
+#pragma once
+#include "common.cuh"
+
+namespace emx {
+
+struct AttnDecodeArgs {
+  const bf16* qkv;        // fused projection output [ (nq + 2*nkv) * head_dim ], q | k | v
+  const bf16* q_norm;     // [head_dim] or nullptr
+  const bf16* k_norm;     // [head_dim] or nullptr
+  float eps;
+  const float* inv_freq;  // rope inverse frequencies [head_dim/2]
+  bf16* kc;               // this layer's K cache [nkv, cap, head_dim]
+  bf16* vc;               // this layer's V cache
+  int cap;
+  int nq, nkv, head_dim;
+  const int* pos;         // device-held offset: row of the new token (nullptr: pos_host)
+  int pos_host;
+  const bf16* q_in;       // non-null: final q heads [nq, head_dim] (no norm/rope, no cache write)
+  float scale;
+  bf16* out;              // attention output [nq * head_dim]
+  float* part;            // split partials [nkv][splits][nq/nkv][head_dim + 2]
+  unsigned* ticket;       // [nkv], zero between launches
+  int splits;
+  int* status;
+};
+
+int attn_decode_splits(int nkv, int num_sms);
+cudaError_t attn_decode_launch(const AttnDecodeArgs& a, cudaStream_t st, bool pdl);
+
+}  // namespace emx

@@ -1,0 +1,526 @@
+// misc.cu — standalone kernels: MLX affine (de)quantization, the seeded
+// generator, RMSNorm, RoPE, SwiGLU pieces, argmax, softmax, embedding gather,
+// the prefill q/k/v post-processing and static-cache writes.
+//
+// Each restates one mlx-c op the reference calls through MlxCtx
+// (crates/mlx-ffi/src/ops/real/*): dequantize_weight (transform.rs:95-109),
+// rms_norm (blas.rs:5-9), grouped_rms_norm (grouped_norm.rs:50-135),
+// rope_dynamic (blas.rs:75-80), silu (blas.rs:33-37), multiply/add
+// (blas.rs:17-31), argmax (array.rs:6-10), softmax_axis (elementwise.rs:68-72),
+// take/embed (core.rs:5-14), slice_update / scatter_single (slice.rs:78-115).
+#include "misc.cuh"
+
+namespace emx {
+
+namespace {
+
+__device__ __forceinline__ uint64_t splitmix64(uint64_t x) {
+  x += 0x9E3779B97F4A7C15ull;
+  x = (x ^ (x >> 30)) * 0xBF58476D1CE4E5B9ull;
+  x = (x ^ (x >> 27)) * 0x94D049BB133111EBull;
+  return x ^ (x >> 31);
+}
+
+// Irwin-Hall(12) normal variate from three 64-bit hashes: the integer sum is
+// exact, the int->float conversion and the 2^-16 scale are exact, so only
+// std*z and mean+y round — identical on any IEEE host.
+__device__ __forceinline__ float normal_at(uint64_t key, uint64_t i, float mean, float std) {
+  uint32_t s = 0;
+#pragma unroll
+  for (int j = 0; j < 3; ++j) {
+    const uint64_t h = splitmix64(key + 3ull * i + (uint64_t)j);
+    s += (uint32_t)(h & 0xffff) + (uint32_t)((h >> 16) & 0xffff) + (uint32_t)((h >> 32) & 0xffff) +
+         (uint32_t)(h >> 48);
+  }
+  const int t = (int)s - 393210;
+  const float z = __fmul_rn(__int2float_rn(t), 1.0f / 65536.0f);
+  return __fadd_rn(mean, __fmul_rn(std, z));
+}
+
+inline uint64_t stream_key(uint64_t seed, uint64_t stream) {
+  auto sm = [](uint64_t x) {
+    x += 0x9E3779B97F4A7C15ull;
+    x = (x ^ (x >> 30)) * 0xBF58476D1CE4E5B9ull;
+    x = (x ^ (x >> 27)) * 0x94D049BB133111EBull;
+    return x ^ (x >> 31);
+  };
+  return sm(seed ^ sm(stream));
+}
+
+inline int blocks_for(size_t n, int threads) {
+  size_t b = (n + threads - 1) / threads;
+  if (b > (size_t)(1u << 30)) b = (size_t)(1u << 30);
+  return (int)(b ? b : 1);
+}
+
+__global__ void dequant_kernel(const uint32_t* w, const bf16* s, const bf16* b, bf16* out, int N, int K, int gs,
+                               int bits) {
+  const int per = 32 / bits;
+  const int ng = K / gs;
+  const size_t total = (size_t)N * K;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const int n = (int)(i / K), k = (int)(i % K);
+    const uint32_t word = w[(size_t)n * (K / per) + k / per];
+    const uint32_t q = (word >> (bits * (k % per))) & ((1u << bits) - 1u);
+    out[i] = dequant1(q, s[(size_t)n * ng + k / gs], b[(size_t)n * ng + k / gs]);
+  }
+}
+
+// One thread per (row, group): min/max, scale/bias in bf16, then the codes.
+// GEN: values are the generator's elements (row0 + n) * K_full + col0 + k of
+// a [*, K_full] tensor, i.e. the shard [row0.., col0..col0+K) of the full one.
+template <bool GEN>
+__global__ void quant_kernel(const float* src_f, const bf16* src_b, uint64_t key, float std, uint32_t* w, bf16* s,
+                             bf16* b, int N, int K, int gs, int bits, size_t row0, int col0, int K_full) {
+  const int ng = K / gs;
+  const size_t total = (size_t)N * ng;
+  const int per = 32 / bits;
+  const float maxq = (float)((1 << bits) - 1);
+  for (size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x; idx < total;
+       idx += (size_t)gridDim.x * blockDim.x) {
+    const int n = (int)(idx / ng), g = (int)(idx % ng);
+    const size_t base = (size_t)n * K + (size_t)g * gs;
+    const size_t gbase = (row0 + n) * (size_t)K_full + col0 + (size_t)g * gs;
+    auto val = [&](int i) -> float {
+      if (GEN) return normal_at(key, gbase + i, 0.0f, std);
+      return src_f ? src_f[base + i] : bf2f(src_b[base + i]);
+    };
+    float mn = val(0), mx = mn;
+    for (int i = 1; i < gs; ++i) {
+      const float v = val(i);
+      mn = v < mn ? v : mn;
+      mx = v > mx ? v : mx;
+    }
+    const float scale = __fdiv_rn(__fsub_rn(mx, mn), maxq);
+    const bf16 sb = f2bf(scale), bb = f2bf(mn);
+    s[idx] = sb;
+    b[idx] = bb;
+    const float sf = bf2f(sb), bf = bf2f(bb);
+    uint32_t* wr = w + (size_t)n * (K / per) + (size_t)g * gs / per;
+    for (int wi = 0; wi < gs / per; ++wi) {
+      uint32_t word = 0;
+      for (int e = 0; e < per; ++e) {
+        float q = 0.0f;
+        if (sf > 0.0f) {
+          q = rintf(__fdiv_rn(__fsub_rn(val(wi * per + e), bf), sf));
+          q = q < 0.0f ? 0.0f : (q > maxq ? maxq : q);
+        }
+        word |= ((uint32_t)q) << (bits * e);
+      }
+      wr[wi] = word;
+    }
+  }
+}
+
+template <typename T>
+__global__ void fill_normal_kernel(uint64_t key, size_t n, float mean, float std, T* out) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+    const float v = normal_at(key, i, mean, std);
+    if constexpr (sizeof(T) == 4) out[i] = v;
+    else out[i] = f2bf(v);
+  }
+}
+
+__global__ void rms_norm_kernel(const bf16* x, const bf16* w, bf16* out, int dims, float eps, int groups) {
+  __shared__ float red[32];
+  const bf16* xr = x + (size_t)blockIdx.x * dims;
+  bf16* orow = out + (size_t)blockIdx.x * dims;
+  const int gd = dims / groups;
+  for (int gi = 0; gi < groups; ++gi) {
+    float ss = 0.f;
+    for (int k = gi * gd + threadIdx.x; k < (gi + 1) * gd; k += blockDim.x) {
+      const float v = bf2f(xr[k]);
+      ss = fmaf(v, v, ss);
+    }
+    ss = block_sum(ss, red);
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)gd), eps)));
+    for (int k = gi * gd + threadIdx.x; k < (gi + 1) * gd; k += blockDim.x) {
+      const float v = bf2f(xr[k]);
+      float o;
+      if (groups == 1) o = __fmul_rn(bfround(__fmul_rn(v, inv)), bf2f(w[k]));
+      else o = __fmul_rn(__fmul_rn(v, inv), bf2f(w[k]));
+      orow[k] = f2bf(o);
+    }
+  }
+}
+
+__global__ void rope_kernel(const bf16* x, bf16* out, int heads, int T, int dims, const float* inv_freq, int offset,
+                            const int* offset_dev) {
+  const int half = dims / 2;
+  const size_t total = (size_t)heads * T * half;
+  const int off = offset + (offset_dev ? *offset_dev : 0);
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const int d = (int)(i % half);
+    const size_t row = i / half;
+    const int t = (int)(row % T);
+    const bf16* xr = x + row * dims;
+    const float th = __fmul_rn((float)(off + t), inv_freq[d]);
+    float sn, cs;
+    sincosf(th, &sn, &cs);
+    const float x1 = bf2f(xr[d]), x2 = bf2f(xr[d + half]);
+    out[row * dims + d] = f2bf(__fsub_rn(__fmul_rn(x1, cs), __fmul_rn(x2, sn)));
+    out[row * dims + d + half] = f2bf(__fadd_rn(__fmul_rn(x1, sn), __fmul_rn(x2, cs)));
+  }
+}
+
+__global__ void inv_freq_kernel(float* inv, int dims, float theta) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < dims / 2) inv[i] = (float)pow((double)theta, -2.0 * (double)i / (double)dims);
+}
+
+__global__ void silu_kernel(const bf16* x, bf16* out, size_t n) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+    const float v = bf2f(x[i]);
+    out[i] = f2bf(__fmul_rn(v, bfround(sigmoid_f(v))));
+  }
+}
+
+__global__ void binop_kernel(const bf16* a, const bf16* b, bf16* out, size_t n, int op) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+    const float x = bf2f(a[i]), y = bf2f(b[i]);
+    out[i] = f2bf(op == 0 ? __fmul_rn(x, y) : __fadd_rn(x, y));
+  }
+}
+
+__global__ void argmax_kernel(const bf16* x, int n, int* out) {
+  const bf16* xr = x + (size_t)blockIdx.x * n;
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float v = bf2f(xr[i]);
+    if (v == v && (v > bv || (v == bv && i < bi))) {
+      bv = v;
+      bi = i;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > bv || (ov == bv && oi < bi)) {
+      bv = ov;
+      bi = oi;
+    }
+  }
+  __shared__ float wv[32];
+  __shared__ int wi[32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane == 0) {
+    wv[warp] = bv;
+    wi[warp] = bi;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
+      if (wv[w] > bv || (wv[w] == bv && wi[w] < bi)) {
+        bv = wv[w];
+        bi = wi[w];
+      }
+    out[blockIdx.x] = bi == 0x7fffffff ? 0 : bi;
+  }
+}
+
+__global__ void softmax_kernel(const bf16* x, bf16* out, int n) {
+  __shared__ float red[32];
+  const bf16* xr = x + (size_t)blockIdx.x * n;
+  bf16* orow = out + (size_t)blockIdx.x * n;
+  float m = -INFINITY;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) m = fmaxf(m, bf2f(xr[i]));
+  m = warp_max(m);
+  __shared__ float wm[32];
+  if ((threadIdx.x & 31) == 0) wm[threadIdx.x >> 5] = m;
+  __syncthreads();
+  m = -INFINITY;
+  for (int w = 0; w < (int)(blockDim.x >> 5); ++w) m = fmaxf(m, wm[w]);
+  float s = 0.f;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) s += expf(bf2f(xr[i]) - m);
+  s = block_sum(s, red);
+  for (int i = threadIdx.x; i < n; i += blockDim.x) orow[i] = f2bf(__fdiv_rn(expf(bf2f(xr[i]) - m), s));
+}
+
+__global__ void embed_kernel(const uint32_t* w, const bf16* s, const bf16* b, const int* ids, int hidden, int gs,
+                             int bits, int vocab, bf16* out, int* status) {
+  const int t = blockIdx.x;
+  int id = ids[t];
+  if (id < 0 || id >= vocab) {
+    if (threadIdx.x == 0) report_status(status, kDevBadToken);
+    id = 0;
+  }
+  const int per = 32 / bits, ng = hidden / gs;
+  for (int k = threadIdx.x; k < hidden; k += blockDim.x) {
+    const uint32_t word = w[(size_t)id * (hidden / per) + k / per];
+    const uint32_t q = (word >> (bits * (k % per))) & ((1u << bits) - 1u);
+    out[(size_t)t * hidden + k] = dequant1(q, s[(size_t)id * ng + k / gs], b[(size_t)id * ng + k / gs]);
+  }
+}
+
+// One warp per (token, head): heads [0, nq) are q, [nq, nq+nkv) are k (normed,
+// roped, written to the cache), [nq+nkv, nq+2nkv) are v (copied to the cache).
+__global__ void prefill_qkv_kernel(const PrefillQkvArgs a) {
+  const int lane = threadIdx.x & 31;
+  const int items_per_tok = a.nq + 2 * a.nkv;
+  const int item = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (item >= a.T * items_per_tok) return;
+  const int t = item / items_per_tok, h = item % items_per_tok;
+  const int hd = a.hd;  // 128
+  const bf16* src = a.qkv + (size_t)t * items_per_tok * hd + (size_t)h * hd;
+  const int pos = a.offset + t;
+  if (h >= a.nq + a.nkv) {
+    const int kvh = h - a.nq - a.nkv;
+    bf16* dst = a.vc + ((size_t)kvh * a.cap + pos) * hd;
+    for (int d = lane; d < hd; d += 32) dst[d] = src[d];
+    return;
+  }
+  const bool is_k = h >= a.nq;
+  const bf16* nw = is_k ? a.k_norm : a.q_norm;
+  float v[4];
+  float ss = 0.f;
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    v[e] = bf2f(src[lane * 4 + e]);
+    ss = fmaf(v[e], v[e], ss);
+  }
+  ss = warp_sum(ss);
+  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)hd), a.eps)));
+  float nv[4], pv[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const int d = lane * 4 + e;
+    nv[e] = nw ? bfround(__fmul_rn(bfround(__fmul_rn(v[e], inv)), bf2f(nw[d]))) : v[e];
+  }
+#pragma unroll
+  for (int e = 0; e < 4; ++e) pv[e] = __shfl_xor_sync(0xffffffffu, nv[e], 16);
+  const float fp = (float)pos;
+  bf16* dst = is_k ? a.kc + ((size_t)(h - a.nq) * a.cap + pos) * hd : a.q_out + ((size_t)h * a.T + t) * hd;
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const int d = lane * 4 + e;
+    const int i = d & (hd / 2 - 1);
+    const float th = __fmul_rn(fp, a.inv_freq[i]);
+    float sn, cs;
+    sincosf(th, &sn, &cs);
+    float o;
+    if (d < hd / 2) o = __fsub_rn(__fmul_rn(nv[e], cs), __fmul_rn(pv[e], sn));
+    else o = __fadd_rn(__fmul_rn(pv[e], sn), __fmul_rn(nv[e], cs));
+    dst[d] = f2bf(o);
+  }
+}
+
+__global__ void slice_update_kernel(bf16* cache, const bf16* upd, int nkv, int cap, int D, int offset,
+                                    const int* offset_dev, int T) {
+  const int off = offset + (offset_dev ? *offset_dev : 0);
+  const size_t total = (size_t)nkv * T * D;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const int d = (int)(i % D);
+    const int t = (int)((i / D) % T);
+    const int h = (int)(i / ((size_t)D * T));
+    if (off + t < cap) cache[((size_t)h * cap + off + t) * D + d] = upd[i];
+  }
+}
+
+__global__ void moe_route_kernel(const bf16* logits, int E, int k, int normalize, int e_base, int e_local, int* idx,
+                                 float* w, int* n) {
+  __shared__ float pr[1024];
+  __shared__ float red[32];
+  pdl_trigger();
+  pdl_wait();
+  float m = -INFINITY;
+  for (int i = threadIdx.x; i < E; i += blockDim.x) m = fmaxf(m, bf2f(logits[i]));
+  m = warp_max(m);
+  __shared__ float wm[32];
+  if ((threadIdx.x & 31) == 0) wm[threadIdx.x >> 5] = m;
+  __syncthreads();
+  m = -INFINITY;
+  for (int i = 0; i < (int)(blockDim.x >> 5); ++i) m = fmaxf(m, wm[i]);
+  float s = 0.f;
+  for (int i = threadIdx.x; i < E; i += blockDim.x) s += expf(bf2f(logits[i]) - m);
+  s = block_sum(s, red);
+  for (int i = threadIdx.x; i < E; i += blockDim.x) pr[i] = bfround(__fdiv_rn(expf(bf2f(logits[i]) - m), s));
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int sel[64];
+    float sw[64];
+    for (int r = 0; r < k; ++r) {
+      int bi = -1;
+      float bv = -INFINITY;
+      for (int i = 0; i < E; ++i)
+        if (pr[i] > bv || (bi < 0 && pr[i] == bv)) {
+          bv = pr[i];
+          bi = i;
+        }
+      if (bi < 0) bi = 0;
+      sel[r] = bi;
+      sw[r] = pr[bi];
+      pr[bi] = -INFINITY;
+    }
+    if (normalize) {
+      float sum = 0.f;
+      for (int r = 0; r < k; ++r) sum = __fadd_rn(sum, sw[r]);
+      if (sum > 1e-20f)
+        for (int r = 0; r < k; ++r) sw[r] = __fdiv_rn(sw[r], sum);
+    }
+    int j = 0;
+    for (int r = 0; r < k; ++r) {
+      if (sel[r] >= e_base && sel[r] < e_base + e_local) {
+        idx[j] = sel[r] - e_base;
+        w[j] = sw[r];
+        ++j;
+      }
+    }
+    *n = j;
+  }
+}
+
+__global__ void moe_combine_kernel(const bf16* y, const float* w, const int* n, int H, float* out) {
+  pdl_trigger();
+  pdl_wait();
+  const int ns = *n;
+  for (int k = blockIdx.x * blockDim.x + threadIdx.x; k < H; k += gridDim.x * blockDim.x) {
+    float acc = 0.f;
+    for (int s = 0; s < ns; ++s) acc = __fadd_rn(acc, __fmul_rn(bf2f(y[(size_t)s * H + k]), w[s]));
+    out[k] = acc;
+  }
+}
+
+cudaError_t launch_pdl(const void* fn, dim3 grid, dim3 block, void** args, cudaStream_t st, bool pdl) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelExC(&cfg, fn, args);
+}
+
+}  // namespace
+
+cudaError_t k_moe_route(const bf16* logits, int E, int k, int normalize, int e_base, int e_local, int* idx,
+                        float* w, int* n, cudaStream_t st, bool pdl) {
+  if (E <= 0 || E > 1024 || k <= 0 || k > 64 || k > E) return cudaErrorInvalidValue;
+  void* args[] = {(void*)&logits, (void*)&E, (void*)&k, (void*)&normalize, (void*)&e_base, (void*)&e_local,
+                  (void*)&idx, (void*)&w, (void*)&n};
+  return launch_pdl((const void*)moe_route_kernel, dim3(1), dim3(256), args, st, pdl);
+}
+
+cudaError_t k_moe_combine(const bf16* y, const float* w, const int* n, int H, float* out, cudaStream_t st, bool pdl) {
+  void* args[] = {(void*)&y, (void*)&w, (void*)&n, (void*)&H, (void*)&out};
+  return launch_pdl((const void*)moe_combine_kernel, dim3((H + 255) / 256), dim3(256), args, st, pdl);
+}
+
+cudaError_t k_dequantize(const uint32_t* w, const bf16* s, const bf16* b, bf16* out, int N, int K, int gs, int bits,
+                         cudaStream_t st) {
+  dequant_kernel<<<blocks_for((size_t)N * K, 256), 256, 0, st>>>(w, s, b, out, N, K, gs, bits);
+  return cudaGetLastError();
+}
+
+cudaError_t k_quantize(const float* src_f32, const bf16* src_bf16, uint32_t* w, bf16* s, bf16* b, int N, int K,
+                       int gs, int bits, cudaStream_t st) {
+  quant_kernel<false><<<blocks_for((size_t)N * (K / gs), 128), 128, 0, st>>>(src_f32, src_bf16, 0, 0.f, w, s, b, N,
+                                                                             K, gs, bits, 0, 0, K);
+  return cudaGetLastError();
+}
+
+cudaError_t k_fill_normal_f32(uint64_t seed, uint64_t stream, size_t n, float mean, float std, float* out,
+                              cudaStream_t st) {
+  fill_normal_kernel<float><<<blocks_for(n, 256), 256, 0, st>>>(stream_key(seed, stream), n, mean, std, out);
+  return cudaGetLastError();
+}
+
+cudaError_t k_fill_normal_bf16(uint64_t seed, uint64_t stream, size_t n, float mean, float std, bf16* out,
+                               cudaStream_t st) {
+  fill_normal_kernel<bf16><<<blocks_for(n, 256), 256, 0, st>>>(stream_key(seed, stream), n, mean, std, out);
+  return cudaGetLastError();
+}
+
+cudaError_t k_fill_quantized(uint64_t seed, uint64_t stream, int N, int K, int gs, int bits, float std, uint32_t* w,
+                             bf16* s, bf16* b, cudaStream_t st) {
+  return k_fill_quantized_shard(seed, stream, N, K, K, 0, 0, gs, bits, std, w, s, b, K, st);
+}
+
+cudaError_t k_fill_quantized_shard(uint64_t seed, uint64_t stream, int n_rows, int n_cols, int K_full, size_t row0,
+                                   int col0, int gs, int bits, float std, uint32_t* w, bf16* s, bf16* b, int ldK,
+                                   cudaStream_t st) {
+  if (ldK != n_cols) return cudaErrorInvalidValue;
+  if (n_rows <= 0) return cudaSuccess;
+  quant_kernel<true><<<blocks_for((size_t)n_rows * (n_cols / gs), 128), 128, 0, st>>>(
+      nullptr, nullptr, stream_key(seed, stream), std, w, s, b, n_rows, n_cols, gs, bits, row0, col0, K_full);
+  return cudaGetLastError();
+}
+
+cudaError_t k_rms_norm(const bf16* x, const bf16* w, bf16* out, int rows, int dims, float eps, int groups,
+                       cudaStream_t st) {
+  if (rows <= 0) return cudaSuccess;
+  rms_norm_kernel<<<rows, 256, 0, st>>>(x, w, out, dims, eps, groups);
+  return cudaGetLastError();
+}
+
+cudaError_t k_rope(const bf16* x, bf16* out, int heads, int T, int dims, const float* inv_freq, int offset,
+                   const int* offset_dev, cudaStream_t st) {
+  const size_t n = (size_t)heads * T * (dims / 2);
+  if (!n) return cudaSuccess;
+  rope_kernel<<<blocks_for(n, 256), 256, 0, st>>>(x, out, heads, T, dims, inv_freq, offset, offset_dev);
+  return cudaGetLastError();
+}
+
+cudaError_t k_rope_inv_freq(float* inv_freq, int dims, float theta, cudaStream_t st) {
+  inv_freq_kernel<<<(dims / 2 + 127) / 128, 128, 0, st>>>(inv_freq, dims, theta);
+  return cudaGetLastError();
+}
+
+cudaError_t k_silu(const bf16* x, bf16* out, size_t n, cudaStream_t st) {
+  if (!n) return cudaSuccess;
+  silu_kernel<<<blocks_for(n, 256), 256, 0, st>>>(x, out, n);
+  return cudaGetLastError();
+}
+
+cudaError_t k_multiply(const bf16* a, const bf16* b, bf16* out, size_t n, cudaStream_t st) {
+  if (!n) return cudaSuccess;
+  binop_kernel<<<blocks_for(n, 256), 256, 0, st>>>(a, b, out, n, 0);
+  return cudaGetLastError();
+}
+
+cudaError_t k_add(const bf16* a, const bf16* b, bf16* out, size_t n, cudaStream_t st) {
+  if (!n) return cudaSuccess;
+  binop_kernel<<<blocks_for(n, 256), 256, 0, st>>>(a, b, out, n, 1);
+  return cudaGetLastError();
+}
+
+cudaError_t k_argmax(const bf16* x, int rows, int n, int* out, cudaStream_t st) {
+  if (rows <= 0) return cudaSuccess;
+  argmax_kernel<<<rows, 1024, 0, st>>>(x, n, out);
+  return cudaGetLastError();
+}
+
+cudaError_t k_softmax(const bf16* x, bf16* out, int rows, int n, cudaStream_t st) {
+  if (rows <= 0) return cudaSuccess;
+  softmax_kernel<<<rows, 256, 0, st>>>(x, out, n);
+  return cudaGetLastError();
+}
+
+cudaError_t k_embed(const uint32_t* w, const bf16* s, const bf16* b, const int* ids, int T, int hidden, int gs,
+                    int bits, int vocab, bf16* out, int* status, cudaStream_t st) {
+  if (T <= 0) return cudaSuccess;
+  embed_kernel<<<T, 256, 0, st>>>(w, s, b, ids, hidden, gs, bits, vocab, out, status);
+  return cudaGetLastError();
+}
+
+cudaError_t k_prefill_qkv(const PrefillQkvArgs& a, cudaStream_t st) {
+  if (a.hd != 128) return cudaErrorInvalidValue;
+  const int items = a.T * (a.nq + 2 * a.nkv);
+  if (!items) return cudaSuccess;
+  prefill_qkv_kernel<<<(items + 7) / 8, 256, 0, st>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t k_slice_update(bf16* cache, const bf16* upd, int nkv, int cap, int D, int offset, const int* offset_dev,
+                           int T, cudaStream_t st) {
+  const size_t n = (size_t)nkv * T * D;
+  if (!n) return cudaSuccess;
+  slice_update_kernel<<<blocks_for(n, 256), 256, 0, st>>>(cache, upd, nkv, cap, D, offset, offset_dev, T);
+  return cudaGetLastError();
+}
+
+}  // namespace emx

@@ -1,0 +1,933 @@
+// qwen3.cu — the Qwen3 engine behind the C ABI: what crates/serve's
+// Qwen3Engine does through MlxCtx, re-designed for one B200 (or a tensor- /
+// expert-parallel group of them).
+//
+//   reference                                   here
+//   ------------------------------------------  -------------------------------------------
+//   load_weights_from_manifest + load-time      emx_qwen3_load_tensor: MLX checkpoint names,
+//   q/k/v and gate/up fusion                    q|k|v and gate|up fused into one device
+//   (loader/weights.rs:17-284, fusion.rs:24-59) tensor each; each rank keeps its shard
+//   alloc_kv_static (engine_ext.rs:267-306)     one bf16 KV allocation [L][2][n_kv][cap][128]
+//   static mask + offset arrays                 device-held offset (no mask: rows <= offset)
+//   compile_shapeless(build_step)               one decode step captured as a CUDA graph
+//   (compiled.rs:79-287)                        (5 kernels per layer + lm_head, chained by PDL)
+//   prefill (forward_qwen3.rs:12-200)           eager stream-ordered prefill
+//   argmax in-graph + to_vec_u32                argmax fused into the lm_head GEMV; 4-byte D2H
+#include <cstring>
+#include <map>
+#include <string>
+#include <vector>
+
+#include "attn_decode.cuh"
+#include "attn_prefill.cuh"
+#include "comm.cuh"
+#include "ctx.cuh"
+#include "misc.cuh"
+#include "qgemm.cuh"
+#include "qgemv.cuh"
+
+namespace emx {
+
+struct QW {
+  uint32_t* w = nullptr;
+  bf16* s = nullptr;
+  bf16* b = nullptr;
+  int N = 0, K = 0, bits = 4, gs = 64;
+  size_t wbytes() const { return (size_t)N * K / (32 / bits) * 4; }
+  size_t sbytes() const { return (size_t)N * (K / gs) * 2; }
+};
+
+struct LayerW {
+  bf16* in_norm = nullptr;
+  bf16* post_norm = nullptr;
+  bf16* q_norm = nullptr;
+  bf16* k_norm = nullptr;
+  QW qkv, o, gate_up, down;  // dense
+  QW router, e_gu, e_down;   // MoE: e_gu [E_l][2*Im][H], e_down [E_l][H][Im]
+  GemvPlan p_qkv{}, p_o{}, p_gu{}, p_down{}, p_router{}, p_egu{}, p_edown{};
+};
+
+// How one checkpoint tensor maps onto this rank's device memory.
+struct Spec {
+  void* dst = nullptr;       // first destination byte
+  size_t dst_pitch = 0;      // bytes between destination rows
+  size_t src_pitch = 0;      // bytes of one full source row
+  size_t src_total = 0;      // bytes of the whole source tensor
+  size_t src_off = 0;        // byte offset of the first copied element
+  size_t col_bytes = 0;      // bytes copied per row
+  int rows = 0;              // rows per block
+  int blocks = 1;            // expert blocks
+  size_t dst_block = 0;      // destination stride between blocks
+  size_t src_block = 0;      // source stride between blocks
+  // generator description (init_random)
+  int kind = 0;              // 0 quantized weight part, 1 norm vector
+  int part = 0;              // 0 weight, 1 scales, 2 biases
+  std::string base;          // generator stream name
+  QW* q = nullptr;           // destination tensor
+  int row0 = 0;              // first global row of the shard
+  int col0 = 0;              // first global column of the shard
+  int K_full = 0;            // full reduction length
+  int n_rows = 0;            // shard rows (per block)
+  int n_cols = 0;            // shard columns
+  int dst_row0 = 0;          // first destination row inside q (per block)
+  int dst_block_rows = 0;    // destination rows between blocks
+  int src_block_rows = 0;    // source rows between blocks
+  int gen_block0 = 0;        // first global block (expert)
+  int norm_len = 0;
+};
+
+}  // namespace emx
+
+using namespace emx;
+
+struct emx_qwen3 {
+  emx_ctx* ctx = nullptr;
+  emx_qwen3_config c{};
+  emx_comm* comm = nullptr;
+  int rank = 0, world = 1;
+  bool moe = false, tp = false, ep = false;
+  int nq = 0, nkv = 0, hd = 128, H = 0, I = 0, E_l = 0, e_base = 0, Im = 0, Nqkv = 0;
+  std::vector<LayerW> L;
+  QW embed, lm;
+  bf16* final_norm = nullptr;
+  float* inv_freq = nullptr;
+  GemvPlan p_lm{};
+  bf16* kv = nullptr;
+  size_t kv_layer = 0;  // elements of one layer's K (or V)
+  std::map<std::string, Spec> specs;
+  std::vector<void*> allocs;
+  // decode buffers
+  bf16 *xa = nullptr, *xb = nullptr, *qkvb = nullptr, *attnb = nullptr, *hb = nullptr, *logits = nullptr;
+  bf16 *moe_y = nullptr, *router_logits = nullptr;
+  float *part = nullptr, *moe_w = nullptr, *am_val = nullptr, *attn_part = nullptr;
+  int *state = nullptr, *token = nullptr, *pos = nullptr, *hist_n = nullptr, *hist = nullptr, *am_idx = nullptr;
+  int *moe_idx = nullptr, *moe_n = nullptr;
+  unsigned *am_ticket = nullptr, *attn_ticket = nullptr;
+  int attn_splits = 0;
+  // prefill buffers
+  bf16 *px = nullptr, *pxn = nullptr, *pqkv = nullptr, *pq = nullptr, *pattn = nullptr, *ph = nullptr;
+  float* ppart = nullptr;
+  int* pids = nullptr;
+  int max_T = 0;
+  // state
+  int offset = 0;
+  cudaGraphExec_t gexec = nullptr;
+  int step_launches = 0;
+  int32_t* pinned = nullptr;  // pinned host staging [kv_cap + 4]
+};
+
+namespace {
+
+#define Q_REQUIRE(cond, ...) \
+  do {                       \
+    if (!(cond)) return fail(EMX_ERR_INVALID, __VA_ARGS__); \
+  } while (0)
+
+int alloc(emx_qwen3* m, size_t bytes, void** p) {
+  int rc = ctx_alloc(m->ctx, bytes, p);
+  if (rc) return rc;
+  m->allocs.push_back(*p);
+  cudaMemsetAsync(*p, 0, bytes, m->ctx->stream);
+  return EMX_OK;
+}
+
+template <typename T>
+int alloc_t(emx_qwen3* m, size_t count, T** p) {
+  void* v = nullptr;
+  int rc = alloc(m, count * sizeof(T), &v);
+  *p = static_cast<T*>(v);
+  return rc;
+}
+
+int alloc_qw(emx_qwen3* m, QW& q, int N, int K, int bits, int gs) {
+  q.N = N;
+  q.K = K;
+  q.bits = bits;
+  q.gs = gs;
+  int rc = alloc_t(m, q.wbytes() / 4, &q.w);
+  if (!rc) rc = alloc_t(m, q.sbytes() / 2, &q.s);
+  if (!rc) rc = alloc_t(m, q.sbytes() / 2, &q.b);
+  return rc;
+}
+
+// Registers the three parts of a quantized checkpoint tensor `base`:
+// full shape [blocks_full * rows_full_per_block, K_full]; this rank keeps rows
+// [row0, row0 + n_rows) of every block in [block0, block0 + blocks) and
+// columns [col0, col0 + n_cols), stored at destination row dst_row0 of each
+// destination block of dst_block_rows rows in q.
+void add_quant(emx_qwen3* m, const std::string& base, QW* q, int rows_full_per_block, int blocks_full, int K_full,
+               int row0, int n_rows, int col0, int n_cols, int dst_row0, int block0, int blocks, int dst_block_rows) {
+  const int per = 32 / q->bits;
+  const int ng_full = K_full / q->gs;
+  for (int part = 0; part < 3; ++part) {
+    Spec s;
+    s.kind = 0;
+    s.part = part;
+    s.base = base;
+    s.q = q;
+    s.row0 = row0;
+    s.col0 = col0;
+    s.K_full = K_full;
+    s.n_rows = n_rows;
+    s.n_cols = n_cols;
+    s.dst_row0 = dst_row0;
+    s.dst_block_rows = dst_block_rows;
+    s.src_block_rows = rows_full_per_block;
+    s.gen_block0 = block0;
+    s.rows = n_rows;
+    s.blocks = blocks;
+    size_t src_row, dst_row, col_off, cols;
+    if (part == 0) {
+      src_row = (size_t)K_full / per * 4;
+      dst_row = (size_t)q->K / per * 4;
+      col_off = (size_t)col0 / per * 4;
+      cols = (size_t)n_cols / per * 4;
+    } else {
+      src_row = (size_t)ng_full * 2;
+      dst_row = (size_t)(q->K / q->gs) * 2;
+      col_off = (size_t)(col0 / q->gs) * 2;
+      cols = (size_t)(n_cols / q->gs) * 2;
+    }
+    char* dbase = part == 0 ? reinterpret_cast<char*>(q->w) : part == 1 ? reinterpret_cast<char*>(q->s)
+                                                                         : reinterpret_cast<char*>(q->b);
+    s.dst = dbase + (size_t)dst_row0 * dst_row;
+    s.dst_pitch = dst_row;
+    s.src_pitch = src_row;
+    s.src_total = src_row * (size_t)rows_full_per_block * blocks_full;
+    s.src_off = (size_t)block0 * rows_full_per_block * src_row + (size_t)row0 * src_row + col_off;
+    s.col_bytes = cols;
+    s.dst_block = (size_t)dst_block_rows * dst_row;
+    s.src_block = (size_t)rows_full_per_block * src_row;
+    static const char* sfx[3] = {".weight", ".scales", ".biases"};
+    m->specs[base + sfx[part]] = s;
+  }
+}
+
+void add_norm(emx_qwen3* m, const std::string& name, bf16* dst, int len) {
+  Spec s;
+  s.kind = 1;
+  s.base = name;
+  s.dst = dst;
+  s.dst_pitch = s.src_pitch = s.col_bytes = (size_t)len * 2;
+  s.src_total = (size_t)len * 2;
+  s.rows = 1;
+  s.norm_len = len;
+  m->specs[name] = s;
+}
+
+GemvArgs gemv_base(const emx_qwen3* m, const QW& q) {
+  GemvArgs a = {};
+  a.w = q.w;
+  a.s = q.s;
+  a.b = q.b;
+  a.N = q.N;
+  a.K = q.K;
+  a.bits = q.bits;
+  a.gs = q.gs;
+  a.x_slots = 1;
+  a.eps = m->c.eps;
+  a.norm_groups = m->c.norm_groups;
+  a.status = m->ctx->status;
+  return a;
+}
+
+int plan(emx_qwen3* m, const QW& q, int epi, int x_slots, int n_rows_override, GemvPlan* p) {
+  const int N = n_rows_override > 0 ? n_rows_override : q.N;
+  if (gemv_make_plan(N, q.K, q.bits, q.gs, epi, x_slots, m->ctx->num_sms, p))
+    return fail(EMX_ERR_INVALID, "no GEMV plan for N=%d K=%d bits=%d group=%d", N, q.K, q.bits, q.gs);
+  return EMX_OK;
+}
+
+int build(emx_qwen3* m) {
+  const emx_qwen3_config& c = m->c;
+  const int W = m->world, r = m->rank;
+  m->hd = c.head_dim;
+  m->H = c.hidden;
+  if (m->tp) {
+    m->nq = c.n_q / W;
+    m->nkv = c.n_kv / W;
+    m->I = c.inter / W;
+  } else {
+    m->nq = c.n_q;
+    m->nkv = c.n_kv;
+    m->I = c.inter;
+  }
+  m->Nqkv = (m->nq + 2 * m->nkv) * m->hd;
+  if (m->moe) {
+    m->Im = c.moe_inter;
+    m->E_l = m->ep ? c.n_experts / W : c.n_experts;
+    m->e_base = m->ep ? r * m->E_l : 0;
+  }
+  const int H = m->H, hd = m->hd;
+  int rc;
+  m->L.resize(c.layers);
+  // embedding / lm_head / final norm (replicated)
+  if ((rc = alloc_qw(m, m->embed, c.vocab, H, c.embed_bits, c.embed_group))) return rc;
+  add_quant(m, "model.embed_tokens", &m->embed, c.vocab, 1, H, 0, c.vocab, 0, H, 0, 0, 1, c.vocab);
+  if (!c.tied) {
+    if ((rc = alloc_qw(m, m->lm, c.vocab, H, c.lm_bits, c.lm_group))) return rc;
+    add_quant(m, "lm_head", &m->lm, c.vocab, 1, H, 0, c.vocab, 0, H, 0, 0, 1, c.vocab);
+  }
+  if ((rc = alloc_t(m, H, &m->final_norm))) return rc;
+  add_norm(m, "model.norm.weight", m->final_norm, H);
+  for (int l = 0; l < c.layers; ++l) {
+    LayerW& lw = m->L[l];
+    const std::string p = "model.layers." + std::to_string(l) + ".";
+    if ((rc = alloc_t(m, H, &lw.in_norm)) || (rc = alloc_t(m, H, &lw.post_norm)) ||
+        (rc = alloc_t(m, hd, &lw.q_norm)) || (rc = alloc_t(m, hd, &lw.k_norm)))
+      return rc;
+    add_norm(m, p + "input_layernorm.weight", lw.in_norm, H);
+    add_norm(m, p + "post_attention_layernorm.weight", lw.post_norm, H);
+    add_norm(m, p + "self_attn.q_norm.weight", lw.q_norm, hd);
+    add_norm(m, p + "self_attn.k_norm.weight", lw.k_norm, hd);
+    // attention: q|k|v rows split by heads under TP
+    if ((rc = alloc_qw(m, lw.qkv, m->Nqkv, H, c.attn_bits, c.attn_group))) return rc;
+    const int qr0 = m->tp ? r * m->nq * hd : 0, kr0 = m->tp ? r * m->nkv * hd : 0;
+    add_quant(m, p + "self_attn.q_proj", &lw.qkv, c.n_q * hd, 1, H, qr0, m->nq * hd, 0, H, 0, 0, 1, m->Nqkv);
+    add_quant(m, p + "self_attn.k_proj", &lw.qkv, c.n_kv * hd, 1, H, kr0, m->nkv * hd, 0, H, m->nq * hd, 0, 1,
+              m->Nqkv);
+    add_quant(m, p + "self_attn.v_proj", &lw.qkv, c.n_kv * hd, 1, H, kr0, m->nkv * hd, 0, H,
+              (m->nq + m->nkv) * hd, 0, 1, m->Nqkv);
+    if ((rc = alloc_qw(m, lw.o, H, m->nq * hd, c.attn_bits, c.attn_group))) return rc;
+    add_quant(m, p + "self_attn.o_proj", &lw.o, H, 1, c.n_q * hd, 0, H, qr0, m->nq * hd, 0, 0, 1, H);
+    if (!m->moe) {
+      if ((rc = alloc_qw(m, lw.gate_up, 2 * m->I, H, c.mlp_bits, c.mlp_group))) return rc;
+      const int ir0 = m->tp ? r * m->I : 0;
+      add_quant(m, p + "mlp.gate_proj", &lw.gate_up, c.inter, 1, H, ir0, m->I, 0, H, 0, 0, 1, 2 * m->I);
+      add_quant(m, p + "mlp.up_proj", &lw.gate_up, c.inter, 1, H, ir0, m->I, 0, H, m->I, 0, 1, 2 * m->I);
+      if ((rc = alloc_qw(m, lw.down, H, m->I, c.mlp_bits, c.mlp_group))) return rc;
+      add_quant(m, p + "mlp.down_proj", &lw.down, H, 1, c.inter, 0, H, ir0, m->I, 0, 0, 1, H);
+    } else {
+      const int E = c.n_experts, Im = m->Im;
+      if ((rc = alloc_qw(m, lw.router, E, H, c.router_bits, c.router_group))) return rc;
+      add_quant(m, p + "mlp.gate", &lw.router, E, 1, H, 0, E, 0, H, 0, 0, 1, E);
+      if ((rc = alloc_qw(m, lw.e_gu, m->E_l * 2 * Im, H, c.expert_bits, c.expert_group))) return rc;
+      add_quant(m, p + "mlp.switch_mlp.gate_proj", &lw.e_gu, Im, E, H, 0, Im, 0, H, 0, m->e_base, m->E_l, 2 * Im);
+      add_quant(m, p + "mlp.switch_mlp.up_proj", &lw.e_gu, Im, E, H, 0, Im, 0, H, Im, m->e_base, m->E_l, 2 * Im);
+      if ((rc = alloc_qw(m, lw.e_down, m->E_l * H, Im, c.expert_bits, c.expert_group))) return rc;
+      add_quant(m, p + "mlp.switch_mlp.down_proj", &lw.e_down, H, E, Im, 0, H, 0, Im, 0, m->e_base, m->E_l, H);
+    }
+    // launch plans
+    if ((rc = plan(m, lw.qkv, kEpiStore, 1, 0, &lw.p_qkv))) return rc;
+    if ((rc = plan(m, lw.o, m->tp ? kEpiF32 : kEpiResid, 1, 0, &lw.p_o))) return rc;
+    if (!m->moe) {
+      if ((rc = plan(m, lw.gate_up, kEpiSwiglu, 1, 0, &lw.p_gu))) return rc;
+      if ((rc = plan(m, lw.down, m->tp ? kEpiF32 : kEpiResid, 1, 0, &lw.p_down))) return rc;
+    } else {
+      if ((rc = plan(m, lw.router, kEpiStore, 1, 0, &lw.p_router))) return rc;
+      if ((rc = plan(m, lw.e_gu, kEpiSwiglu, 1, c.top_k * 2 * m->Im, &lw.p_egu))) return rc;
+      if ((rc = plan(m, lw.e_down, kEpiStore, c.top_k, c.top_k * H, &lw.p_edown))) return rc;
+    }
+  }
+  if ((rc = plan(m, c.tied ? m->embed : m->lm, kEpiArgmax, 1, 0, &m->p_lm))) return rc;
+  // rope table, KV cache, decode state
+  if ((rc = alloc_t(m, hd / 2, &m->inv_freq))) return rc;
+  if (k_rope_inv_freq(m->inv_freq, hd, c.rope_theta, m->ctx->stream) != cudaSuccess)
+    return fail(EMX_ERR_CUDA, "rope table");
+  m->kv_layer = (size_t)m->nkv * c.kv_cap * hd;
+  if ((rc = alloc_t(m, m->kv_layer * 2 * c.layers, &m->kv))) return rc;
+  if ((rc = alloc_t(m, H, &m->xa)) || (rc = alloc_t(m, H, &m->xb)) || (rc = alloc_t(m, m->Nqkv, &m->qkvb)) ||
+      (rc = alloc_t(m, (size_t)m->nq * hd, &m->attnb)) || (rc = alloc_t(m, c.vocab, &m->logits)) ||
+      (rc = alloc_t(m, H, &m->part)))
+    return rc;
+  const size_t hsz = m->moe ? (size_t)c.top_k * m->Im : (size_t)m->I;
+  if ((rc = alloc_t(m, hsz, &m->hb))) return rc;
+  if (m->moe) {
+    if ((rc = alloc_t(m, (size_t)c.top_k * H, &m->moe_y)) || (rc = alloc_t(m, c.n_experts, &m->router_logits)) ||
+        (rc = alloc_t(m, 64, &m->moe_w)) || (rc = alloc_t(m, 64, &m->moe_idx)) || (rc = alloc_t(m, 4, &m->moe_n)))
+      return rc;
+  }
+  if ((rc = alloc_t(m, 64, &m->state))) return rc;
+  m->token = m->state + 0;
+  m->pos = m->state + 1;
+  m->hist_n = m->state + 2;
+  if ((rc = alloc_t(m, (size_t)c.kv_cap, &m->hist))) return rc;
+  if ((rc = alloc_t(m, 1024, &m->am_val)) || (rc = alloc_t(m, 1024, &m->am_idx)) ||
+      (rc = alloc_t(m, 16, &m->am_ticket)))
+    return rc;
+  m->attn_splits = attn_decode_splits(m->nkv, m->ctx->num_sms);
+  const int hpg = m->nq / m->nkv;
+  if ((rc = alloc_t(m, (size_t)m->nkv * m->attn_splits * hpg * (hd + 2), &m->attn_part)) ||
+      (rc = alloc_t(m, (size_t)m->nkv, &m->attn_ticket)))
+    return rc;
+  // prefill buffers
+  m->max_T = c.max_prefill > 0 ? c.max_prefill : 1;
+  const size_t T = (size_t)m->max_T;
+  if ((rc = alloc_t(m, T * H, &m->px)) || (rc = alloc_t(m, T * H, &m->pxn)) ||
+      (rc = alloc_t(m, T * m->Nqkv, &m->pqkv)) || (rc = alloc_t(m, T * m->nq * hd, &m->pq)) ||
+      (rc = alloc_t(m, T * m->nq * hd, &m->pattn)) || (rc = alloc_t(m, T, &m->pids)))
+    return rc;
+  if (!m->moe && (rc = alloc_t(m, T * 2 * m->I, &m->ph))) return rc;
+  if ((m->tp || m->ep) && (rc = alloc_t(m, T * H, &m->ppart))) return rc;
+  if (cudaMallocHost(reinterpret_cast<void**>(&m->pinned), sizeof(int32_t) * ((size_t)c.kv_cap + 8)) != cudaSuccess)
+    return fail(EMX_ERR_OOM, "pinned staging buffer");
+  return ctx_sync_check(m->ctx, "emx_qwen3_create");
+}
+
+// ------------------------------------------------------------ decode step
+
+int launch_gemv(emx_qwen3* m, const GemvArgs& a, const GemvPlan& p, bool pdl) {
+  cudaError_t e = gemv_launch(a, p, m->ctx->stream, pdl);
+  if (e != cudaSuccess) return fail_cuda(e, "decode gemv launch");
+  ++m->step_launches;
+  return EMX_OK;
+}
+
+int enqueue_step(emx_qwen3* m) {
+  const emx_qwen3_config& c = m->c;
+  cudaStream_t st = m->ctx->stream;
+  m->step_launches = 0;
+  bf16* cur = m->xa;
+  bf16* nxt = m->xb;
+  bool pending_add = false;  // the previous block's output still has to be added to `cur`
+  auto set_add = [&](GemvArgs& a) {
+    // the residual add of the previous block's sharded / expert output, fused here
+    a.pro = kProAddNorm;
+    a.x = cur;
+    a.x_out = nxt;
+    if (m->moe && !m->ep) {
+      a.moe_y = m->moe_y;
+      a.moe_w = m->moe_w;
+      a.moe_n = m->moe_n;
+    } else {
+      a.add_f32 = m->part;
+      a.add_round = m->tp ? 1 : 0;
+    }
+  };
+  int rc;
+  for (int l = 0; l < c.layers; ++l) {
+    LayerW& lw = m->L[l];
+    bf16* kc = m->kv + m->kv_layer * (2 * (size_t)l);
+    bf16* vc = kc + m->kv_layer;
+    // ---- input norm + fused qkv projection
+    {
+      GemvArgs a = gemv_base(m, lw.qkv);
+      if (l == 0) {
+        a.pro = kProEmbedNorm;
+        a.emb_w = m->embed.w;
+        a.emb_s = m->embed.s;
+        a.emb_b = m->embed.b;
+        a.emb_bits = m->embed.bits;
+        a.emb_gs = m->embed.gs;
+        a.vocab = c.vocab;
+        a.token = m->token;
+        a.x_out = cur;
+      } else if (pending_add) {
+        set_add(a);
+      } else {
+        a.pro = kProNorm;
+        a.x = cur;
+      }
+      a.norm_w = lw.in_norm;
+      a.epi = kEpiStore;
+      a.y = m->qkvb;
+      if ((rc = launch_gemv(m, a, lw.p_qkv, m->step_launches > 0))) return rc;
+      if (pending_add) {
+        std::swap(cur, nxt);
+        pending_add = false;
+      }
+    }
+    // ---- attention (q/k norm, rope, KV write, flash-decode)
+    {
+      AttnDecodeArgs a = {};
+      a.qkv = m->qkvb;
+      a.q_norm = lw.q_norm;
+      a.k_norm = lw.k_norm;
+      a.eps = c.eps;
+      a.inv_freq = m->inv_freq;
+      a.kc = kc;
+      a.vc = vc;
+      a.cap = c.kv_cap;
+      a.nq = m->nq;
+      a.nkv = m->nkv;
+      a.head_dim = m->hd;
+      a.pos = m->pos;
+      a.scale = 1.0f / sqrtf((float)m->hd);
+      a.out = m->attnb;
+      a.part = m->attn_part;
+      a.ticket = m->attn_ticket;
+      a.splits = m->attn_splits;
+      a.status = m->ctx->status;
+      cudaError_t e = attn_decode_launch(a, st, true);
+      if (e != cudaSuccess) return fail_cuda(e, "attention launch");
+      ++m->step_launches;
+    }
+    // ---- o projection (+ residual, or fp32 partial + all-reduce under TP)
+    {
+      GemvArgs a = gemv_base(m, lw.o);
+      a.pro = kProX;
+      a.x = m->attnb;
+      if (m->tp) {
+        a.epi = kEpiF32;
+        a.yf = m->part;
+      } else {
+        a.epi = kEpiResid;
+        a.res = cur;
+        a.y = cur;
+      }
+      if ((rc = launch_gemv(m, a, lw.p_o, true))) return rc;
+      if (m->tp) {
+        if ((rc = comm_all_reduce(m->comm, m->part, (size_t)m->H, EMX_F32, st))) return rc;
+        pending_add = true;
+      }
+    }
+    if (!m->moe) {
+      GemvArgs a = gemv_base(m, lw.gate_up);
+      if (pending_add) set_add(a);
+      else {
+        a.pro = kProNorm;
+        a.x = cur;
+      }
+      a.norm_w = lw.post_norm;
+      a.epi = kEpiSwiglu;
+      a.y = m->hb;
+      if ((rc = launch_gemv(m, a, lw.p_gu, true))) return rc;
+      if (pending_add) {
+        std::swap(cur, nxt);
+        pending_add = false;
+      }
+      GemvArgs d = gemv_base(m, lw.down);
+      d.pro = kProX;
+      d.x = m->hb;
+      if (m->tp) {
+        d.epi = kEpiF32;
+        d.yf = m->part;
+      } else {
+        d.epi = kEpiResid;
+        d.res = cur;
+        d.y = cur;
+      }
+      if ((rc = launch_gemv(m, d, lw.p_down, true))) return rc;
+      if (m->tp) {
+        if ((rc = comm_all_reduce(m->comm, m->part, (size_t)m->H, EMX_F32, st))) return rc;
+        pending_add = true;
+      }
+    } else {
+      // router -> top-k -> gathered expert SwiGLU -> gathered expert down
+      GemvArgs ra = gemv_base(m, lw.router);
+      ra.pro = kProNorm;
+      ra.x = cur;
+      ra.norm_w = lw.post_norm;
+      ra.epi = kEpiStore;
+      ra.y = m->router_logits;
+      if ((rc = launch_gemv(m, ra, lw.p_router, true))) return rc;
+      cudaError_t e = k_moe_route(m->router_logits, c.n_experts, c.top_k, c.norm_topk, m->e_base, m->E_l,
+                                  m->moe_idx, m->moe_w, m->moe_n, st, true);
+      if (e != cudaSuccess) return fail_cuda(e, "moe route");
+      ++m->step_launches;
+      GemvArgs ga = gemv_base(m, lw.e_gu);
+      ga.N = c.top_k * 2 * m->Im;
+      ga.pro = kProNorm;
+      ga.x = cur;
+      ga.norm_w = lw.post_norm;
+      ga.epi = kEpiSwiglu;
+      ga.y = m->hb;
+      ga.slot_expert = m->moe_idx;
+      ga.n_slots = m->moe_n;
+      ga.slot_rows = m->Im;
+      if ((rc = launch_gemv(m, ga, lw.p_egu, true))) return rc;
+      GemvArgs da = gemv_base(m, lw.e_down);
+      da.N = c.top_k * m->H;
+      da.pro = kProX;
+      da.x = m->hb;
+      da.x_slots = c.top_k;
+      da.epi = kEpiStore;
+      da.y = m->moe_y;
+      da.slot_expert = m->moe_idx;
+      da.n_slots = m->moe_n;
+      da.slot_rows = m->H;
+      if ((rc = launch_gemv(m, da, lw.p_edown, true))) return rc;
+      if (m->ep) {
+        e = k_moe_combine(m->moe_y, m->moe_w, m->moe_n, m->H, m->part, st, true);
+        if (e != cudaSuccess) return fail_cuda(e, "moe combine");
+        ++m->step_launches;
+        if ((rc = comm_all_reduce(m->comm, m->part, (size_t)m->H, EMX_F32, st))) return rc;
+      }
+      pending_add = true;
+    }
+  }
+  // ---- final norm + lm_head + greedy argmax (token and offset stay on device)
+  {
+    const QW& lmw = c.tied ? m->embed : m->lm;
+    GemvArgs a = gemv_base(m, lmw);
+    if (pending_add) set_add(a);
+    else {
+      a.pro = kProNorm;
+      a.x = cur;
+    }
+    a.norm_w = m->final_norm;
+    a.epi = kEpiArgmax;
+    a.y = m->logits;
+    a.am_val = m->am_val;
+    a.am_idx = m->am_idx;
+    a.am_ticket = m->am_ticket;
+    a.tok_out = m->token;
+    a.hist = m->hist;
+    a.hist_n = m->hist_n;
+    a.hist_cap = c.kv_cap;
+    a.pos = m->pos;
+    a.pos_inc = 1;
+    if ((rc = launch_gemv(m, a, m->p_lm, true))) return rc;
+  }
+  return EMX_OK;
+}
+
+int ensure_graph(emx_qwen3* m) {
+  if (m->gexec) return EMX_OK;
+  cudaStream_t st = m->ctx->stream;
+  cudaGraph_t g = nullptr;
+  EMX_CHECK_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeRelaxed), "begin capture");
+  int rc = enqueue_step(m);
+  cudaError_t e = cudaStreamEndCapture(st, &g);
+  if (rc) {
+    if (g) cudaGraphDestroy(g);
+    return rc;
+  }
+  if (e != cudaSuccess) return fail_cuda(e, "end capture");
+  e = cudaGraphInstantiate(&m->gexec, g, 0);
+  cudaGraphDestroy(g);
+  if (e != cudaSuccess) {
+    m->gexec = nullptr;
+    return fail_cuda(e, "graph instantiate");
+  }
+  return EMX_OK;
+}
+
+int run_steps(emx_qwen3* m, int n) {
+  int rc = ensure_graph(m);
+  if (rc) return rc;
+  for (int i = 0; i < n; ++i) EMX_CHECK_CUDA(cudaGraphLaunch(m->gexec, m->ctx->stream), "graph launch");
+  m->offset += n;
+  return EMX_OK;
+}
+
+// --------------------------------------------------------------- prefill
+
+int gemm(emx_qwen3* m, const QW& q, const bf16* x, int T, int epi, bf16* y, const bf16* res) {
+  GemmArgs g = {};
+  g.x = x;
+  g.w = q.w;
+  g.s = q.s;
+  g.b = q.b;
+  g.M = T;
+  g.N = q.N;
+  g.K = q.K;
+  g.bits = q.bits;
+  g.gs = q.gs;
+  g.epi = epi;
+  g.y = y;
+  g.res = res;
+  int rc = gemm_run(m->ctx->gemm, g, m->ctx->stream);
+  if (rc) return fail(EMX_ERR_CUDA, "prefill gemm failed (%d)", rc);
+  return EMX_OK;
+}
+
+int prefill_impl(emx_qwen3* m, const int32_t* ids_dev, int T) {
+  const emx_qwen3_config& c = m->c;
+  cudaStream_t st = m->ctx->stream;
+  const int H = m->H, hd = m->hd;
+  const int off = m->offset;
+  int rc;
+  cudaError_t e = k_embed(m->embed.w, m->embed.s, m->embed.b, ids_dev, T, H, m->embed.gs, m->embed.bits, c.vocab,
+                          m->px, m->ctx->status, st);
+  if (e != cudaSuccess) return fail_cuda(e, "prefill embed");
+  for (int l = 0; l < c.layers; ++l) {
+    LayerW& lw = m->L[l];
+    bf16* kc = m->kv + m->kv_layer * (2 * (size_t)l);
+    bf16* vc = kc + m->kv_layer;
+    if ((e = k_rms_norm(m->px, lw.in_norm, m->pxn, T, H, c.eps, c.norm_groups, st)) != cudaSuccess)
+      return fail_cuda(e, "prefill norm");
+    if ((rc = gemm(m, lw.qkv, m->pxn, T, kGemmStore, m->pqkv, nullptr))) return rc;
+    PrefillQkvArgs pa = {};
+    pa.qkv = m->pqkv;
+    pa.q_norm = lw.q_norm;
+    pa.k_norm = lw.k_norm;
+    pa.eps = c.eps;
+    pa.inv_freq = m->inv_freq;
+    pa.T = T;
+    pa.nq = m->nq;
+    pa.nkv = m->nkv;
+    pa.hd = hd;
+    pa.offset = off;
+    pa.q_out = m->pq;
+    pa.kc = kc;
+    pa.vc = vc;
+    pa.cap = c.kv_cap;
+    if ((e = k_prefill_qkv(pa, st)) != cudaSuccess) return fail_cuda(e, "prefill qkv post");
+    AttnPrefillArgs aa = {};
+    aa.q = m->pq;
+    aa.kc = kc;
+    aa.vc = vc;
+    aa.cap = c.kv_cap;
+    aa.offset = off;
+    aa.T = T;
+    aa.nq = m->nq;
+    aa.nkv = m->nkv;
+    aa.head_dim = hd;
+    aa.scale = 1.0f / sqrtf((float)hd);
+    aa.out = m->pattn;
+    aa.out_tnd = 1;
+    if ((e = attn_prefill_launch(aa, st)) != cudaSuccess) return fail_cuda(e, "prefill attention");
+    if (m->tp) {
+      return fail(EMX_ERR_INVALID, "tensor-parallel prefill is not supported yet");
+    }
+    if ((rc = gemm(m, lw.o, m->pattn, T, kGemmResid, m->px, m->px))) return rc;
+    if ((e = k_rms_norm(m->px, lw.post_norm, m->pxn, T, H, c.eps, c.norm_groups, st)) != cudaSuccess)
+      return fail_cuda(e, "prefill norm");
+    if (!m->moe) {
+      if ((rc = gemm(m, lw.gate_up, m->pxn, T, kGemmSwiglu, m->ph, nullptr))) return rc;
+      if ((rc = gemm(m, lw.down, m->ph, T, kGemmResid, m->px, m->px))) return rc;
+    } else {
+      return fail(EMX_ERR_INVALID, "MoE prefill is not supported yet");
+    }
+  }
+  // final norm + lm_head on the last row, greedy token, offset += T
+  const QW& lmw = c.tied ? m->embed : m->lm;
+  GemvArgs a = gemv_base(m, lmw);
+  a.pro = kProNorm;
+  a.x = m->px + (size_t)(T - 1) * H;
+  a.norm_w = m->final_norm;
+  a.epi = kEpiArgmax;
+  a.y = m->logits;
+  a.am_val = m->am_val;
+  a.am_idx = m->am_idx;
+  a.am_ticket = m->am_ticket;
+  a.tok_out = m->token;
+  a.pos = m->pos;
+  a.pos_inc = T;
+  e = gemv_launch(a, m->p_lm, st, false);
+  if (e != cudaSuccess) return fail_cuda(e, "prefill lm_head");
+  m->offset += T;
+  return EMX_OK;
+}
+
+int init_random_impl(emx_qwen3* m, uint64_t seed) {
+  cudaStream_t st = m->ctx->stream;
+  for (auto& kv : m->specs) {
+    const Spec& s = kv.second;
+    const uint64_t stream = [&] {
+      uint64_t h = 0xcbf29ce484222325ull;
+      for (unsigned char ch : s.base) {
+        h ^= ch;
+        h *= 0x100000001b3ull;
+      }
+      return h;
+    }();
+    cudaError_t e = cudaSuccess;
+    if (s.kind == 1) {
+      e = k_fill_normal_bf16(seed, stream, (size_t)s.norm_len, 1.0f, 0.05f, static_cast<bf16*>(s.dst), st);
+    } else {
+      if (s.part != 0) continue;  // weight, scales and biases come from one generator pass
+      QW* q = s.q;
+      const int per = 32 / q->bits, ngl = q->K / q->gs;
+      for (int b = 0; b < s.blocks; ++b) {
+        const size_t dst_row = (size_t)b * s.dst_block_rows + s.dst_row0;
+        const size_t gen_row0 = (size_t)(s.gen_block0 + b) * s.src_block_rows + s.row0;
+        e = k_fill_quantized_shard(seed, stream, s.n_rows, s.n_cols, s.K_full, gen_row0, s.col0, q->gs, q->bits,
+                                   0.02f, q->w + dst_row * (q->K / per), q->s + dst_row * ngl,
+                                   q->b + dst_row * ngl, q->K, st);
+        if (e != cudaSuccess) break;
+      }
+    }
+    if (e != cudaSuccess) return fail_cuda(e, "init_random");
+  }
+  return ctx_sync_check(m->ctx, "emx_qwen3_init_random");
+}
+
+}  // namespace
+
+extern "C" {
+
+int emx_qwen3_create(emx_ctx* ctx, const emx_qwen3_config* cfg, emx_comm* comm, emx_qwen3** out) {
+  Q_REQUIRE(ctx && cfg && out, "emx_qwen3_create: null argument");
+  *out = nullptr;
+  const emx_qwen3_config& c = *cfg;
+  Q_REQUIRE(c.hidden > 0 && c.layers > 0 && c.n_q > 0 && c.n_kv > 0 && c.vocab > 0 && c.kv_cap > 0,
+            "emx_qwen3_create: bad dimensions");
+  Q_REQUIRE(c.head_dim == 128, "emx_qwen3_create: head_dim must be 128 (got %d)", c.head_dim);
+  Q_REQUIRE(c.n_q % c.n_kv == 0 && (c.n_q / c.n_kv == 1 || c.n_q / c.n_kv == 2 || c.n_q / c.n_kv == 4 ||
+                                    c.n_q / c.n_kv == 8),
+            "emx_qwen3_create: n_q / n_kv must be 1, 2, 4 or 8");
+  Q_REQUIRE(c.norm_groups >= 1 && c.hidden % c.norm_groups == 0, "emx_qwen3_create: norm_groups");
+  Q_REQUIRE(c.n_experts == 0 || (c.top_k >= 1 && c.top_k <= 64 && c.top_k <= c.n_experts && c.moe_inter > 0),
+            "emx_qwen3_create: MoE parameters");
+  emx_qwen3* m = new emx_qwen3();
+  m->ctx = ctx;
+  m->c = c;
+  m->comm = comm;
+  m->moe = c.n_experts > 0;
+  if (comm && comm->nranks > 1) {
+    m->rank = comm->rank;
+    m->world = comm->nranks;
+    m->tp = !m->moe;
+    m->ep = m->moe;
+    if (m->tp && (c.n_q % m->world || c.n_kv % m->world || c.inter % m->world || (c.inter / m->world) % 64)) {
+      delete m;
+      return fail(EMX_ERR_INVALID, "emx_qwen3_create: heads / intermediate not divisible across %d ranks", m->world);
+    }
+    if (m->ep && c.n_experts % m->world) {
+      delete m;
+      return fail(EMX_ERR_INVALID, "emx_qwen3_create: %d experts not divisible across %d ranks", c.n_experts,
+                  m->world);
+    }
+  }
+  cudaSetDevice(ctx->device);
+  int rc = build(m);
+  if (rc) {
+    emx_qwen3_destroy(m);
+    return rc;
+  }
+  *out = m;
+  return EMX_OK;
+}
+
+int emx_qwen3_destroy(emx_qwen3* m) {
+  if (!m) return EMX_OK;
+  cudaStreamSynchronize(m->ctx->stream);
+  if (m->gexec) cudaGraphExecDestroy(m->gexec);
+  for (void* p : m->allocs) ctx_free(m->ctx, p);
+  if (m->pinned) cudaFreeHost(m->pinned);
+  delete m;
+  return EMX_OK;
+}
+
+int emx_qwen3_load_tensor(emx_qwen3* m, const char* name, const void* host, size_t bytes) {
+  Q_REQUIRE(m && name && host, "emx_qwen3_load_tensor: null argument");
+  auto it = m->specs.find(name);
+  Q_REQUIRE(it != m->specs.end(), "emx_qwen3_load_tensor: unknown tensor '%s'", name);
+  const Spec& s = it->second;
+  Q_REQUIRE(bytes == s.src_total, "emx_qwen3_load_tensor: '%s' has %zu bytes, expected %zu", name, bytes,
+            s.src_total);
+  const char* src = static_cast<const char*>(host);
+  for (int b = 0; b < s.blocks; ++b) {
+    EMX_CHECK_CUDA(cudaMemcpy2DAsync(static_cast<char*>(s.dst) + (size_t)b * s.dst_block, s.dst_pitch,
+                                     src + s.src_off + (size_t)b * s.src_block, s.src_pitch, s.col_bytes, s.rows,
+                                     cudaMemcpyHostToDevice, m->ctx->stream),
+                   "emx_qwen3_load_tensor");
+  }
+  return ctx_sync_check(m->ctx, "emx_qwen3_load_tensor");
+}
+
+int emx_qwen3_read_tensor(emx_qwen3* m, const char* name, void* host, size_t bytes) {
+  Q_REQUIRE(m && name && host, "emx_qwen3_read_tensor: null argument");
+  auto it = m->specs.find(name);
+  Q_REQUIRE(it != m->specs.end(), "emx_qwen3_read_tensor: unknown tensor '%s'", name);
+  const Spec& s = it->second;
+  const size_t need = s.col_bytes * s.rows * s.blocks;
+  Q_REQUIRE(bytes == need, "emx_qwen3_read_tensor: '%s' shard has %zu bytes, got %zu", name, need, bytes);
+  char* dst = static_cast<char*>(host);
+  for (int b = 0; b < s.blocks; ++b) {
+    EMX_CHECK_CUDA(cudaMemcpy2DAsync(dst + (size_t)b * s.col_bytes * s.rows, s.col_bytes,
+                                     static_cast<const char*>(s.dst) + (size_t)b * s.dst_block, s.dst_pitch,
+                                     s.col_bytes, s.rows, cudaMemcpyDeviceToHost, m->ctx->stream),
+                   "emx_qwen3_read_tensor");
+  }
+  return ctx_sync_check(m->ctx, "emx_qwen3_read_tensor");
+}
+
+int emx_qwen3_init_random(emx_qwen3* m, uint64_t seed) {
+  Q_REQUIRE(m, "emx_qwen3_init_random: null model");
+  return init_random_impl(m, seed);
+}
+
+int emx_qwen3_reset(emx_qwen3* m) {
+  Q_REQUIRE(m, "emx_qwen3_reset: null model");
+  m->offset = 0;
+  EMX_CHECK_CUDA(cudaMemsetAsync(m->state, 0, sizeof(int) * 64, m->ctx->stream), "reset");
+  return ctx_sync_check(m->ctx, "emx_qwen3_reset");
+}
+
+int emx_qwen3_offset(emx_qwen3* m, int* offset) {
+  Q_REQUIRE(m && offset, "emx_qwen3_offset: null argument");
+  *offset = m->offset;
+  return EMX_OK;
+}
+
+int emx_qwen3_prefill_device(emx_qwen3* m, const int32_t* ids, int T) {
+  Q_REQUIRE(m && ids, "emx_qwen3_prefill: null argument");
+  Q_REQUIRE(T >= 1 && T <= m->max_T, "emx_qwen3_prefill: T=%d outside [1, max_prefill=%d]", T, m->max_T);
+  if (m->offset + T > m->c.kv_cap)
+    return fail(EMX_ERR_STATE, "static KV overflow offset=%d + T=%d > cap=%d", m->offset, T, m->c.kv_cap);
+  return prefill_impl(m, ids, T);
+}
+
+int emx_qwen3_prefill(emx_qwen3* m, const int32_t* tokens, int T, int32_t* next_token, void* logits) {
+  Q_REQUIRE(m && tokens, "emx_qwen3_prefill: null argument");
+  Q_REQUIRE(T >= 1 && T <= m->max_T, "emx_qwen3_prefill: T=%d outside [1, max_prefill=%d]", T, m->max_T);
+  if (m->offset + T > m->c.kv_cap)
+    return fail(EMX_ERR_STATE, "static KV overflow offset=%d + T=%d > cap=%d", m->offset, T, m->c.kv_cap);
+  EMX_CHECK_CUDA(cudaMemcpyAsync(m->pids, tokens, sizeof(int32_t) * T, cudaMemcpyHostToDevice, m->ctx->stream),
+                 "prefill ids");
+  int rc = prefill_impl(m, m->pids, T);
+  if (rc) return rc;
+  if (logits)
+    EMX_CHECK_CUDA(cudaMemcpyAsync(logits, m->logits, (size_t)m->c.vocab * 2, cudaMemcpyDeviceToHost, m->ctx->stream),
+                   "prefill logits");
+  if (next_token)
+    EMX_CHECK_CUDA(cudaMemcpyAsync(m->pinned, m->token, sizeof(int32_t), cudaMemcpyDeviceToHost, m->ctx->stream),
+                   "prefill token");
+  rc = ctx_sync_check(m->ctx, "emx_qwen3_prefill");
+  if (rc) return rc;
+  if (next_token) *next_token = m->pinned[0];
+  return EMX_OK;
+}
+
+int emx_qwen3_decode_step(emx_qwen3* m, int32_t token, int32_t* next_token, void* logits) {
+  Q_REQUIRE(m, "emx_qwen3_decode_step: null model");
+  Q_REQUIRE(token >= 0 && token < m->c.vocab, "emx_qwen3_decode_step: token %d outside [0, %d)", token, m->c.vocab);
+  if (m->offset + 1 > m->c.kv_cap)
+    return fail(EMX_ERR_STATE, "static KV overflow offset=%d cap=%d", m->offset, m->c.kv_cap);
+  m->pinned[0] = token;
+  EMX_CHECK_CUDA(cudaMemcpyAsync(m->token, m->pinned, sizeof(int32_t), cudaMemcpyHostToDevice, m->ctx->stream),
+                 "decode token");
+  int rc = run_steps(m, 1);
+  if (rc) return rc;
+  if (logits)
+    EMX_CHECK_CUDA(cudaMemcpyAsync(logits, m->logits, (size_t)m->c.vocab * 2, cudaMemcpyDeviceToHost, m->ctx->stream),
+                   "decode logits");
+  EMX_CHECK_CUDA(cudaMemcpyAsync(m->pinned + 1, m->token, sizeof(int32_t), cudaMemcpyDeviceToHost, m->ctx->stream),
+                 "decode next token");
+  rc = ctx_sync_check(m->ctx, "emx_qwen3_decode_step");
+  if (rc) return rc;
+  if (next_token) *next_token = m->pinned[1];
+  return EMX_OK;
+}
+
+int emx_qwen3_decode(emx_qwen3* m, int32_t token, int n, int32_t* tokens_out) {
+  Q_REQUIRE(m && tokens_out, "emx_qwen3_decode: null argument");
+  Q_REQUIRE(n >= 1, "emx_qwen3_decode: n=%d", n);
+  Q_REQUIRE(token >= 0 && token < m->c.vocab, "emx_qwen3_decode: token %d outside [0, %d)", token, m->c.vocab);
+  if (m->offset + n > m->c.kv_cap)
+    return fail(EMX_ERR_STATE, "static KV overflow offset=%d + n=%d > cap=%d", m->offset, n, m->c.kv_cap);
+  m->pinned[0] = token;
+  m->pinned[1] = 0;
+  EMX_CHECK_CUDA(cudaMemcpyAsync(m->token, m->pinned, sizeof(int32_t), cudaMemcpyHostToDevice, m->ctx->stream),
+                 "decode token");
+  EMX_CHECK_CUDA(cudaMemcpyAsync(m->hist_n, m->pinned + 1, sizeof(int32_t), cudaMemcpyHostToDevice, m->ctx->stream),
+                 "decode history");
+  int rc = run_steps(m, n);
+  if (rc) return rc;
+  EMX_CHECK_CUDA(cudaMemcpyAsync(m->pinned, m->hist, sizeof(int32_t) * n, cudaMemcpyDeviceToHost, m->ctx->stream),
+                 "decode tokens");
+  rc = ctx_sync_check(m->ctx, "emx_qwen3_decode");
+  if (rc) return rc;
+  memcpy(tokens_out, m->pinned, sizeof(int32_t) * n);
+  return EMX_OK;
+}
+
+int emx_qwen3_decode_device(emx_qwen3* m, int n) {
+  Q_REQUIRE(m && n >= 0, "emx_qwen3_decode_device: bad argument");
+  if (m->offset + n > m->c.kv_cap)
+    return fail(EMX_ERR_STATE, "static KV overflow offset=%d + n=%d > cap=%d", m->offset, n, m->c.kv_cap);
+  return run_steps(m, n);
+}
+
+int emx_qwen3_step_launches(emx_qwen3* m, int* n) {
+  Q_REQUIRE(m && n, "emx_qwen3_step_launches: null argument");
+  int rc = ensure_graph(m);
+  if (rc) return rc;
+  *n = m->step_launches;
+  return EMX_OK;
+}
+
+}  // extern "C"
