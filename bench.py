@@ -1,0 +1,373 @@
+"""Benchmark: batch-1 greedy decode (and prefill) of the Qwen3-1.7B-shape
+random-init model (attention int8 gs64, MLP int4 gs64, tied int4 embeddings)
+on B200, through libemx.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c3] [--prompt 128]
+    python bench.py --impl reference ...   # the CPU oracle (reference restatement) arm
+
+One step = one greedy decode token (the whole 28-layer forward + lm_head +
+argmax, replayed from a CUDA graph).  The timed region holds exactly K steps,
+bracketed by a barrier and a device synchronise, timed with CUDA events on
+the engine's stream; with N GPUs (torchrun) every rank runs its own replica
+(the 1.7B model is not sharded: "replicas only") and `value` is the sum of
+all ranks' tokens over the slowest rank's time.  Weights (1.1 GB) are larger
+than L2 (126 MB), so every step streams them from HBM.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path[:0] = [os.path.join(ROOT, "engine-mlx_b200"), os.path.join(ROOT, "oracle")]
+
+METRIC = "bs1 decode tok/s + prefill tok/s, Qwen3-1.7B-shape int4; % HBM roofline"
+UNIT = "tok/s"
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d.get("hbm_gbs", 6650.0), d.get("bf16_tflops", 1590.0), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+# ------------------------------------------------------------- roofline bytes
+def qbytes(N, K, bits, gs):
+    return N * K * bits // 8 + 2 * N * (K // gs) * 2
+
+
+def decode_bytes(cfg, ctx_len):
+    """Algorithmic HBM bytes of one decode token at `ctx_len` valid KV rows:
+    packed weights + bf16 scales/biases of every linear, norm weights, the
+    embedding row, the KV rows read and the new K/V row written."""
+    H, hd, L = cfg.hidden, cfg.head_dim, cfg.layers
+    per_layer = qbytes((cfg.n_q + 2 * cfg.n_kv) * hd, H, cfg.attn_bits, cfg.attn_group)
+    per_layer += qbytes(H, cfg.n_q * hd, cfg.attn_bits, cfg.attn_group)
+    if cfg.n_experts:
+        per_layer += qbytes(cfg.n_experts, H, cfg.router_bits, cfg.router_group)
+        per_layer += cfg.top_k * (qbytes(2 * cfg.moe_inter, H, cfg.expert_bits, cfg.expert_group) +
+                                  qbytes(H, cfg.moe_inter, cfg.expert_bits, cfg.expert_group))
+    else:
+        per_layer += qbytes(2 * cfg.inter, H, cfg.mlp_bits, cfg.mlp_group)
+        per_layer += qbytes(H, cfg.inter, cfg.mlp_bits, cfg.mlp_group)
+    per_layer += 2 * H * 2 + 2 * hd * 2                       # norm weights
+    per_layer += 2 * cfg.n_kv * ctx_len * hd * 2               # K and V rows read
+    per_layer += 2 * cfg.n_kv * hd * 2                         # new K/V row written
+    lm = qbytes(cfg.vocab, H, cfg.lm_bits if not cfg.tied else cfg.embed_bits,
+                cfg.lm_group if not cfg.tied else cfg.embed_group)
+    embed_row = H * cfg.embed_bits // 8 + 2 * (H // cfg.embed_group) * 2
+    return L * per_layer + lm + H * 2 + embed_row
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi samples (SM clock, throttle reasons) during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.device = device
+        self.lines = []
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "100", "-i", str(self.device)], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        time.sleep(0.2)
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() in ("active", "1"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------------ arms
+def cpu_baseline(cfg, seed, steps, threads=None):
+    """The CPU oracle (restatement of the reference path, OpenMP) on this host:
+    decode tok/s over a bounded sample (16-token prompt, `steps` greedy steps)."""
+    import numpy as np
+    import oracle
+
+    if threads:
+        oracle.lib().orc_set_num_threads(threads)
+    ck = oracle.make_checkpoint(cfg, seed)
+    m = oracle.Model(cfg, ck)
+    prompt = (np.arange(16, dtype=np.int32) * 7919) % cfg.vocab
+    t = m.prefill(prompt)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        t = m.decode(t)
+    dt = time.perf_counter() - t0
+    m.close()
+    return steps / dt, oracle.lib().orc_num_threads()
+
+
+def run_reference(args, cfg, rank):
+    if rank != 0:
+        return
+    steps = max(1, min(args.steps, 8))
+    for _ in range(min(args.warmup, 1)):
+        pass
+    v, cores = cpu_baseline(cfg, args.seed, steps)
+    line = {"metric": METRIC, "value": v, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus, "steps": steps,
+            "warmup": 0, "ms_per_step": 1000.0 / v, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16 activations, int4/int8 affine weights", "data": "synthetic",
+            "config": workload(args, cfg),
+            "cpu_baseline": {"value": v, "unit": UNIT, "cores": cores, "kind": "port",
+                             "sample": f"{args.config}: 16-token prompt then {steps} greedy decode steps "
+                                       "(CPU oracle restatement of the reference path; MLX itself is not "
+                                       "buildable here)"},
+            "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def workload(args, cfg):
+    return {"workload": f"{args.config} (Qwen3-1.7B shape)" if args.config == "c3" else args.config,
+            "model": f"random-init {args.config}", "hidden": cfg.hidden, "layers": cfg.layers,
+            "attn_bits": cfg.attn_bits, "mlp_bits": cfg.mlp_bits, "group_size": cfg.mlp_group,
+            "global_batch": 1, "prompt": args.prompt, "decode_tokens": args.steps, "seq_len": args.prompt,
+            "kv_cap": cfg.kv_cap, "parallelism": f"replicas x{args.gpus}",
+            "l2": "inputs larger than L2 (1.1 GB of weights streamed per token)"}
+
+
+def run_engine(args, cfg, rank, world, dist):
+    import numpy as np
+
+    import emx
+
+    dev = int(os.environ.get("LOCAL_RANK", "0"))
+    import torch
+
+    torch.cuda.set_device(dev)
+    ctx = emx.Ctx(dev)
+    m = emx.Qwen3(ctx, cfg)
+    m.init_random(args.seed)
+    stream_ptr = emx.C.c_void_p()
+    emx.lib().emx_ctx_stream(ctx.h, emx.C.byref(stream_ptr))
+    st = torch.cuda.ExternalStream(stream_ptr.value, device=dev)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    rng = np.random.default_rng(args.seed + rank)
+    prompt = rng.integers(0, cfg.vocab, args.prompt).astype(np.int32)
+    ids = ctx.put(prompt)
+    # ---- prefill tok/s (device-resident ids), a few repetitions
+    pre = {}
+    for T in sorted({args.prompt, *args.prefill_lengths}):
+        if T > cfg.max_prefill or T + 8 > cfg.kv_cap:
+            continue
+        idsT = ctx.put(rng.integers(0, cfg.vocab, T).astype(np.int32))
+        reps = 3 if T <= 2048 else 1
+        times = []
+        for r in range(reps + 1):
+            m.reset()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            ctx.synchronize()
+            e0.record(st)
+            m.prefill_device(idsT, T)
+            e1.record(st)
+            e1.synchronize()
+            if r:
+                times.append(e0.elapsed_time(e1))
+        pre[str(T)] = T / (statistics.median(times) / 1000.0)
+        idsT.free()
+    # ---- decode: warm-up W steps, then K timed steps
+    m.reset()
+    m.prefill_device(ids, args.prompt)
+    m.decode_device(max(args.warmup, 3))
+    ctx.synchronize()
+    launches = m.step_launches()
+    barrier()
+    with ClockSampler(dev) as clk:
+        ctx.synchronize()
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        m.decode_device(args.steps)
+        e1.record(st)
+        e1.synchronize()
+        ms = e0.elapsed_time(e1)
+        barrier()
+    start_ctx = args.prompt + max(args.warmup, 3)
+    ms_max = ms
+    if dist is not None:
+        t = torch.tensor([ms], device=f"cuda:{dev}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_max = float(t.item())
+    value = world * args.steps / (ms_max / 1000.0)
+    # ---- end to end through the public API: host token in, host token out
+    m.reset()
+    tok = m.prefill(prompt)
+    for _ in range(3):
+        tok = m.decode_step(tok)
+    n_e2e = min(args.steps, 256)
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(n_e2e):
+        tok = m.decode_step(tok)
+    e2e_s = time.perf_counter() - t0
+    e2e = n_e2e / e2e_s
+    if dist is not None:
+        t = torch.tensor([e2e_s], device=f"cuda:{dev}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e = world * n_e2e / float(t.item())
+    # ---- roofline of the decode step (all GEMVs + attention + lm_head)
+    hbm, _, kind = peaks()
+    mean_ctx = start_ctx + (args.steps - 1) / 2.0
+    step_bytes = decode_bytes(cfg, mean_ctx)
+    achieved = step_bytes / (ms / args.steps / 1000.0) / 1e9
+    # ---- the dominant kernel alone: the gate_up GEMV shape over rotating copies (> L2)
+    kern = gemv_kernel_roofline(ctx, st, cfg, torch, hbm)
+    m.close()
+    if rank != 0:
+        ctx.close()
+        return
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": max(args.warmup, 3), "ms_per_step": ms_max / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16 activations, int4/int8 affine weights",
+            "data": "synthetic (seeded random-init weights and token ids)", "config": workload(args, cfg),
+            "prefill_tok_s": pre, "decode_context": [start_ctx, start_ctx + args.steps],
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                         "traffic": None, "peak_kind": kind, "scope": "whole decode step",
+                         "bytes_per_step": step_bytes},
+            "kernel_roofline": kern,
+            "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4,
+                    "api": "emx_qwen3_decode_step", "steps": n_e2e},
+            "gpu_launches": launches * args.steps, "launches_per_step": launches,
+            "clocks": clk.summary()}
+    if world == 1 and not args.no_cpu_baseline:
+        v, cores = cpu_baseline(cfg, args.seed, args.cpu_steps)
+        line["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": cores, "kind": "port",
+                                "sample": f"{args.config}: 16-token prompt then {args.cpu_steps} greedy decode "
+                                          "steps on the CPU oracle (OpenMP)"}
+    print(json.dumps(line), flush=True)
+    ctx.close()
+
+
+def gemv_kernel_roofline(ctx, st, cfg, torch, hbm):
+    """qgemv on the gate_up shape [2*inter, hidden] (int4 gs64) alone: 16 weight
+    copies (> L2) rotated over 160 launches, CUDA events on the ctx stream."""
+    import numpy as np
+
+    import emx
+
+    N, K = 2 * cfg.inter, cfg.hidden
+    bits, gs = cfg.mlp_bits, cfg.mlp_group
+    copies = 16
+    wsz, ssz = N * K * bits // 8, N * (K // gs) * 2
+    w = [ctx.alloc(wsz) for _ in range(copies)]
+    s = [ctx.alloc(ssz) for _ in range(copies)]
+    b = [ctx.alloc(ssz) for _ in range(copies)]
+    for i in range(copies):
+        emx.lib().emx_memset(ctx.h, w[i].ptr, 0x5A, wsz)
+        emx.lib().emx_memset(ctx.h, s[i].ptr, 0x3C, ssz)
+        emx.lib().emx_memset(ctx.h, b[i].ptr, 0x00, ssz)
+    x = ctx.put(np.full(K, 0x3F80, np.uint16))
+    y = ctx.alloc(N * 2)
+    for i in range(8):
+        ctx.quantized_matmul(x, w[i % copies], s[i % copies], b[i % copies], 1, N, K, gs, bits, out=y)
+    ctx.synchronize()
+    n = 160
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for i in range(n):
+        ctx.quantized_matmul(x, w[i % copies], s[i % copies], b[i % copies], 1, N, K, gs, bits, out=y)
+    e1.record(st)
+    e1.synchronize()
+    us = e0.elapsed_time(e1) * 1000.0 / n
+    per = qbytes(N, K, bits, gs) + K * 2 + N * 2
+    for a in w + s + b + [x, y]:
+        a.free()
+    ach = per / (us * 1e-6) / 1e9
+    return {"kernel": "qgemv_kernel<4,64> (gate_up shape, standalone, no PDL overlap)", "shape": [N, K],
+            "bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s", "frac": ach / hbm, "us_per_launch": us,
+            "bytes_per_launch": per, "traffic": None}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1024)
+    ap.add_argument("--warmup", type=int, default=16)
+    ap.add_argument("--config", default="c3")
+    ap.add_argument("--prompt", type=int, default=128)
+    ap.add_argument("--prefill-lengths", type=int, nargs="*", default=[128, 2048, 8192])
+    ap.add_argument("--impl", default="emx", choices=["emx", "reference"])
+    ap.add_argument("--seed", type=int, default=1234)
+    ap.add_argument("--cpu-steps", type=int, default=4)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+
+    import emx
+
+    cfg = emx.CONFIGS[args.config]
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, cfg, rank)
+        return
+    import dataclasses
+
+    cfg = dataclasses.replace(cfg, kv_cap=max(cfg.kv_cap, args.prompt + args.steps + max(args.warmup, 3) + 8))
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as td
+
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+        td.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+        dist = td
+    try:
+        run_engine(args, cfg, rank, world, dist)
+    finally:
+        if dist is not None:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -89,11 +89,24 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Longest any bounded wait may take before it gives up.
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
+
 // Bounded wait on an mbarrier phase.  Returns false (and records a status)
-// when the spin limit is reached; the caller then skips the dependent work.
+// after kWaitLimitNs or kSpinLimit polls; the caller then skips the dependent
+// work (its outputs are garbage, the status word says so) and the kernel ends.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* status) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
   for (uint32_t i = 0; i < kSpinLimit; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 255u) == 255u && globaltimer_ns() - t0 > kWaitLimitNs) break;
   }
   report_status(status, kDevTimeoutMbar);
   return false;

@@ -382,6 +382,22 @@ __global__ void moe_combine_kernel(const bf16* y, const float* w, const int* n, 
   }
 }
 
+__global__ void add_f32_kernel(bf16* x, const float* add, size_t n, int round) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+    const float a = round ? bfround(add[i]) : add[i];
+    x[i] = f2bf(__fadd_rn(bf2f(x[i]), a));
+  }
+}
+
+__global__ void moe_residual_kernel(bf16* x, const bf16* y, const float* w, const int* n, int H) {
+  const int ns = *n;
+  for (int k = blockIdx.x * blockDim.x + threadIdx.x; k < H; k += gridDim.x * blockDim.x) {
+    float acc = 0.f;
+    for (int s = 0; s < ns; ++s) acc = __fadd_rn(acc, __fmul_rn(bf2f(y[(size_t)s * H + k]), w[s]));
+    x[k] = f2bf(__fadd_rn(bf2f(x[k]), acc));
+  }
+}
+
 cudaError_t launch_pdl(const void* fn, dim3 grid, dim3 block, void** args, cudaStream_t st, bool pdl) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
@@ -403,6 +419,17 @@ cudaError_t k_moe_route(const bf16* logits, int E, int k, int normalize, int e_b
   void* args[] = {(void*)&logits, (void*)&E, (void*)&k, (void*)&normalize, (void*)&e_base, (void*)&e_local,
                   (void*)&idx, (void*)&w, (void*)&n};
   return launch_pdl((const void*)moe_route_kernel, dim3(1), dim3(256), args, st, pdl);
+}
+
+cudaError_t k_add_f32(bf16* x, const float* add, size_t n, int round, cudaStream_t st) {
+  if (!n) return cudaSuccess;
+  add_f32_kernel<<<blocks_for(n, 256), 256, 0, st>>>(x, add, n, round);
+  return cudaGetLastError();
+}
+
+cudaError_t k_moe_residual(bf16* x, const bf16* y, const float* w, const int* n, int H, cudaStream_t st) {
+  moe_residual_kernel<<<(H + 255) / 256, 256, 0, st>>>(x, y, w, n, H);
+  return cudaGetLastError();
 }
 
 cudaError_t k_moe_combine(const bf16* y, const float* w, const int* n, int H, float* out, cudaStream_t st, bool pdl) {

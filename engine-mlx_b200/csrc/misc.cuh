@@ -70,6 +70,13 @@ cudaError_t k_moe_route(const bf16* logits, int E, int k, int normalize, int e_b
 // out[k] = sum_{s < *n} w[s] * y[s, k] in fp32, slot order (expert-parallel partial).
 cudaError_t k_moe_combine(const bf16* y, const float* w, const int* n, int H, float* out, cudaStream_t st, bool pdl);
 
+// x[i] = bf16(x[i] + addend[i]) with addend = bf16(add[i]) when `round`, else
+// add[i] (rows x n, fp32 add) — the residual add after a tensor- / expert-
+// parallel sum.
+cudaError_t k_add_f32(bf16* x, const float* add, size_t n, int round, cudaStream_t st);
+// x[k] = bf16(x[k] + sum_{s < *n} w[s] * y[s, k]) — one token's MoE residual.
+cudaError_t k_moe_residual(bf16* x, const bf16* y, const float* w, const int* n, int H, cudaStream_t st);
+
 // cache[nkv, cap, D] rows [offset, offset+T) <- upd[nkv, T, D].
 cudaError_t k_slice_update(bf16* cache, const bf16* upd, int nkv, int cap, int D, int offset, const int* offset_dev,
                            int T, cudaStream_t st);

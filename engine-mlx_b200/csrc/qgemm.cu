@@ -78,7 +78,8 @@ void gemm_ctx_destroy(GemmCtx* c) {
 int gemm_run(GemmCtx* c, const GemmArgs& a, cudaStream_t st) {
   if (a.M <= 0) return 0;
   if (cublasSetStream(c->h, st) != CUBLAS_STATUS_SUCCESS) return -1;
-  const bool epi_tmp = a.epi != kGemmStore;
+  const bool epi_tmp = a.epi == kGemmResid || a.epi == kGemmSwiglu;
+  const bool f32out = a.epi == kGemmF32;
   bf16* dst = a.y;
   if (epi_tmp) {
     int e = grow(reinterpret_cast<void**>(&c->tmp), &c->tmp_bytes, (size_t)a.M * a.N * 2);
@@ -102,9 +103,10 @@ int gemm_run(GemmCtx* c, const GemmArgs& a, cudaStream_t st) {
                                   reinterpret_cast<bf16*>(c->scratch), nr, a.K, a.gs, a.bits, st);
     if (ce != cudaSuccess) return (int)ce;
     // column-major view: C^T[N, M] = W[N, K] . X^T[K, M]
+    void* cptr = f32out ? static_cast<void*>(a.yf + n0) : static_cast<void*>(dst + n0);
     cublasStatus_t cs = cublasGemmEx(c->h, CUBLAS_OP_T, CUBLAS_OP_N, nr, a.M, a.K, &alpha, c->scratch, CUDA_R_16BF,
-                                     a.K, a.x, CUDA_R_16BF, a.K, &beta, dst + n0, CUDA_R_16BF, a.N,
-                                     CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
+                                     a.K, a.x, CUDA_R_16BF, a.K, &beta, cptr, f32out ? CUDA_R_32F : CUDA_R_16BF,
+                                     a.N, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
     if (cs != CUBLAS_STATUS_SUCCESS) return 1000 + (int)cs;
   }
   if (a.epi == kGemmResid) {

@@ -8,6 +8,7 @@ enum GemmEpi : int {
   kGemmStore = 0,   // y[m, n] = bf16(acc)
   kGemmResid = 1,   // y[m, n] = bf16(res[m, n] + bf16(acc))
   kGemmSwiglu = 2,  // weight rows [0,I) gate, [I,2I) up; y[m, n] (n < I) = silu(g) * u
+  kGemmF32 = 3,     // yf[m, n] = acc (fp32, e.g. a tensor-parallel partial)
 };
 
 struct GemmArgs {
@@ -19,6 +20,7 @@ struct GemmArgs {
   int epi;
   bf16* y;         // [M, N] (or [M, N/2] for SwiGLU)
   const bf16* res; // [M, N] for kGemmResid (may alias y)
+  float* yf;       // [M, N] for kGemmF32
 };
 
 struct GemmCtx;  // per-context scratch + library handles

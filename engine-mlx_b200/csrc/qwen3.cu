@@ -603,8 +603,9 @@ int run_steps(emx_qwen3* m, int n) {
 
 // --------------------------------------------------------------- prefill
 
-int gemm(emx_qwen3* m, const QW& q, const bf16* x, int T, int epi, bf16* y, const bf16* res) {
+int gemm(emx_qwen3* m, const QW& q, const bf16* x, int T, int epi, bf16* y, const bf16* res, float* yf = nullptr) {
   GemmArgs g = {};
+  g.yf = yf;
   g.x = x;
   g.w = q.w;
   g.s = q.s;
@@ -668,17 +669,67 @@ int prefill_impl(emx_qwen3* m, const int32_t* ids_dev, int T) {
     aa.out = m->pattn;
     aa.out_tnd = 1;
     if ((e = attn_prefill_launch(aa, st)) != cudaSuccess) return fail_cuda(e, "prefill attention");
-    if (m->tp) {
-      return fail(EMX_ERR_INVALID, "tensor-parallel prefill is not supported yet");
-    }
-    if ((rc = gemm(m, lw.o, m->pattn, T, kGemmResid, m->px, m->px))) return rc;
+    // row-split o_proj under TP: fp32 partials, sum over ranks, then the residual add
+    auto row_parallel = [&](const QW& q, const bf16* x) -> int {
+      if (!m->tp) return gemm(m, q, x, T, kGemmResid, m->px, m->px);
+      int r2 = gemm(m, q, x, T, kGemmF32, nullptr, nullptr, m->ppart);
+      if (r2) return r2;
+      if ((r2 = comm_all_reduce(m->comm, m->ppart, (size_t)T * H, EMX_F32, st))) return r2;
+      cudaError_t e2 = k_add_f32(m->px, m->ppart, (size_t)T * H, 1, st);
+      return e2 == cudaSuccess ? EMX_OK : fail_cuda(e2, "prefill residual");
+    };
+    if ((rc = row_parallel(lw.o, m->pattn))) return rc;
     if ((e = k_rms_norm(m->px, lw.post_norm, m->pxn, T, H, c.eps, c.norm_groups, st)) != cudaSuccess)
       return fail_cuda(e, "prefill norm");
     if (!m->moe) {
       if ((rc = gemm(m, lw.gate_up, m->pxn, T, kGemmSwiglu, m->ph, nullptr))) return rc;
-      if ((rc = gemm(m, lw.down, m->ph, T, kGemmResid, m->px, m->px))) return rc;
+      if ((rc = row_parallel(lw.down, m->ph))) return rc;
     } else {
-      return fail(EMX_ERR_INVALID, "MoE prefill is not supported yet");
+      // token by token through the decode-path MoE kernels (route, gathered
+      // expert SwiGLU, gathered expert down), as moe_forward_batch routes each
+      // token independently (crates/ops/src/moe.rs:174-207)
+      for (int t = 0; t < T; ++t) {
+        const bf16* xrow = m->pxn + (size_t)t * H;
+        GemvArgs ra = gemv_base(m, lw.router);
+        ra.pro = kProX;
+        ra.x = xrow;
+        ra.epi = kEpiStore;
+        ra.y = m->router_logits;
+        if ((e = gemv_launch(ra, lw.p_router, st, false)) != cudaSuccess) return fail_cuda(e, "prefill router");
+        if ((e = k_moe_route(m->router_logits, c.n_experts, c.top_k, c.norm_topk, m->e_base, m->E_l, m->moe_idx,
+                             m->moe_w, m->moe_n, st, false)) != cudaSuccess)
+          return fail_cuda(e, "prefill route");
+        GemvArgs ga = gemv_base(m, lw.e_gu);
+        ga.N = c.top_k * 2 * m->Im;
+        ga.pro = kProX;
+        ga.x = xrow;
+        ga.epi = kEpiSwiglu;
+        ga.y = m->hb;
+        ga.slot_expert = m->moe_idx;
+        ga.n_slots = m->moe_n;
+        ga.slot_rows = m->Im;
+        if ((e = gemv_launch(ga, lw.p_egu, st, false)) != cudaSuccess) return fail_cuda(e, "prefill experts");
+        GemvArgs da = gemv_base(m, lw.e_down);
+        da.N = c.top_k * H;
+        da.pro = kProX;
+        da.x = m->hb;
+        da.x_slots = c.top_k;
+        da.epi = kEpiStore;
+        da.y = m->moe_y;
+        da.slot_expert = m->moe_idx;
+        da.n_slots = m->moe_n;
+        da.slot_rows = H;
+        if ((e = gemv_launch(da, lw.p_edown, st, false)) != cudaSuccess) return fail_cuda(e, "prefill experts");
+        if (m->ep) {
+          if ((e = k_moe_combine(m->moe_y, m->moe_w, m->moe_n, H, m->part, st, false)) != cudaSuccess)
+            return fail_cuda(e, "prefill combine");
+          if ((rc = comm_all_reduce(m->comm, m->part, (size_t)H, EMX_F32, st))) return rc;
+          if ((e = k_add_f32(m->px + (size_t)t * H, m->part, (size_t)H, 0, st)) != cudaSuccess)
+            return fail_cuda(e, "prefill residual");
+        } else if ((e = k_moe_residual(m->px + (size_t)t * H, m->moe_y, m->moe_w, m->moe_n, H, st)) != cudaSuccess) {
+          return fail_cuda(e, "prefill residual");
+        }
+      }
     }
   }
   // final norm + lm_head on the last row, greedy token, offset += T
