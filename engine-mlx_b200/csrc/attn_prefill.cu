@@ -152,19 +152,24 @@ __global__ void __launch_bounds__(kThreads) attn_prefill_kernel(const AttnPrefil
       alpha[i] = (m_r[i] == -INFINITY) ? 0.f : exp2f(m_r[i] - mx[i]);
       m_r[i] = mx[i];
     }
-    uint32_t pf[4][4];  // P as A fragments: 4 k-steps of 16 keys
+    // P as A fragments (4 k-steps of 16 keys), split into bf16 hi + lo parts
+    // so that P.V keeps ~16 significant bits of each probability.
+    uint32_t pf[4][4], pl[4][4];
 #pragma unroll
     for (int nt = 0; nt < 8; ++nt) {
-      float p[4];
+      float p[4], lo[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const float mm = m_r[e >> 1];
         p[e] = (mm == -INFINITY) ? 0.f : exp2f(s[nt][e] - mm);
         rs[e >> 1] += p[e];
+        lo[e] = p[e] - bfround(p[e]);
       }
       const int ks = nt >> 1, hi = nt & 1;
       pf[ks][hi * 2 + 0] = pack_bf16(p[0], p[1]);
       pf[ks][hi * 2 + 1] = pack_bf16(p[2], p[3]);
+      pl[ks][hi * 2 + 0] = pack_bf16(lo[0], lo[1]);
+      pl[ks][hi * 2 + 1] = pack_bf16(lo[2], lo[3]);
     }
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
@@ -192,6 +197,8 @@ __global__ void __launch_bounds__(kThreads) attn_prefill_kernel(const AttnPrefil
         // A regs order: a0 (row g, k 0-7), a1 (row g+8, k 0-7), a2 (row g, k 8-15), a3 (row g+8, k 8-15)
         mma_bf16_16816(o[2 * db], a0, a1, a2, a3, vf[0], vf[1]);
         mma_bf16_16816(o[2 * db + 1], a0, a1, a2, a3, vf[2], vf[3]);
+        mma_bf16_16816(o[2 * db], pl[ks][0], pl[ks][1], pl[ks][2], pl[ks][3], vf[0], vf[1]);
+        mma_bf16_16816(o[2 * db + 1], pl[ks][0], pl[ks][1], pl[ks][2], pl[ks][3], vf[2], vf[3]);
       }
     }
     __syncthreads();

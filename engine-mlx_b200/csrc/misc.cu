@@ -10,6 +10,8 @@
 // take/embed (core.rs:5-14), slice_update / scatter_single (slice.rs:78-115).
 #include "misc.cuh"
 
+#include <algorithm>
+
 namespace emx {
 
 namespace {
@@ -53,16 +55,24 @@ inline int blocks_for(size_t n, int threads) {
   return (int)(b ? b : 1);
 }
 
-__global__ void dequant_kernel(const uint32_t* w, const bf16* s, const bf16* b, bf16* out, int N, int K, int gs,
-                               int bits) {
-  const int per = 32 / bits;
-  const int ng = K / gs;
-  const size_t total = (size_t)N * K;
-  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
-    const int n = (int)(i / K), k = (int)(i % K);
-    const uint32_t word = w[(size_t)n * (K / per) + k / per];
-    const uint32_t q = (word >> (bits * (k % per))) & ((1u << bits) - 1u);
-    out[i] = dequant1(q, s[(size_t)n * ng + k / gs], b[(size_t)n * ng + k / gs]);
+// One thread per packed word: 8 (int4) or 4 (int8) codes -> one vector store.
+template <int BITS>
+__global__ void dequant_kernel(const uint32_t* w, const bf16* s, const bf16* b, bf16* out, int N, int K, int gs) {
+  constexpr int PER = 32 / BITS;
+  const int wpr = K / PER, ng = K / gs;
+  const long long total = (long long)N * wpr;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int n = (int)(i / wpr), kw = (int)(i - (long long)n * wpr);
+    const uint32_t word = w[i];
+    const int g = kw * PER / gs;
+    const bf16 sv = s[(size_t)n * ng + g], bv = b[(size_t)n * ng + g];
+    __align__(16) bf16 v[PER];
+#pragma unroll
+    for (int e = 0; e < PER; ++e) v[e] = dequant1((word >> (BITS * e)) & ((1u << BITS) - 1u), sv, bv);
+    bf16* dst = out + (size_t)n * K + (size_t)kw * PER;
+    if (PER == 8) *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(v);
+    else *reinterpret_cast<uint2*>(dst) = *reinterpret_cast<const uint2*>(v);
   }
 }
 
@@ -439,7 +449,10 @@ cudaError_t k_moe_combine(const bf16* y, const float* w, const int* n, int H, fl
 
 cudaError_t k_dequantize(const uint32_t* w, const bf16* s, const bf16* b, bf16* out, int N, int K, int gs, int bits,
                          cudaStream_t st) {
-  dequant_kernel<<<blocks_for((size_t)N * K, 256), 256, 0, st>>>(w, s, b, out, N, K, gs, bits);
+  const size_t words = (size_t)N * K / (32 / bits);
+  const int blocks = (int)std::min<size_t>((words + 255) / 256, 148 * 64);
+  if (bits == 4) dequant_kernel<4><<<blocks, 256, 0, st>>>(w, s, b, out, N, K, gs);
+  else dequant_kernel<8><<<blocks, 256, 0, st>>>(w, s, b, out, N, K, gs);
   return cudaGetLastError();
 }
 

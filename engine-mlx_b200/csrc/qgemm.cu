@@ -86,10 +86,12 @@ int gemm_run(GemmCtx* c, const GemmArgs& a, cudaStream_t st) {
     if (e) return e;
     dst = c->tmp;
   }
-  // rows of W per chunk so that the dequantized chunk fits the scratch
+  // rows of W per chunk so that the dequantized chunk fits the scratch (the
+  // whole matrix up to 1 GiB, so a prefill GEMM is one library call)
   size_t row_bytes = (size_t)a.K * 2;
-  if (c->scratch_bytes < row_bytes * 16) {
-    int e = grow(&c->scratch, &c->scratch_bytes, row_bytes * 1024);
+  const size_t want = std::min((size_t)a.N * row_bytes, (size_t)1 << 30);
+  if (c->scratch_bytes < want) {
+    int e = grow(&c->scratch, &c->scratch_bytes, want);
     if (e) return e;
   }
   int rows = (int)std::min<size_t>((size_t)a.N, c->scratch_bytes / row_bytes);
