@@ -12,8 +12,10 @@
 // exp(-1e9 - m) == 0).  Work split: grid (splits, n_kv); each CTA owns one KV
 // head (and the q heads that share it) over a contiguous slice of the valid
 // rows, keeps the softmax partial (m, l, acc), and the last CTA of a head
-// merges the slices.  Before griddepcontrol.wait each CTA asks L2 to prefetch
-// its K/V slice (a hint only, so a stale offset is harmless).
+// merges the slices.  Only ceil(L / kMinRows) splits (at most the grid's) take
+// part, so short contexts do not pay for a wide merge; the others return at
+// once.  Before griddepcontrol.wait each CTA asks L2 to prefetch its K/V
+// slice (a hint only, so a stale offset is harmless).
 #include "attn_decode.cuh"
 
 namespace emx {
@@ -23,6 +25,12 @@ namespace {
 constexpr int kHD = 128;
 constexpr int kThreads = 128;
 constexpr int kTile = 128;
+constexpr int kMinRows = 64;  // fewest rows a split is given
+
+__device__ __forceinline__ int active_splits(int L, int grid) {
+  const int s = (L + kMinRows - 1) / kMinRows;
+  return s < grid ? s : grid;
+}
 
 template <int HPG>
 __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const AttnDecodeArgs a) {
@@ -31,11 +39,11 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const AttnDecodeA
   __shared__ float sc[HPG][kTile];     // scores -> probabilities for one tile
   __shared__ float stat_m[HPG], stat_l[HPG], stat_a[HPG];
   __shared__ float sacc[4][HPG][kHD];  // per-warp partial outputs
+  __shared__ float swt[HPG][64];       // merge weights of the splits
   __shared__ unsigned last;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int split = blockIdx.x, kvh = blockIdx.y;
-  const int splits = gridDim.x;
   const size_t head_stride = (size_t)a.cap * kHD;
   bf16* kc = a.kc + (size_t)kvh * head_stride;
   bf16* vc = a.vc + (size_t)kvh * head_stride;
@@ -44,7 +52,8 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const AttnDecodeA
   // ---- L2 warm-up of this CTA's K/V rows (offset may be one step stale) ----
   if (tid == 0) {
     const int pg = a.pos ? *reinterpret_cast<const volatile int*>(a.pos) : a.pos_host;
-    if (pg >= 0 && pg < a.cap) {
+    const int splits = active_splits(pg + 1, gridDim.x);
+    if (pg >= 0 && pg < a.cap && split < splits) {
       const int L = pg + 1;
       const int p0 = (int)((long long)split * L / splits), p1 = (int)((long long)(split + 1) * L / splits);
       if (p1 > p0) {
@@ -62,6 +71,8 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const AttnDecodeA
     return;
   }
   const int L = p + 1;
+  const int splits = active_splits(L, gridDim.x);
+  if (split >= splits) return;
   const int p0 = (int)((long long)split * L / splits), p1 = (int)((long long)(split + 1) * L / splits);
   const bool owns_new = (p >= p0 && p < p1) && a.q_in == nullptr;
 
@@ -239,20 +250,35 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const AttnDecodeA
   __syncthreads();
   if (!last) return;
   __threadfence();
-  const volatile float* vp = a.part + (size_t)kvh * splits * part_stride;
+  // merge: the splits' (m, l) into per-split weights exp(m_s - M) / sum, then
+  // every output element sums its splits with all loads in flight at once
+  // (L2-coherent loads: the partials were written by other CTAs)
+  const float* pb = a.part + (size_t)kvh * splits * part_stride;
+  for (int h = warp; h < HPG; h += 4) {
+    float ms = -INFINITY, ls = 0.f;
+    if (lane < splits) {
+      ms = __ldcg(pb + (size_t)lane * part_stride + h * (kHD + 2));
+      ls = __ldcg(pb + (size_t)lane * part_stride + h * (kHD + 2) + 1);
+    }
+    float ms2 = -INFINITY, ls2 = 0.f;
+    if (lane + 32 < splits) {
+      ms2 = __ldcg(pb + (size_t)(lane + 32) * part_stride + h * (kHD + 2));
+      ls2 = __ldcg(pb + (size_t)(lane + 32) * part_stride + h * (kHD + 2) + 1);
+    }
+    const float M = warp_max(fmaxf(ms, ms2));
+    const float w1 = ms == -INFINITY ? 0.f : expf(ms - M), w2 = ms2 == -INFINITY ? 0.f : expf(ms2 - M);
+    const float den = warp_sum(fmaf(w1, ls, w2 * ls2));
+    if (lane < splits) swt[h][lane] = __fdiv_rn(w1, den);
+    if (lane + 32 < splits) swt[h][lane + 32] = __fdiv_rn(w2, den);
+  }
+  __syncthreads();
   for (int i = tid; i < HPG * kHD; i += kThreads) {
     const int h = i / kHD, d = i % kHD;
-    float M = -INFINITY;
-    for (int s = 0; s < splits; ++s) M = fmaxf(M, vp[s * part_stride + h * (kHD + 2)]);
-    float num = 0.f, den = 0.f;
-    for (int s = 0; s < splits; ++s) {
-      const float ms = vp[s * part_stride + h * (kHD + 2)];
-      if (ms == -INFINITY) continue;
-      const float w = expf(ms - M);
-      den = fmaf(w, vp[s * part_stride + h * (kHD + 2) + 1], den);
-      num = fmaf(w, vp[s * part_stride + h * (kHD + 2) + 2 + d], num);
-    }
-    a.out[(size_t)(kvh * HPG + h) * kHD + d] = f2bf(__fdiv_rn(num, den));
+    const float* src = pb + h * (kHD + 2) + 2 + d;
+    float num = 0.f;
+#pragma unroll 8
+    for (int s2 = 0; s2 < splits; ++s2) num = fmaf(swt[h][s2], __ldcg(src + (size_t)s2 * part_stride), num);
+    a.out[(size_t)(kvh * HPG + h) * kHD + d] = f2bf(num);
   }
   if (tid == 0) a.ticket[kvh] = 0u;
 }

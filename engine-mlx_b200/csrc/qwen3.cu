@@ -876,6 +876,17 @@ int emx_qwen3_read_tensor(emx_qwen3* m, const char* name, void* host, size_t byt
   return ctx_sync_check(m->ctx, "emx_qwen3_read_tensor");
 }
 
+int emx_qwen3_read_kv(emx_qwen3* m, int layer, int which, void* host, size_t bytes) {
+  Q_REQUIRE(m && host, "emx_qwen3_read_kv: null argument");
+  Q_REQUIRE(layer >= 0 && layer < m->c.layers && (which == 0 || which == 1),
+            "emx_qwen3_read_kv: layer %d / which %d out of range", layer, which);
+  const size_t need = m->kv_layer * sizeof(bf16);
+  Q_REQUIRE(bytes == need, "emx_qwen3_read_kv: cache slab has %zu bytes, got %zu", need, bytes);
+  const bf16* src = m->kv + m->kv_layer * (2 * (size_t)layer + which);
+  EMX_CHECK_CUDA(cudaMemcpyAsync(host, src, need, cudaMemcpyDeviceToHost, m->ctx->stream), "emx_qwen3_read_kv");
+  return ctx_sync_check(m->ctx, "emx_qwen3_read_kv");
+}
+
 int emx_qwen3_init_random(emx_qwen3* m, uint64_t seed) {
   Q_REQUIRE(m, "emx_qwen3_init_random: null model");
   return init_random_impl(m, seed);

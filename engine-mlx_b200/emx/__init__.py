@@ -87,6 +87,7 @@ _SIGS = {
     "emx_qwen3_destroy": (C.c_int, [C.c_void_p]),
     "emx_qwen3_load_tensor": (C.c_int, [C.c_void_p, C.c_char_p, C.c_void_p, C.c_size_t]),
     "emx_qwen3_read_tensor": (C.c_int, [C.c_void_p, C.c_char_p, C.c_void_p, C.c_size_t]),
+    "emx_qwen3_read_kv": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_size_t]),
     "emx_qwen3_init_random": (C.c_int, [C.c_void_p, C.c_uint64]),
     "emx_qwen3_reset": (C.c_int, [C.c_void_p]),
     "emx_qwen3_offset": (C.c_int, [C.c_void_p, C.POINTER(C.c_int)]),
@@ -337,6 +338,7 @@ class Comm:
         _check(lib().emx_comm_init(ctx.h, buf, nranks, rank, C.byref(h)))
         self.h = h.value
         self.ctx = ctx
+        self.nranks, self.rank = nranks, rank
 
     def all_reduce_sum(self, buf: Buffer, count: int, dtype: int):
         _check(lib().emx_all_reduce_sum(self.h, buf.ptr, count, dtype))
@@ -453,7 +455,7 @@ class Qwen3:
     """Qwen3Engine equivalent over the C ABI (crates/serve/src/engine.rs, forward_qwen3.rs)."""
 
     def __init__(self, ctx: Ctx, cfg: Qwen3Config, comm: Optional[Comm] = None):
-        self.ctx, self.cfg = ctx, cfg
+        self.ctx, self.cfg, self.comm = ctx, cfg, comm
         self._c = cfg.c_struct()
         h = C.c_void_p()
         _check(lib().emx_qwen3_create(ctx.h, C.byref(self._c), comm.h if comm else None, C.byref(h)))
@@ -472,6 +474,14 @@ class Qwen3:
         buf = np.empty(nbytes, dtype=np.uint8)
         _check(lib().emx_qwen3_read_tensor(self.h, name.encode(), buf.ctypes.data, nbytes))
         return buf.tobytes()
+
+    def read_kv(self, layer: int, which: int) -> np.ndarray:
+        """This rank's K (which=0) or V (which=1) cache of one layer, bf16 bits [n_kv_local, kv_cap, head_dim]."""
+        c = self.cfg
+        nkv = c.n_kv // (self.comm.nranks if self.comm is not None and c.n_experts == 0 else 1)
+        out = np.empty((nkv, c.kv_cap, c.head_dim), dtype=np.uint16)
+        _check(lib().emx_qwen3_read_kv(self.h, layer, which, out.ctypes.data, out.nbytes))
+        return out
 
     def init_random(self, seed: int):
         _check(lib().emx_qwen3_init_random(self.h, C.c_uint64(seed)))

@@ -191,6 +191,11 @@ int emx_qwen3_destroy(emx_qwen3* m);
 int emx_qwen3_load_tensor(emx_qwen3* m, const char* name, const void* host, size_t bytes);
 /* Copies a loaded tensor (this rank's shard, fused layout) back to the host. */
 int emx_qwen3_read_tensor(emx_qwen3* m, const char* name, void* host, size_t bytes);
+/* Copies layer `layer`'s K (which = 0) or V (which = 1) cache of this rank to
+ * the host: bf16 [n_kv_local, kv_cap, head_dim], rows >= offset unspecified.
+ * The engine's per-layer kv_bufs pair (crates/serve/src/engine_ext.rs:69-90)
+ * holds the same K/V arrays. */
+int emx_qwen3_read_kv(emx_qwen3* m, int layer, int which, void* host, size_t bytes);
 /* Seeded synthetic weights generated on the device (linears N(0, 0.02^2)
  * quantized with the affine formula, norms 1 + N(0, 0.05^2) in bf16). */
 int emx_qwen3_init_random(emx_qwen3* m, uint64_t seed);

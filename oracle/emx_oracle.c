@@ -191,8 +191,16 @@ void orc_dequantize(const uint32_t* wq, const uint16_t* scales, const uint16_t* 
 
 /* mlx_quantized_matmul (crates/mlx-ffi/src/ops/real/transform.rs:127-138),
  * called as qmatmul (crates/ops/src/quant.rs:57-76) for every Qwen3 linear. */
+/* Summation order of orc_qmatmul's fp32 reductions: 0 ascending k (the
+ * reference's order), 1 descending.  Both are valid fp32 evaluations of the
+ * same sums; running a model under each measures the bf16 rounding-noise
+ * floor that any re-ordered implementation (a GPU kernel) is held against. */
+static int g_sum_reverse = 0;
+void orc_set_sum_order(int reverse) { g_sum_reverse = reverse ? 1 : 0; }
+
 void orc_qmatmul(const uint16_t* x, const uint32_t* wq, const uint16_t* scales, const uint16_t* biases,
                  int M, int N, int K, int gs, int bits, uint16_t* y) {
+    const int rev = g_sum_reverse;
     const int per = 32 / bits;
     const int ng = K / gs;
     if (M == 1) {
@@ -208,11 +216,13 @@ void orc_qmatmul(const uint16_t* x, const uint32_t* wq, const uint16_t* scales, 
         for (int n = 0; n < N; ++n) {
             const uint32_t* qr = wq + (size_t)n * (K / per);
             float acc = 0.0f;
-            for (int g = 0; g < ng; ++g) {
+            for (int gi = 0; gi < ng; ++gi) {
+                const int g = rev ? ng - 1 - gi : gi;
                 float dot = 0.0f;
                 const float* xg = xf + g * gs;
                 const uint32_t* qw = qr + (g * gs) / per;
-                for (int i = 0; i < gs; ++i) {
+                for (int ii = 0; ii < gs; ++ii) {
+                    const int i = rev ? gs - 1 - ii : ii;
                     uint32_t q = (qw[i / per] >> (bits * (i % per))) & ((1u << bits) - 1u);
                     dot += xg[i] * (float)q;
                 }
@@ -243,7 +253,10 @@ void orc_qmatmul(const uint16_t* x, const uint32_t* wq, const uint16_t* scales, 
             const float* xr = xf + (size_t)m * K;
             const float* wr = wf + (size_t)n * K;
             float acc = 0.0f;
-            for (int k = 0; k < K; ++k) acc += xr[k] * wr[k];
+            if (rev)
+                for (int k = K - 1; k >= 0; --k) acc += xr[k] * wr[k];
+            else
+                for (int k = 0; k < K; ++k) acc += xr[k] * wr[k];
             y[(size_t)m * N + n] = TOBF(acc);
         }
     }

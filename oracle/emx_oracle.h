@@ -47,6 +47,8 @@ void orc_f32_to_bf16_n(const float* in, uint16_t* out, size_t n);
 void orc_bf16_to_f32_n(const uint16_t* in, float* out, size_t n);
 int orc_num_threads(void);
 void orc_set_num_threads(int n);
+/* 0: reductions in ascending index order (default); 1: descending. */
+void orc_set_sum_order(int reverse);
 
 /* ---- seeded synthetic generator (same stream as emx_fill_normal) ------- */
 uint64_t orc_splitmix64(uint64_t x);

@@ -22,6 +22,7 @@ _SIGS = {
     "orc_f64_to_bf16": (C.c_uint16, [C.c_double]),
     "orc_num_threads": (C.c_int, []),
     "orc_set_num_threads": (None, [C.c_int]),
+    "orc_set_sum_order": (None, [C.c_int]),
     "orc_name_stream": (C.c_uint64, [C.c_char_p]),
     "orc_fill_normal": (None, [C.c_uint64, C.c_uint64, C.c_size_t, C.c_float, C.c_float, _P]),
     "orc_quantize": (None, [_P, C.c_int, C.c_int, C.c_int, C.c_int, _P, _P, _P]),

@@ -200,3 +200,21 @@ def test_generator_statistics():
     assert abs(float(z.mean())) < 0.01 and abs(float(z.std()) - 1.0) < 0.01
     z2 = oracle.fill_normal(5, oracle.name_stream("stats"), 1000, 0.0, 1.0)
     assert np.array_equal(z[:1000], z2)
+
+
+def test_sum_order_switch_changes_only_rounding():
+    """The descending-order reductions (used to measure the noise floor) give a
+    different but equally valid fp32 evaluation, and the switch resets."""
+    rng = np.random.default_rng(5)
+    x = oracle.to_bf16(rng.standard_normal((8, 2048)).astype(np.float32))
+    wq, s, b = oracle.quantize(oracle.to_bf16(rng.standard_normal((1024, 2048)).astype(np.float32) * 0.02), 64, 4)
+    fwd = oracle.qmatmul(x, wq, s, b, 64, 4)
+    oracle.lib().orc_set_sum_order(1)
+    try:
+        rev = oracle.qmatmul(x, wq, s, b, 64, 4)
+    finally:
+        oracle.lib().orc_set_sum_order(0)
+    again = oracle.qmatmul(x, wq, s, b, 64, 4)
+    assert np.array_equal(fwd, again)
+    ulps = np.abs(fwd.astype(np.int32) - rev.astype(np.int32))
+    assert ulps.max() <= 1 and 0 < np.count_nonzero(ulps) < ulps.size // 100
