@@ -68,6 +68,7 @@ _SIGS = {
                            C.c_void_p]),
     "emx_sdpa_causal": (C.c_int, [C.c_void_p] + [C.c_void_p] * 4 + [C.c_int] * 4 + [C.c_float, C.c_int]),
     "emx_sdpa_decode": (C.c_int, [C.c_void_p] + [C.c_void_p] * 4 + [C.c_int] * 5 + [C.c_float]),
+    "emx_sdpa_decode_noalloc": (C.c_int, [C.c_void_p] + [C.c_void_p] * 4 + [C.c_int] * 5 + [C.c_float]),
     "emx_silu": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t]),
     "emx_multiply": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t]),
     "emx_add": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t]),
@@ -270,6 +271,11 @@ class Ctx:
     def sdpa_decode(self, q, kc, vc, nq, nkv, cap, hd, length, scale):
         out = self.alloc(nq * hd * 2)
         _check(lib().emx_sdpa_decode(self.h, q.ptr, kc.ptr, vc.ptr, out.ptr, nq, nkv, cap, hd, length, scale))
+        return out
+
+    def sdpa_decode_noalloc(self, q, kc, vc, out, nq, nkv, cap, hd, length, scale):
+        """emx_sdpa_decode into a caller-provided `out`, with no device allocation."""
+        _check(lib().emx_sdpa_decode_noalloc(self.h, q.ptr, kc.ptr, vc.ptr, out.ptr, nq, nkv, cap, hd, length, scale))
         return out
 
     def silu(self, x, n):

@@ -117,6 +117,17 @@ int emx_sdpa_causal(emx_ctx* ctx, const void* q, const void* k, const void* v, v
  * q[nq,D] attends rows [0, length) of k,v[nkv,cap,D]; out[nq,D]. */
 int emx_sdpa_decode(emx_ctx* ctx, const void* q, const void* k_cache, const void* v_cache, void* out, int nq,
                     int nkv, int cap, int head_dim, int length, float scale);
+/* No counterpart in the reference (MLX allocates every op's output and
+ * temporaries itself).  emx_sdpa_decode with the same arguments and a
+ * bit-identical result, but it allocates nothing: its split partials and
+ * merge tickets live in one static 1 MiB device array (n_kv <= 64 and
+ * n_q * splits * (head_dim + 2) * 4 bytes <= 1 MiB - 256, else
+ * EMX_ERR_INVALID).  The array is shared per device, so calls that overlap
+ * in time race; calls on one stream are safe.  The first call on a device
+ * looks the array up (cudaGetSymbolAddress) and should come before any
+ * stream capture begins. */
+int emx_sdpa_decode_noalloc(emx_ctx* ctx, const void* q, const void* k_cache, const void* v_cache, void* out, int nq,
+                            int nkv, int cap, int head_dim, int length, float scale);
 /* MlxCtx::silu / multiply / add (blas.rs:17-37), bf16 elementwise. */
 int emx_silu(emx_ctx* ctx, const void* x, void* out, size_t n);
 int emx_multiply(emx_ctx* ctx, const void* a, const void* b, void* out, size_t n);
