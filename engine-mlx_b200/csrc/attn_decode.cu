@@ -14,8 +14,15 @@
 // rows, keeps the softmax partial (m, l, acc), and the last CTA of a head
 // merges the slices.  Only ceil(L / kMinRows) splits (at most the grid's) take
 // part, so short contexts do not pay for a wide merge; the others return at
-// once.  Before griddepcontrol.wait each CTA asks L2 to prefetch its K/V
-// slice (a hint only, so a stale offset is harmless).
+// once.
+//
+// Every cached row before the new one is final before this kernel starts
+// (it was written by an earlier step), so before griddepcontrol.wait each
+// CTA asks the bulk-copy engine for its first 64-row K and V tiles (a ring of
+// two) and stages the norm weights and RoPE frequencies: after the wait only
+// the new row's q/k/v depend on the previous kernel.  The position is read
+// again after the wait; should it differ from the one the copies were
+// planned with, the CTA lets those copies land and plans again.
 #include "attn_decode.cuh"
 
 namespace emx {
@@ -24,22 +31,39 @@ namespace {
 
 constexpr int kHD = 128;
 constexpr int kThreads = 128;
-constexpr int kTile = 128;
+constexpr int kTile = 64;     // rows per K / V tile
+constexpr int kNBuf = 2;      // tiles in flight
 constexpr int kMinRows = 64;  // fewest rows a split is given
+constexpr int kTileBytes = kTile * kHD * 2;
+constexpr int kDynSmem = 128 + 2 * kNBuf * kTileBytes;
 
 __device__ __forceinline__ int active_splits(int L, int grid) {
   const int s = (L + kMinRows - 1) / kMinRows;
   return s < grid ? s : grid;
 }
 
+__device__ __forceinline__ void split_range(int L, int splits, int split, int& p0, int& p1) {
+  p0 = (int)((long long)split * L / splits);
+  p1 = (int)((long long)(split + 1) * L / splits);
+}
+
 template <int HPG>
 __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const AttnDecodeArgs a) {
+  extern __shared__ __align__(128) unsigned char dsm[];
+  uint64_t* mbar = reinterpret_cast<uint64_t*>(dsm);
+  bf16* kb = reinterpret_cast<bf16*>(dsm + 128);  // [kNBuf][kTile][kHD]
+  bf16* vb = kb + kNBuf * kTile * kHD;
   __shared__ float qs[HPG][kHD];       // q * scale (fp32 of the bf16 rope output)
   __shared__ float qn[HPG + 1][kHD];   // normed q heads (+ k) before rope
   __shared__ float sc[HPG][kTile];     // scores -> probabilities for one tile
   __shared__ float stat_m[HPG], stat_l[HPG], stat_a[HPG];
   __shared__ float sacc[4][HPG][kHD];  // per-warp partial outputs
   __shared__ float swt[HPG][64];       // merge weights of the splits
+  __shared__ float nwq[kHD], nwk[kHD], invf[kHD / 2];
+  __shared__ __align__(16) bf16 knew[kHD];  // the new row (owner split)
+  __shared__ __align__(16) bf16 vnew[kHD];
+  __shared__ int base_use[kNBuf];  // completed uses of each buffer before this plan
+  __shared__ int plan_p;           // position the issued copies were planned for
   __shared__ unsigned last;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -48,32 +72,85 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const AttnDecodeA
   bf16* kc = a.kc + (size_t)kvh * head_stride;
   bf16* vc = a.vc + (size_t)kvh * head_stride;
 
-  pdl_trigger();
-  // ---- L2 warm-up of this CTA's K/V rows (offset may be one step stale) ----
   if (tid == 0) {
+    for (int i = 0; i < kNBuf; ++i) {
+      mbar_init(&mbar[i], 1);
+      base_use[i] = 0;
+    }
+    fence_mbar_init();
+  }
+  // static inputs (weights, RoPE table) before the wait
+  if (!a.q_in) {
+    for (int i = tid; i < kHD; i += kThreads) {
+      nwq[i] = a.q_norm ? bf2f(a.q_norm[i]) : 1.0f;
+      nwk[i] = a.k_norm ? bf2f(a.k_norm[i]) : 1.0f;
+    }
+    for (int i = tid; i < kHD / 2; i += kThreads) invf[i] = a.inv_freq[i];
+  }
+  __syncthreads();
+  pdl_trigger();
+
+  // Tile t of the current plan: rows [p0 + 64t, ...) of this split, minus
+  // the new row p when this kernel computes it (never copied); buffer
+  // t % kNBuf.  With q given (no new row) every row up to p is copied.
+  const int row_end_adj = a.q_in ? 1 : 0;
+  auto issue = [&](int t, int p, int p0, int p1) {
+    const int buf = t % kNBuf;
+    const int r0 = p0 + t * kTile;
+    const int r1 = min(min(r0 + kTile, p1), p + row_end_adj);
+    const uint32_t bytes = r1 > r0 ? (uint32_t)(r1 - r0) * kHD * 2 : 0u;
+    mbar_arrive_expect_tx(&mbar[buf], 2 * bytes);
+    if (bytes) {
+      bulk_g2s(kb + (size_t)buf * kTile * kHD, kc + (size_t)r0 * kHD, bytes, &mbar[buf]);
+      bulk_g2s(vb + (size_t)buf * kTile * kHD, vc + (size_t)r0 * kHD, bytes, &mbar[buf]);
+    }
+  };
+  auto parity = [&](int t) -> uint32_t { return (uint32_t)((base_use[t % kNBuf] + t / kNBuf) & 1); };
+
+  int n_issued = 0;  // thread 0: tiles issued under the current plan
+  if (tid == 0) {
+    plan_p = -1;
     const int pg = a.pos ? *reinterpret_cast<const volatile int*>(a.pos) : a.pos_host;
-    const int splits = active_splits(pg + 1, gridDim.x);
-    if (pg >= 0 && pg < a.cap && split < splits) {
-      const int L = pg + 1;
-      const int p0 = (int)((long long)split * L / splits), p1 = (int)((long long)(split + 1) * L / splits);
-      if (p1 > p0) {
-        const uint32_t bytes = (uint32_t)(p1 - p0) * kHD * 2;
-        bulk_prefetch_l2(kc + (size_t)p0 * kHD, bytes);
-        bulk_prefetch_l2(vc + (size_t)p0 * kHD, bytes);
+    if (pg >= 0 && pg < a.cap) {
+      const int splits = active_splits(pg + 1, gridDim.x);
+      if (split < splits) {
+        int p0, p1;
+        split_range(pg + 1, splits, split, p0, p1);
+        const int ntile = (p1 - p0 + kTile - 1) / kTile;
+        for (; n_issued < min(ntile, kNBuf); ++n_issued) issue(n_issued, pg, p0, p1);
+        if (p1 - p0 > kNBuf * kTile) {  // later tiles: an L2 hint only
+          const uint32_t rest = (uint32_t)(p1 - p0 - kNBuf * kTile) * kHD * 2;
+          bulk_prefetch_l2(kc + (size_t)(p0 + kNBuf * kTile) * kHD, rest);
+          bulk_prefetch_l2(vc + (size_t)(p0 + kNBuf * kTile) * kHD, rest);
+        }
+        plan_p = pg;
       }
     }
   }
   pdl_wait();
 
   const int p = a.pos ? *a.pos : a.pos_host;
-  if (p < 0 || p >= a.cap) {
-    if (tid == 0 && split == 0 && kvh == 0) report_status(a.status, kDevKvOverflow);
+  const bool bad = p < 0 || p >= a.cap;
+  const int L = p + 1;
+  const int splits = bad ? 0 : active_splits(L, gridDim.x);
+  int p0 = 0, p1 = 0;
+  if (!bad) split_range(L, splits, split, p0, p1);
+  const int ntile = (p1 - p0 + kTile - 1) / kTile;
+  // a plan for another position (or one no longer needed): let its copies land
+  if (tid == 0 && plan_p >= 0 && (plan_p != p || bad || split >= splits)) {
+    for (int t = 0; t < n_issued; ++t) mbar_wait_bounded(&mbar[t % kNBuf], parity(t), a.status);
+    for (int b = 0; b < kNBuf; ++b) base_use[b] += (n_issued + kNBuf - 1 - b) / kNBuf;
+    n_issued = 0;
+    plan_p = -1;
+  }
+  if (bad || split >= splits) {
+    if (bad && tid == 0 && split == 0 && kvh == 0) report_status(a.status, kDevKvOverflow);
     return;
   }
-  const int L = p + 1;
-  const int splits = active_splits(L, gridDim.x);
-  if (split >= splits) return;
-  const int p0 = (int)((long long)split * L / splits), p1 = (int)((long long)(split + 1) * L / splits);
+  if (tid == 0 && plan_p < 0) {
+    for (; n_issued < min(ntile, kNBuf); ++n_issued) issue(n_issued, p, p0, p1);
+    plan_p = p;
+  }
   const bool owns_new = (p >= p0 && p < p1) && a.q_in == nullptr;
 
   // ---- q heads (and k/v of the new row when owned): rms_norm + rope -------
@@ -86,20 +163,23 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const AttnDecodeA
     const bool is_k = hh == HPG;
     const bf16* src = is_k ? a.qkv + (size_t)a.nq * kHD + (size_t)kvh * kHD
                            : a.qkv + (size_t)(kvh * HPG + hh) * kHD;
-    const bf16* nw = is_k ? a.k_norm : a.q_norm;
+    const float* nw = is_k ? nwk : nwq;
+    const bool has_norm = is_k ? a.k_norm != nullptr : a.q_norm != nullptr;
     float v[4];
     float ss = 0.f;
+    const uint2 raw = *reinterpret_cast<const uint2*>(src + lane * 4);
+    v[0] = __uint_as_float(raw.x << 16);
+    v[1] = __uint_as_float(raw.x & 0xffff0000u);
+    v[2] = __uint_as_float(raw.y << 16);
+    v[3] = __uint_as_float(raw.y & 0xffff0000u);
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      v[e] = bf2f(src[lane * 4 + e]);
-      ss = fmaf(v[e], v[e], ss);
-    }
+    for (int e = 0; e < 4; ++e) ss = fmaf(v[e], v[e], ss);
     ss = warp_sum(ss);
     const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)kHD), a.eps)));
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       const int d = lane * 4 + e;
-      qn[hh][d] = nw ? bfround(__fmul_rn(bfround(__fmul_rn(v[e], inv)), bf2f(nw[d]))) : v[e];
+      qn[hh][d] = has_norm ? bfround(__fmul_rn(bfround(__fmul_rn(v[e], inv)), nw[d])) : v[e];
     }
     __syncwarp();
     const float fp = (float)p;
@@ -107,7 +187,7 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const AttnDecodeA
     for (int e = 0; e < 4; ++e) {
       const int d = lane * 4 + e;
       const int i = d & (kHD / 2 - 1);
-      const float th = __fmul_rn(fp, a.inv_freq[i]);
+      const float th = __fmul_rn(fp, invf[i]);
       float sn, cs;
       sincosf(th, &sn, &cs);
       const float x1 = qn[hh][i], x2 = qn[hh][i + kHD / 2];
@@ -115,13 +195,18 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const AttnDecodeA
       if (d < kHD / 2) o = __fsub_rn(__fmul_rn(x1, cs), __fmul_rn(x2, sn));
       else o = __fadd_rn(__fmul_rn(x1, sn), __fmul_rn(x2, cs));
       o = bfround(o);
-      if (is_k) kc[(size_t)p * kHD + d] = f2bf(o);
-      else qs[hh][d] = __fmul_rn(o, a.scale);
+      if (is_k) {
+        kc[(size_t)p * kHD + d] = f2bf(o);
+        knew[d] = f2bf(o);
+      } else {
+        qs[hh][d] = __fmul_rn(o, a.scale);
+      }
     }
     if (is_k) {
       const bf16* vsrc = a.qkv + (size_t)(a.nq + a.nkv) * kHD + (size_t)kvh * kHD;
-#pragma unroll
-      for (int e = 0; e < 4; ++e) vc[(size_t)p * kHD + lane * 4 + e] = vsrc[lane * 4 + e];
+      const uint2 vr = *reinterpret_cast<const uint2*>(vsrc + lane * 4);
+      *reinterpret_cast<uint2*>(vc + (size_t)p * kHD + lane * 4) = vr;
+      *reinterpret_cast<uint2*>(vnew + lane * 4) = vr;
     }
   }
   if (tid < HPG) {
@@ -144,15 +229,27 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const AttnDecodeA
 #pragma unroll
     for (int e = 0; e < 8; ++e) acc[h][e] = 0.f;
 
-  for (int t0 = p0; t0 < p1; t0 += kTile) {
+  for (int t = 0; t < ntile; ++t) {
+    const int buf = t % kNBuf;
+    const int t0 = p0 + t * kTile;
     const int tn = min(kTile, p1 - t0);
+    bf16* kt = kb + (size_t)buf * kTile * kHD;
+    bf16* vt = vb + (size_t)buf * kTile * kHD;
+    mbar_wait_bounded(&mbar[buf], parity(t), a.status);
+    // the new row is never copied: the owner puts it in place
+    if (owns_new && p >= t0 && p < t0 + tn) {
+      const int r = p - t0;
+      if (tid < kHD / 8) {
+        reinterpret_cast<uint4*>(kt + (size_t)r * kHD)[tid] = reinterpret_cast<const uint4*>(knew)[tid];
+        reinterpret_cast<uint4*>(vt + (size_t)r * kHD)[tid] = reinterpret_cast<const uint4*>(vnew)[tid];
+      }
+      __syncthreads();
+    }
     // QK^T: two rows per warp step, 16 lanes x 8 dims per row
-    // (trip count uniform across the warp: both halves run every shuffle)
     for (int jb = warp * 2; jb < tn; jb += 8) {
       const int jj = jb + half;
       const bool valid = jj < tn;
-      const uint4 kv = valid ? *reinterpret_cast<const uint4*>(kc + (size_t)(t0 + jj) * kHD + dl)
-                             : make_uint4(0u, 0u, 0u, 0u);
+      const uint4 kv = valid ? *reinterpret_cast<const uint4*>(kt + (size_t)jj * kHD + dl) : make_uint4(0u, 0u, 0u, 0u);
       const uint32_t kw[4] = {kv.x, kv.y, kv.z, kv.w};
       float kf[8];
 #pragma unroll
@@ -204,7 +301,7 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const AttnDecodeA
       for (int e = 0; e < 8; ++e) acc[h][e] *= al;
     }
     for (int jj = warp * 2 + half; jj < tn; jj += 8) {
-      const uint4 vv = *reinterpret_cast<const uint4*>(vc + (size_t)(t0 + jj) * kHD + dl);
+      const uint4 vv = *reinterpret_cast<const uint4*>(vt + (size_t)jj * kHD + dl);
       const uint32_t vw[4] = {vv.x, vv.y, vv.z, vv.w};
       float vf[8];
 #pragma unroll
@@ -220,6 +317,11 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const AttnDecodeA
       }
     }
     __syncthreads();
+    // refill this buffer with the tile kNBuf ahead
+    if (tid == 0 && t + kNBuf < ntile) {
+      fence_proxy_async();
+      issue(t + kNBuf, p, p0, p1);
+    }
   }
 
   // ---- merge the 8 row slots, publish this split's partial ---------------
@@ -234,6 +336,15 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const AttnDecodeA
       for (int e = 0; e < 8; ++e) sacc[warp][h][dl + e] = acc[h][e];
   }
   __syncthreads();
+  if (splits == 1) {
+    // a single split needs no merge: normalise and store
+    for (int i = tid; i < HPG * kHD; i += kThreads) {
+      const int h = i / kHD, d = i % kHD;
+      const float num = sacc[0][h][d] + sacc[1][h][d] + sacc[2][h][d] + sacc[3][h][d];
+      a.out[(size_t)(kvh * HPG + h) * kHD + d] = f2bf(__fmul_rn(num, __fdiv_rn(1.0f, stat_l[h])));
+    }
+    return;
+  }
   const size_t part_stride = (size_t)HPG * (kHD + 2);
   float* part = a.part + ((size_t)kvh * splits + split) * part_stride;
   for (int i = tid; i < HPG * kHD; i += kThreads) {
@@ -285,17 +396,20 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const AttnDecodeA
 
 template <int HPG>
 cudaError_t launch_t(const AttnDecodeArgs& a, cudaStream_t st, bool pdl) {
+  auto kern = attn_decode_kernel<HPG>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kDynSmem);
+  if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.splits, a.nkv);
   cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = 0;
+  cfg.dynamicSmemBytes = kDynSmem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, attn_decode_kernel<HPG>, a);
+  return cudaLaunchKernelEx(&cfg, kern, a);
 }
 
 }  // namespace
@@ -309,6 +423,7 @@ int attn_decode_splits(int nkv, int num_sms) {
 
 cudaError_t attn_decode_launch(const AttnDecodeArgs& a, cudaStream_t st, bool pdl) {
   if (a.head_dim != kHD || a.nkv <= 0 || a.nq % a.nkv != 0) return cudaErrorInvalidValue;
+  if ((reinterpret_cast<uintptr_t>(a.kc) | reinterpret_cast<uintptr_t>(a.vc)) & 15) return cudaErrorInvalidValue;
   switch (a.nq / a.nkv) {
     case 1: return launch_t<1>(a, st, pdl);
     case 2: return launch_t<2>(a, st, pdl);

@@ -147,10 +147,12 @@ __device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes
 
 // ---------------------------------------------------------- tensor cores
 // Warp-level m16n8k16 bf16 MMA with fp32 accumulation (used by the batch-1
-// GEMV as a dot-product engine and by the prefill kernels' fragments).
+// GEMV as a dot-product engine and by the prefill kernels' fragments).  Not
+// volatile: it is a pure function of its registers, and the compiler must be
+// free to hoist the next shared-memory loads above it.
 __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                                uint32_t b0, uint32_t b1) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
       "{%0,%1,%2,%3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])

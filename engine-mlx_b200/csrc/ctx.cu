@@ -4,6 +4,7 @@
 // its kernel on the context stream and returns a status; none has a host
 // fallback.
 #include "ctx.cuh"
+#include "pgemv.cuh"
 
 #include <cstdio>
 #include <cstring>
@@ -323,6 +324,52 @@ int emx_quantized_matmul(emx_ctx* c, const void* x, const void* w, const void* s
   g.y = static_cast<bf16*>(y);
   rc = gemm_run(c->gemm, g, c->stream);
   if (rc) return fail(EMX_ERR_CUDA, "emx_quantized_matmul (gemm): error %d", rc);
+  return EMX_OK;
+}
+
+int emx_qpack_bytes(int N, int K, int gs, int bits, size_t* bytes) {
+  EMX_REQUIRE(bytes, "emx_qpack_bytes: null argument");
+  int rc = check_quant(N, K, gs, bits, "emx_qpack_bytes");
+  if (rc) return rc;
+  EMX_REQUIRE(N % 16 == 0, "emx_qpack_bytes: N=%d must be a multiple of 16", N);
+  *bytes = pgemv_packed_bytes(N, K, bits, gs, PackMap{1, N, 1});
+  return EMX_OK;
+}
+
+int emx_qpack(emx_ctx* c, const void* w, const void* s, const void* b, void* out, int N, int K, int gs, int bits) {
+  EMX_REQUIRE(c && w && s && b && out, "emx_qpack: null argument");
+  int rc = check_quant(N, K, gs, bits, "emx_qpack");
+  if (rc) return rc;
+  EMX_REQUIRE(N % 16 == 0, "emx_qpack: N=%d must be a multiple of 16", N);
+  EMX_CHECK_CUDA(pgemv_pack(static_cast<const uint32_t*>(w), static_cast<const bf16*>(s), static_cast<const bf16*>(b),
+                            N, K, bits, gs, PackMap{1, N, 1}, static_cast<unsigned char*>(out), c->stream),
+                 "emx_qpack");
+  return EMX_OK;
+}
+
+int emx_quantized_matvec_packed(emx_ctx* c, const void* x, const void* packed, void* y, int N, int K, int gs,
+                                int bits) {
+  EMX_REQUIRE(c && x && packed && y, "emx_quantized_matvec_packed: null argument");
+  int rc = check_quant(N, K, gs, bits, "emx_quantized_matvec_packed");
+  if (rc) return rc;
+  EMX_REQUIRE(N % 16 == 0, "emx_quantized_matvec_packed: N=%d must be a multiple of 16", N);
+  EMX_REQUIRE(aligned16(packed) && aligned16(x), "emx_quantized_matvec_packed: x / packed must be 16-byte aligned");
+  PgemvPlan plan;
+  if (pgemv_make_plan(N, K, bits, gs, kEpiStore, 1, c->num_sms, 110 * 1024, &plan))
+    return fail(EMX_ERR_INVALID, "emx_quantized_matvec_packed: unsupported shape N=%d K=%d", N, K);
+  GemvArgs a = {};
+  a.w = static_cast<const uint32_t*>(packed);
+  a.N = N;
+  a.K = K;
+  a.bits = bits;
+  a.gs = gs;
+  a.pro = kProX;
+  a.epi = kEpiStore;
+  a.x = static_cast<const bf16*>(x);
+  a.x_slots = 1;
+  a.y = static_cast<bf16*>(y);
+  a.status = c->status;
+  EMX_CHECK_CUDA(pgemv_launch(a, plan, c->stream, false), "emx_quantized_matvec_packed");
   return EMX_OK;
 }
 

@@ -24,6 +24,7 @@
 #include "ctx.cuh"
 #include "misc.cuh"
 #include "qgemm.cuh"
+#include "pgemv.cuh"
 #include "qgemv.cuh"
 
 namespace emx {
@@ -33,6 +34,8 @@ struct QW {
   bf16* s = nullptr;
   bf16* b = nullptr;
   int N = 0, K = 0, bits = 4, gs = 64;
+  unsigned char* pk = nullptr;  // packed copy for the decode GEMV (pgemv layout)
+  PackMap map{1, 0, 1};
   size_t wbytes() const { return (size_t)N * K / (32 / bits) * 4; }
   size_t sbytes() const { return (size_t)N * (K / gs) * 2; }
 };
@@ -44,7 +47,7 @@ struct LayerW {
   bf16* k_norm = nullptr;
   QW qkv, o, gate_up, down;  // dense
   QW router, e_gu, e_down;   // MoE: e_gu [E_l][2*Im][H], e_down [E_l][H][Im]
-  GemvPlan p_qkv{}, p_o{}, p_gu{}, p_down{}, p_router{}, p_egu{}, p_edown{};
+  PgemvPlan p_qkv{}, p_o{}, p_gu{}, p_down{}, p_router{}, p_egu{}, p_edown{};
 };
 
 // How one checkpoint tensor maps onto this rank's device memory.
@@ -91,7 +94,8 @@ struct emx_qwen3 {
   QW embed, lm;
   bf16* final_norm = nullptr;
   float* inv_freq = nullptr;
-  GemvPlan p_lm{};
+  PgemvPlan p_lm{};
+  bool packed_ok = false;  // packed copies match the loaded weights
   bf16* kv = nullptr;
   size_t kv_layer = 0;  // elements of one layer's K (or V)
   std::map<std::string, Spec> specs;
@@ -217,9 +221,7 @@ void add_norm(emx_qwen3* m, const std::string& name, bf16* dst, int len) {
 
 GemvArgs gemv_base(const emx_qwen3* m, const QW& q) {
   GemvArgs a = {};
-  a.w = q.w;
-  a.s = q.s;
-  a.b = q.b;
+  a.w = reinterpret_cast<const uint32_t*>(q.pk);
   a.N = q.N;
   a.K = q.K;
   a.bits = q.bits;
@@ -231,10 +233,47 @@ GemvArgs gemv_base(const emx_qwen3* m, const QW& q) {
   return a;
 }
 
-int plan(emx_qwen3* m, const QW& q, int epi, int x_slots, int n_rows_override, GemvPlan* p) {
+// Shared memory a decode GEMV may claim: two CTAs per SM, so that the next
+// kernel of the step is resident (and streaming its weights) while this one
+// computes.  The lm_head, last in the step, may take more for a deeper ring.
+constexpr int kGemvBudget = 110 * 1024;
+constexpr int kGemvBudgetLast = 160 * 1024;
+
+int plan(emx_qwen3* m, const QW& q, int epi, int x_slots, int n_rows_override, PgemvPlan* p,
+         int budget = kGemvBudget) {
   const int N = n_rows_override > 0 ? n_rows_override : q.N;
-  if (gemv_make_plan(N, q.K, q.bits, q.gs, epi, x_slots, m->ctx->num_sms, p))
+  if (pgemv_make_plan(N, q.K, q.bits, q.gs, epi, x_slots, m->ctx->num_sms, budget, p))
     return fail(EMX_ERR_INVALID, "no GEMV plan for N=%d K=%d bits=%d group=%d", N, q.K, q.bits, q.gs);
+  return EMX_OK;
+}
+
+// Device memory for the packed copy of a decode matrix.
+int alloc_packed(emx_qwen3* m, QW& q, int blocks, int R, int halves) {
+  q.map = PackMap{blocks, R, halves};
+  void* v = nullptr;
+  int rc = alloc(m, pgemv_packed_bytes(q.N, q.K, q.bits, q.gs, q.map), &v);
+  q.pk = static_cast<unsigned char*>(v);
+  return rc;
+}
+
+int pack_one(emx_qwen3* m, QW& q) {
+  if (!q.pk) return EMX_OK;
+  cudaError_t e = pgemv_pack(q.w, q.s, q.b, q.N, q.K, q.bits, q.gs, q.map, q.pk, m->ctx->stream);
+  return e == cudaSuccess ? EMX_OK : fail_cuda(e, "weight packing");
+}
+
+// Re-packs every decode matrix after weights changed (load / init_random).
+int ensure_packed(emx_qwen3* m) {
+  if (m->packed_ok) return EMX_OK;
+  int rc;
+  if ((rc = pack_one(m, m->c.tied ? m->embed : m->lm))) return rc;
+  for (auto& lw : m->L) {
+    if ((rc = pack_one(m, lw.qkv)) || (rc = pack_one(m, lw.o)) || (rc = pack_one(m, lw.gate_up)) ||
+        (rc = pack_one(m, lw.down)) || (rc = pack_one(m, lw.router)) || (rc = pack_one(m, lw.e_gu)) ||
+        (rc = pack_one(m, lw.e_down)))
+      return rc;
+  }
+  m->packed_ok = true;
   return EMX_OK;
 }
 
@@ -268,6 +307,7 @@ int build(emx_qwen3* m) {
     if ((rc = alloc_qw(m, m->lm, c.vocab, H, c.lm_bits, c.lm_group))) return rc;
     add_quant(m, "lm_head", &m->lm, c.vocab, 1, H, 0, c.vocab, 0, H, 0, 0, 1, c.vocab);
   }
+  if ((rc = alloc_packed(m, c.tied ? m->embed : m->lm, 1, c.vocab, 1))) return rc;
   if ((rc = alloc_t(m, H, &m->final_norm))) return rc;
   add_norm(m, "model.norm.weight", m->final_norm, H);
   for (int l = 0; l < c.layers; ++l) {
@@ -288,23 +328,30 @@ int build(emx_qwen3* m) {
               m->Nqkv);
     add_quant(m, p + "self_attn.v_proj", &lw.qkv, c.n_kv * hd, 1, H, kr0, m->nkv * hd, 0, H,
               (m->nq + m->nkv) * hd, 0, 1, m->Nqkv);
+    if ((rc = alloc_packed(m, lw.qkv, 1, m->Nqkv, 1))) return rc;
     if ((rc = alloc_qw(m, lw.o, H, m->nq * hd, c.attn_bits, c.attn_group))) return rc;
+    if ((rc = alloc_packed(m, lw.o, 1, H, 1))) return rc;
     add_quant(m, p + "self_attn.o_proj", &lw.o, H, 1, c.n_q * hd, 0, H, qr0, m->nq * hd, 0, 0, 1, H);
     if (!m->moe) {
       if ((rc = alloc_qw(m, lw.gate_up, 2 * m->I, H, c.mlp_bits, c.mlp_group))) return rc;
       const int ir0 = m->tp ? r * m->I : 0;
       add_quant(m, p + "mlp.gate_proj", &lw.gate_up, c.inter, 1, H, ir0, m->I, 0, H, 0, 0, 1, 2 * m->I);
       add_quant(m, p + "mlp.up_proj", &lw.gate_up, c.inter, 1, H, ir0, m->I, 0, H, m->I, 0, 1, 2 * m->I);
+      if ((rc = alloc_packed(m, lw.gate_up, 1, 2 * m->I, 2))) return rc;
       if ((rc = alloc_qw(m, lw.down, H, m->I, c.mlp_bits, c.mlp_group))) return rc;
+      if ((rc = alloc_packed(m, lw.down, 1, H, 1))) return rc;
       add_quant(m, p + "mlp.down_proj", &lw.down, H, 1, c.inter, 0, H, ir0, m->I, 0, 0, 1, H);
     } else {
       const int E = c.n_experts, Im = m->Im;
       if ((rc = alloc_qw(m, lw.router, E, H, c.router_bits, c.router_group))) return rc;
       add_quant(m, p + "mlp.gate", &lw.router, E, 1, H, 0, E, 0, H, 0, 0, 1, E);
+      if ((rc = alloc_packed(m, lw.router, 1, E, 1))) return rc;
       if ((rc = alloc_qw(m, lw.e_gu, m->E_l * 2 * Im, H, c.expert_bits, c.expert_group))) return rc;
+      if ((rc = alloc_packed(m, lw.e_gu, m->E_l, 2 * Im, 2))) return rc;
       add_quant(m, p + "mlp.switch_mlp.gate_proj", &lw.e_gu, Im, E, H, 0, Im, 0, H, 0, m->e_base, m->E_l, 2 * Im);
       add_quant(m, p + "mlp.switch_mlp.up_proj", &lw.e_gu, Im, E, H, 0, Im, 0, H, Im, m->e_base, m->E_l, 2 * Im);
       if ((rc = alloc_qw(m, lw.e_down, m->E_l * H, Im, c.expert_bits, c.expert_group))) return rc;
+      if ((rc = alloc_packed(m, lw.e_down, m->E_l, H, 1))) return rc;
       add_quant(m, p + "mlp.switch_mlp.down_proj", &lw.e_down, H, E, Im, 0, H, 0, Im, 0, m->e_base, m->E_l, H);
     }
     // launch plans
@@ -319,7 +366,7 @@ int build(emx_qwen3* m) {
       if ((rc = plan(m, lw.e_down, kEpiStore, c.top_k, c.top_k * H, &lw.p_edown))) return rc;
     }
   }
-  if ((rc = plan(m, c.tied ? m->embed : m->lm, kEpiArgmax, 1, 0, &m->p_lm))) return rc;
+  if ((rc = plan(m, c.tied ? m->embed : m->lm, kEpiArgmax, 1, 0, &m->p_lm, kGemvBudgetLast))) return rc;
   // rope table, KV cache, decode state
   if ((rc = alloc_t(m, hd / 2, &m->inv_freq))) return rc;
   if (k_rope_inv_freq(m->inv_freq, hd, c.rope_theta, m->ctx->stream) != cudaSuccess)
@@ -366,8 +413,8 @@ int build(emx_qwen3* m) {
 
 // ------------------------------------------------------------ decode step
 
-int launch_gemv(emx_qwen3* m, const GemvArgs& a, const GemvPlan& p, bool pdl) {
-  cudaError_t e = gemv_launch(a, p, m->ctx->stream, pdl);
+int launch_gemv(emx_qwen3* m, const GemvArgs& a, const PgemvPlan& p, bool pdl) {
+  cudaError_t e = pgemv_launch(a, p, m->ctx->stream, pdl);
   if (e != cudaSuccess) return fail_cuda(e, "decode gemv launch");
   ++m->step_launches;
   return EMX_OK;
@@ -594,7 +641,9 @@ int ensure_graph(emx_qwen3* m) {
 }
 
 int run_steps(emx_qwen3* m, int n) {
-  int rc = ensure_graph(m);
+  int rc = ensure_packed(m);
+  if (rc) return rc;
+  rc = ensure_graph(m);
   if (rc) return rc;
   for (int i = 0; i < n; ++i) EMX_CHECK_CUDA(cudaGraphLaunch(m->gexec, m->ctx->stream), "graph launch");
   m->offset += n;
@@ -628,7 +677,8 @@ int prefill_impl(emx_qwen3* m, const int32_t* ids_dev, int T) {
   cudaStream_t st = m->ctx->stream;
   const int H = m->H, hd = m->hd;
   const int off = m->offset;
-  int rc;
+  int rc = ensure_packed(m);
+  if (rc) return rc;
   cudaError_t e = k_embed(m->embed.w, m->embed.s, m->embed.b, ids_dev, T, H, m->embed.gs, m->embed.bits, c.vocab,
                           m->px, m->ctx->status, st);
   if (e != cudaSuccess) return fail_cuda(e, "prefill embed");
@@ -695,7 +745,7 @@ int prefill_impl(emx_qwen3* m, const int32_t* ids_dev, int T) {
         ra.x = xrow;
         ra.epi = kEpiStore;
         ra.y = m->router_logits;
-        if ((e = gemv_launch(ra, lw.p_router, st, false)) != cudaSuccess) return fail_cuda(e, "prefill router");
+        if ((e = pgemv_launch(ra, lw.p_router, st, false)) != cudaSuccess) return fail_cuda(e, "prefill router");
         if ((e = k_moe_route(m->router_logits, c.n_experts, c.top_k, c.norm_topk, m->e_base, m->E_l, m->moe_idx,
                              m->moe_w, m->moe_n, st, false)) != cudaSuccess)
           return fail_cuda(e, "prefill route");
@@ -708,7 +758,7 @@ int prefill_impl(emx_qwen3* m, const int32_t* ids_dev, int T) {
         ga.slot_expert = m->moe_idx;
         ga.n_slots = m->moe_n;
         ga.slot_rows = m->Im;
-        if ((e = gemv_launch(ga, lw.p_egu, st, false)) != cudaSuccess) return fail_cuda(e, "prefill experts");
+        if ((e = pgemv_launch(ga, lw.p_egu, st, false)) != cudaSuccess) return fail_cuda(e, "prefill experts");
         GemvArgs da = gemv_base(m, lw.e_down);
         da.N = c.top_k * H;
         da.pro = kProX;
@@ -719,7 +769,7 @@ int prefill_impl(emx_qwen3* m, const int32_t* ids_dev, int T) {
         da.slot_expert = m->moe_idx;
         da.n_slots = m->moe_n;
         da.slot_rows = H;
-        if ((e = gemv_launch(da, lw.p_edown, st, false)) != cudaSuccess) return fail_cuda(e, "prefill experts");
+        if ((e = pgemv_launch(da, lw.p_edown, st, false)) != cudaSuccess) return fail_cuda(e, "prefill experts");
         if (m->ep) {
           if ((e = k_moe_combine(m->moe_y, m->moe_w, m->moe_n, H, m->part, st, false)) != cudaSuccess)
             return fail_cuda(e, "prefill combine");
@@ -746,7 +796,7 @@ int prefill_impl(emx_qwen3* m, const int32_t* ids_dev, int T) {
   a.tok_out = m->token;
   a.pos = m->pos;
   a.pos_inc = T;
-  e = gemv_launch(a, m->p_lm, st, false);
+  e = pgemv_launch(a, m->p_lm, st, false);
   if (e != cudaSuccess) return fail_cuda(e, "prefill lm_head");
   m->offset += T;
   return EMX_OK;
@@ -849,6 +899,7 @@ int emx_qwen3_load_tensor(emx_qwen3* m, const char* name, const void* host, size
   const Spec& s = it->second;
   Q_REQUIRE(bytes == s.src_total, "emx_qwen3_load_tensor: '%s' has %zu bytes, expected %zu", name, bytes,
             s.src_total);
+  m->packed_ok = false;
   const char* src = static_cast<const char*>(host);
   for (int b = 0; b < s.blocks; ++b) {
     EMX_CHECK_CUDA(cudaMemcpy2DAsync(static_cast<char*>(s.dst) + (size_t)b * s.dst_block, s.dst_pitch,
@@ -889,6 +940,7 @@ int emx_qwen3_read_kv(emx_qwen3* m, int layer, int which, void* host, size_t byt
 
 int emx_qwen3_init_random(emx_qwen3* m, uint64_t seed) {
   Q_REQUIRE(m, "emx_qwen3_init_random: null model");
+  m->packed_ok = false;
   return init_random_impl(m, seed);
 }
 

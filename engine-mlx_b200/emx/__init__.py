@@ -67,6 +67,9 @@ _SIGS = {
     "emx_rope": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_float, C.c_int,
                            C.c_void_p]),
     "emx_sdpa_causal": (C.c_int, [C.c_void_p] + [C.c_void_p] * 4 + [C.c_int] * 4 + [C.c_float, C.c_int]),
+    "emx_qpack_bytes": (C.c_int, [C.c_int] * 4 + [C.POINTER(C.c_size_t)]),
+    "emx_qpack": (C.c_int, [C.c_void_p] * 5 + [C.c_int] * 4),
+    "emx_quantized_matvec_packed": (C.c_int, [C.c_void_p] * 4 + [C.c_int] * 4),
     "emx_sdpa_decode": (C.c_int, [C.c_void_p] + [C.c_void_p] * 4 + [C.c_int] * 5 + [C.c_float]),
     "emx_sdpa_decode_noalloc": (C.c_int, [C.c_void_p] + [C.c_void_p] * 4 + [C.c_int] * 5 + [C.c_float]),
     "emx_silu": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t]),
@@ -234,6 +237,19 @@ class Ctx:
         _check(lib().emx_quantized_matmul(self.h, x.ptr, w.ptr, s.ptr, b.ptr, out.ptr, M, N, K, int(transpose),
                                           group_size, bits))
         return out
+
+    def qpack(self, w, s, b, N, K, group_size, bits):
+        """Packed (decode-GEMV) layout of an affine tensor, in a new buffer."""
+        n = C.c_size_t()
+        _check(lib().emx_qpack_bytes(N, K, group_size, bits, C.byref(n)))
+        out = self.alloc(n.value)
+        _check(lib().emx_qpack(self.h, w.ptr, s.ptr, b.ptr, out.ptr, N, K, group_size, bits))
+        return out
+
+    def quantized_matvec_packed(self, x, packed, N, K, group_size, bits):
+        y = self.alloc(N * 2)
+        _check(lib().emx_quantized_matvec_packed(self.h, x.ptr, packed.ptr, y.ptr, N, K, group_size, bits))
+        return y
 
     def dequantize(self, w, s, b, N, K, group_size, bits):
         out = self.alloc(N * K * 2)

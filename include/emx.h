@@ -91,6 +91,18 @@ int emx_set_memory_limit(emx_ctx* ctx, size_t limit, size_t* previous);
  * M == 1 runs the batch-1 GEMV, M > 1 the prefill GEMM. */
 int emx_quantized_matmul(emx_ctx* ctx, const void* x, const void* w, const void* scales, const void* biases, void* y,
                          int M, int N, int K, int transpose, int group_size, int bits);
+/* No reference counterpart (MLX reads the affine layout directly): the
+ * load-time re-layout of an affine tensor (w [N][K*bits/32], scales/biases
+ * [N][K/group]) into the packed tile layout that the engine's batch-1 decode
+ * GEMV streams.  emx_qpack_bytes gives the size of `out` (N a multiple of
+ * 16). */
+int emx_qpack_bytes(int N, int K, int group_size, int bits, size_t* bytes);
+int emx_qpack(emx_ctx* ctx, const void* w, const void* scales, const void* biases, void* out, int N, int K,
+              int group_size, int bits);
+/* MlxCtx::quantized_matmul at M == 1 (transform.rs:127-138) over a packed
+ * tensor: y[N] = x[K] . dequant(w)^T, the decode GEMV the engine runs. */
+int emx_quantized_matvec_packed(emx_ctx* ctx, const void* x, const void* packed, void* y, int N, int K,
+                                int group_size, int bits);
 /* MlxCtx::dequantize_weight (transform.rs:95-109): out bf16[N,K]. */
 int emx_dequantize(emx_ctx* ctx, const void* w, const void* scales, const void* biases, void* out, int N, int K,
                    int group_size, int bits);

@@ -118,6 +118,45 @@ def test_gemv_model_shapes(ctx, N, K, bits):
     assert_close(y.read(np.uint16, (1, N)), ref, what=f"N={N} K={K}")
 
 
+@pytest.mark.parametrize("bits,gs", QCASES)
+def test_packed_gemv_matches_oracle(ctx, bits, gs):
+    """The engine's decode GEMV (load-time packed layout) on the committed fixtures."""
+    t = f"q{bits}_{gs}"
+    w, s, b = (ctx.put(OPS[t + p]) for p in ("_w", "_s", "_b"))
+    pk = ctx.qpack(w, s, b, 64, 1024, gs, bits)
+    y = ctx.quantized_matvec_packed(ctx.put(OPS[t + "_x1"]), pk, 64, 1024, gs, bits)
+    got = y.read(np.uint16, (1, 64))
+    assert_close(got, OPS[t + "_y1"], what=t)
+
+
+@pytest.mark.parametrize("N,K,bits", [(151936, 2048, 4), (256, 25600, 4), (4096, 2048, 8), (2048, 6144, 4),
+                                      (12288, 2048, 4), (2048, 2048, 8), (1024, 768, 4), (128, 2048, 4),
+                                      (2048, 3072, 4), (1536, 2048, 4)])
+def test_packed_gemv_model_shapes(ctx, N, K, bits):
+    """Decode shapes of the configs through the packed GEMV: lm_head, 32B down,
+    1.7B qkv / o int8, 1.7B gate_up / down, MoE expert down (K=768: a half-empty
+    last span), router, 0.6B down, MoE expert gate_up."""
+    q = _linear(11, f"shape.{N}.{K}", N, K, 64, bits)
+    x = oracle.to_bf16(np.random.default_rng(N + K).standard_normal((1, K)).astype(np.float32))
+    ref = oracle.qmatmul(x, q["weight"], q["scales"], q["biases"], 64, bits)
+    pk = ctx.qpack(ctx.put(q["weight"]), ctx.put(q["scales"]), ctx.put(q["biases"]), N, K, 64, bits)
+    got = ctx.quantized_matvec_packed(ctx.put(x), pk, N, K, 64, bits).read(np.uint16, (1, N))
+    assert_close(got, ref, what=f"N={N} K={K}")
+    # fp32 sums in another order flip the bf16 rounding of a few outputs
+    assert np.mean(got != ref) <= 0.03, f"bit-equal fraction {np.mean(got == ref):.4f}"
+    assert ctx.device_status() == 0
+
+
+def test_packed_gemv_rejects_bad_shapes(ctx):
+    b = ctx.alloc(1 << 16)
+    with pytest.raises(emx.EmxError):
+        ctx.quantized_matvec_packed(b, b, 72, 1024, 64, 4)  # N not a multiple of 16
+    with pytest.raises(emx.EmxError):
+        ctx.quantized_matvec_packed(b, b, 64, 1000, 64, 4)  # K not a multiple of the group
+    with pytest.raises(emx.EmxError):
+        ctx.qpack(b, b, b, 64, 1024, 64, 3)
+
+
 def test_qmatmul_rejects_bad_shapes(ctx):
     x = ctx.alloc(4096)
     with pytest.raises(emx.EmxError) as ei:
