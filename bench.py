@@ -181,11 +181,18 @@ def run_engine(args, cfg, rank, world, dist):
 
     torch.cuda.set_device(dev)
     ctx = emx.Ctx(dev)
-    m = emx.Qwen3(ctx, cfg)
-    m.init_random(args.seed)
     stream_ptr = emx.C.c_void_p()
     emx.lib().emx_ctx_stream(ctx.h, emx.C.byref(stream_ptr))
     st = torch.cuda.ExternalStream(stream_ptr.value, device=dev)
+    if args.kernel_only:
+        hbm, _, kind = peaks()
+        if rank == 0:
+            print(json.dumps(dict(gemv_kernel_roofline(ctx, st, cfg, torch, hbm), peak_kind=kind)), flush=True)
+        ctx.close()
+        return
+    m = emx.Qwen3(ctx, cfg)
+    m.init_random(args.seed)
+    m.compiled = not args.eager
 
     def barrier():
         if dist is not None:
@@ -270,10 +277,11 @@ def run_engine(args, cfg, rank, world, dist):
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16 activations, int4/int8 affine weights",
             "data": "synthetic (seeded random-init weights and token ids)", "config": workload(args, cfg),
             "prefill_tok_s": pre, "decode_context": [start_ctx, start_ctx + args.steps],
-            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                         "traffic": None, "peak_kind": kind, "scope": "whole decode step",
-                         "bytes_per_step": step_bytes},
-            "kernel_roofline": kern,
+            "roofline": dict(kern, peak_kind=kind),
+            "step_roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                              "frac": achieved / hbm, "traffic": None, "peak_kind": kind,
+                              "scope": "whole decode step (weights + scales/biases + KV read per token)",
+                              "bytes_per_step": step_bytes},
             "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4,
                     "api": "emx_qwen3_decode_step", "steps": n_e2e},
             "gpu_launches": launches * args.steps, "launches_per_step": launches,
@@ -288,8 +296,12 @@ def run_engine(args, cfg, rank, world, dist):
 
 
 def gemv_kernel_roofline(ctx, st, cfg, torch, hbm):
-    """qgemv on the gate_up shape [2*inter, hidden] (int4 gs64) alone: 16 weight
-    copies (> L2) rotated over 160 launches, CUDA events on the ctx stream."""
+    """The dominant kernel of the decode step, pgemv_kernel (the packed batch-1
+    GEMV: ~80% of the step), alone on the step's most expensive shape, the
+    fused gate|up projection [2*inter, hidden]: 16 packed copies (> L2)
+    rotated over 160 launches, CUDA events on the context's stream.
+    Algorithmic bytes per launch: packed codes + bf16 scales and biases + x in
+    + y out."""
     import numpy as np
 
     import emx
@@ -298,33 +310,32 @@ def gemv_kernel_roofline(ctx, st, cfg, torch, hbm):
     bits, gs = cfg.mlp_bits, cfg.mlp_group
     copies = 16
     wsz, ssz = N * K * bits // 8, N * (K // gs) * 2
-    w = [ctx.alloc(wsz) for _ in range(copies)]
-    s = [ctx.alloc(ssz) for _ in range(copies)]
-    b = [ctx.alloc(ssz) for _ in range(copies)]
-    for i in range(copies):
-        emx.lib().emx_memset(ctx.h, w[i].ptr, 0x5A, wsz)
-        emx.lib().emx_memset(ctx.h, s[i].ptr, 0x3C, ssz)
-        emx.lib().emx_memset(ctx.h, b[i].ptr, 0x00, ssz)
+    w, s, b = ctx.alloc(wsz), ctx.alloc(ssz), ctx.alloc(ssz)
+    emx.lib().emx_memset(ctx.h, w.ptr, 0x5A, wsz)
+    emx.lib().emx_memset(ctx.h, s.ptr, 0x3C, ssz)
+    emx.lib().emx_memset(ctx.h, b.ptr, 0x00, ssz)
+    pk = [ctx.qpack(w, s, b, N, K, gs, bits) for _ in range(copies)]
     x = ctx.put(np.full(K, 0x3F80, np.uint16))
     y = ctx.alloc(N * 2)
+    L = emx.lib()
     for i in range(8):
-        ctx.quantized_matmul(x, w[i % copies], s[i % copies], b[i % copies], 1, N, K, gs, bits, out=y)
+        L.emx_quantized_matvec_packed(ctx.h, x.ptr, pk[i % copies].ptr, y.ptr, N, K, gs, bits)
     ctx.synchronize()
     n = 160
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(st)
     for i in range(n):
-        ctx.quantized_matmul(x, w[i % copies], s[i % copies], b[i % copies], 1, N, K, gs, bits, out=y)
+        L.emx_quantized_matvec_packed(ctx.h, x.ptr, pk[i % copies].ptr, y.ptr, N, K, gs, bits)
     e1.record(st)
     e1.synchronize()
     us = e0.elapsed_time(e1) * 1000.0 / n
     per = qbytes(N, K, bits, gs) + K * 2 + N * 2
-    for a in w + s + b + [x, y]:
+    for a in pk + [w, s, b, x, y]:
         a.free()
     ach = per / (us * 1e-6) / 1e9
-    return {"kernel": "qgemv_kernel<4,64> (gate_up shape, standalone, no PDL overlap)", "shape": [N, K],
-            "bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s", "frac": ach / hbm, "us_per_launch": us,
-            "bytes_per_launch": per, "traffic": None}
+    return {"kernel": f"pgemv_kernel<{bits},{gs}> (gate|up shape, standalone: no PDL overlap with a neighbour)",
+            "shape": [N, K], "bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s", "frac": ach / hbm,
+            "us_per_launch": us, "bytes_per_launch": per, "traffic": None}
 
 
 def main():
@@ -339,6 +350,10 @@ def main():
     ap.add_argument("--seed", type=int, default=1234)
     ap.add_argument("--cpu-steps", type=int, default=4)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--eager", action="store_true",
+                    help="decode without the CUDA graph (kernels in plain stream order): for profilers")
+    ap.add_argument("--kernel-only", action="store_true",
+                    help="time only the dominant kernel (packed GEMV, gate|up shape) and print its roofline")
     args = ap.parse_args()
 
     import emx

@@ -45,6 +45,7 @@ struct PGeom {
   int x_slots, xk;
   int red_rows;
   int nw_bytes;  // room for the norm weights (fetched before the wait)
+  unsigned long long lbt_magic;  // ceil(2^32 / (halves * S)): tile -> logical block
   int off_x, off_nw, off_zero, off_xs, off_red, off_buf;
 };
 
@@ -91,14 +92,16 @@ __device__ __forceinline__ void unpack8f(uint4 v, float (&f)[8]) {
   }
 }
 
-__device__ __forceinline__ uint4 pack8f(const float (&f)[8]) {
+// Eight floats that are bf16 values already (no rounding needed).
+__device__ __forceinline__ uint4 pack8exact(const float (&f)[8]) {
   uint4 r;
-  r.x = (uint32_t)f2bits(f[0]) | ((uint32_t)f2bits(f[1]) << 16);
-  r.y = (uint32_t)f2bits(f[2]) | ((uint32_t)f2bits(f[3]) << 16);
-  r.z = (uint32_t)f2bits(f[4]) | ((uint32_t)f2bits(f[5]) << 16);
-  r.w = (uint32_t)f2bits(f[6]) | ((uint32_t)f2bits(f[7]) << 16);
+  r.x = (__float_as_uint(f[0]) >> 16) | (__float_as_uint(f[1]) & 0xffff0000u);
+  r.y = (__float_as_uint(f[2]) >> 16) | (__float_as_uint(f[3]) & 0xffff0000u);
+  r.z = (__float_as_uint(f[4]) >> 16) | (__float_as_uint(f[5]) & 0xffff0000u);
+  r.w = (__float_as_uint(f[6]) >> 16) | (__float_as_uint(f[7]) & 0xffff0000u);
   return r;
 }
+
 
 // The pre-norm source values of elements [8c, 8c+8) (bf16 values as float).
 __device__ __forceinline__ void src8(const GemvArgs& a, int c, int tok, float (&v)[8]) {
@@ -275,10 +278,10 @@ __global__ void __launch_bounds__(kThreads, 2) pgemv_kernel(const GemvArgs a, co
   {
     const int K = geo.K;
     const int nch = K / 8;
-    auto emit = [&](int slot, int c, bool valid, const float (&o)[8]) {
+    auto emit_raw = [&](int slot, int c, bool valid, uint4 raw, const float (&o)[8]) {
       float ps = 0.f;
       if (valid) {
-        *reinterpret_cast<uint4*>(xsm + (size_t)slot * geo.xk + c * 8) = pack8f(o);
+        *reinterpret_cast<uint4*>(xsm + (size_t)slot * geo.xk + c * 8) = raw;
 #pragma unroll
         for (int e = 0; e < 8; ++e) ps += o[e];
       }
@@ -286,18 +289,21 @@ __global__ void __launch_bounds__(kThreads, 2) pgemv_kernel(const GemvArgs a, co
       for (int off = 1; off < CPG; off <<= 1) ps += __shfl_xor_sync(0xffffffffu, ps, off);
       if (valid && (c % CPG) == 0) xs[slot * S * 8 + c / CPG] = ps;
     };
+    // o holds bf16 values (the norm output is rounded per element)
+    auto emit = [&](int slot, int c, bool valid, const float (&o)[8]) {
+      emit_raw(slot, c, valid, valid ? pack8exact(o) : make_uint4(0u, 0u, 0u, 0u), o);
+    };
     if (a.pro == kProX) {
       for (int slot = 0; slot < geo.x_slots; ++slot) {
 #pragma unroll 1
         for (int it = 0; it * kThreads < nch; ++it) {
           const int c = it * kThreads + tid;
           const bool valid = c < nch;
+          const uint4 raw = valid ? *reinterpret_cast<const uint4*>(a.x + (size_t)slot * K + c * 8)
+                                  : make_uint4(0u, 0u, 0u, 0u);
           float v[8];
-          if (valid) unpack8f(*reinterpret_cast<const uint4*>(a.x + (size_t)slot * K + c * 8), v);
-          else
-#pragma unroll
-            for (int e = 0; e < 8; ++e) v[e] = 0.f;
-          emit(slot, c, valid, v);
+          unpack8f(raw, v);
+          emit_raw(slot, c, valid, raw, v);
         }
       }
     } else {
@@ -320,7 +326,7 @@ __global__ void __launch_bounds__(kThreads, 2) pgemv_kernel(const GemvArgs a, co
 #pragma unroll
         for (int gi = 0; gi < 8; ++gi)
           if (grp == gi) ssg[gi] += ss;
-        const uint4 pk = pack8f(v);
+        const uint4 pk = pack8exact(v);
         *reinterpret_cast<uint4*>(xsm + c * 8) = pk;
         if (store) *reinterpret_cast<uint4*>(a.x_out + c * 8) = pk;
       }
@@ -380,9 +386,9 @@ __global__ void __launch_bounds__(kThreads, 2) pgemv_kernel(const GemvArgs a, co
     constexpr float C = BITS == 4 ? 128.0f : 2176.0f;
     // tile -> (logical block, half, span) by a 64-bit multiply, not a
     // division: floor(n / d) == (n * ceil(2^32 / d)) >> 32 for n < 2^32 / d
-    // (the magic is 2^32 itself for d == 1, hence 64 bits)
-    const unsigned long long lbt_magic = (0x100000000ull + lb_tiles - 1) / lb_tiles;
-    const unsigned long long lps_magic = (0x100000000ull + lps - 1) / lps;
+    // (the magic is 2^32 itself for d == 1, hence 64 bits; the host computes
+    // it, a 64-bit division here would cost the critical path ~0.5 us)
+    const unsigned long long lbt_magic = geo.lbt_magic;
     for (int st = 0; st < nst; ++st) {
       const int buf = st % geo.nbuf;
       const int a0 = T0 + st * geo.stage_tiles, a1 = min(T1, a0 + geo.stage_tiles);
@@ -397,7 +403,7 @@ __global__ void __launch_bounds__(kThreads, 2) pgemv_kernel(const GemvArgs a, co
           const int h = rem >= S ? 1 : 0;
           const int sp = rem - h * S;
           const unsigned char* tile = sbase + (size_t)ti * geo.tile_bytes;
-          const int xsl = geo.x_slots > 1 ? (int)(((unsigned long long)lb * lps_magic) >> 32) : 0;
+          const int xsl = geo.x_slots > 1 ? lb / lps : 0;
           const bf16* xv = xsm + (size_t)xsl * geo.xk + sp * SPAN_K + (hs * 4 + t) * GS;
           const unsigned char* pbx = has_x ? reinterpret_cast<const unsigned char*>(xv) : zero;
           const unsigned char* aw = tile + hs * (A_BYTES / 2) + lane * 16;
@@ -675,6 +681,8 @@ void make_pgeom(int N, int K, int bits, int gs, int epi, const PgemvPlan& p, PGe
   g->xk = g->S * 8 * gs;
   g->red_rows = p.lbs_max * g->halves * 16;
   g->nw_bytes = (p.x_slots == 1 && K <= 8192) ? ((K * 2 + 15) & ~15) : 0;
+  const unsigned long long lbt = (unsigned long long)g->halves * g->S;
+  g->lbt_magic = (0x100000000ull + lbt - 1) / lbt;
   (void)N;
   pgeom_layout(*g, gs);
 }
@@ -707,7 +715,8 @@ cudaError_t pgemv_pack(const uint32_t* w, const bf16* s, const bf16* b, int N, i
   return cudaGetLastError();
 }
 
-int pgemv_make_plan(int N, int K, int bits, int gs, int epi, int x_slots, int num_sms, int budget, PgemvPlan* plan) {
+int pgemv_make_plan(int N, int K, int bits, int gs, int epi, int x_slots, int num_sms, int budget, PgemvPlan* plan,
+                    int ctas_per_sm) {
   if (!(bits == 4 || bits == 8) || !(gs == 32 || gs == 64 || gs == 128)) return -1;
   if (K <= 0 || N <= 0 || K % gs != 0) return -1;
   const bool sw = epi == kEpiSwiglu;
@@ -720,7 +729,7 @@ int pgemv_make_plan(int N, int K, int bits, int gs, int epi, int x_slots, int nu
   p.halves = halves;
   p.lb_total = LB;
   p.x_slots = x_slots > 1 ? x_slots : 1;
-  p.grid = std::max(1, std::min(LB, num_sms));
+  p.grid = std::max(1, std::min(LB, num_sms * std::max(1, ctas_per_sm)));
   p.lbs_max = (LB + p.grid - 1) / p.grid;
   const int S = (K / gs + 7) / 8;
   const int tb = ptile_bytes(bits, gs);

@@ -56,8 +56,11 @@ struct PgemvPlan {
 };
 
 // N = physical rows of one launch (2x logical rows for SwiGLU); `budget` is
-// the dynamic shared memory the plan may use.  Returns 0 or -1 (unsupported).
-int pgemv_make_plan(int N, int K, int bits, int gs, int epi, int x_slots, int num_sms, int budget, PgemvPlan* plan);
+// the dynamic shared memory the plan may use; `ctas_per_sm` > 1 spreads a
+// streamed matrix over more CTAs (more warps hiding the dequant latency).
+// Returns 0 or -1 (unsupported).
+int pgemv_make_plan(int N, int K, int bits, int gs, int epi, int x_slots, int num_sms, int budget, PgemvPlan* plan,
+                    int ctas_per_sm = 1);
 
 // One GEMV; a.w must point at the packed matrix (a.s / a.b unused).
 cudaError_t pgemv_launch(const GemvArgs& a, const PgemvPlan& p, cudaStream_t st, bool pdl);

@@ -96,6 +96,7 @@ struct emx_qwen3 {
   float* inv_freq = nullptr;
   PgemvPlan p_lm{};
   bool packed_ok = false;  // packed copies match the loaded weights
+  bool compiled = true;    // decode through the captured graph (PDL chain) or eagerly
   bf16* kv = nullptr;
   size_t kv_layer = 0;  // elements of one layer's K (or V)
   std::map<std::string, Spec> specs;
@@ -235,14 +236,13 @@ GemvArgs gemv_base(const emx_qwen3* m, const QW& q) {
 
 // Shared memory a decode GEMV may claim: two CTAs per SM, so that the next
 // kernel of the step is resident (and streaming its weights) while this one
-// computes.  The lm_head, last in the step, may take more for a deeper ring.
+// computes.  The lm_head streams far more than it can hold and its dequant
+// is the longest compute of the step: it runs two CTAs per SM.
 constexpr int kGemvBudget = 110 * 1024;
-constexpr int kGemvBudgetLast = 160 * 1024;
 
-int plan(emx_qwen3* m, const QW& q, int epi, int x_slots, int n_rows_override, PgemvPlan* p,
-         int budget = kGemvBudget) {
+int plan(emx_qwen3* m, const QW& q, int epi, int x_slots, int n_rows_override, PgemvPlan* p, int ctas_per_sm = 1) {
   const int N = n_rows_override > 0 ? n_rows_override : q.N;
-  if (pgemv_make_plan(N, q.K, q.bits, q.gs, epi, x_slots, m->ctx->num_sms, budget, p))
+  if (pgemv_make_plan(N, q.K, q.bits, q.gs, epi, x_slots, m->ctx->num_sms, kGemvBudget, p, ctas_per_sm))
     return fail(EMX_ERR_INVALID, "no GEMV plan for N=%d K=%d bits=%d group=%d", N, q.K, q.bits, q.gs);
   return EMX_OK;
 }
@@ -366,7 +366,7 @@ int build(emx_qwen3* m) {
       if ((rc = plan(m, lw.e_down, kEpiStore, c.top_k, c.top_k * H, &lw.p_edown))) return rc;
     }
   }
-  if ((rc = plan(m, c.tied ? m->embed : m->lm, kEpiArgmax, 1, 0, &m->p_lm, kGemvBudgetLast))) return rc;
+  if ((rc = plan(m, c.tied ? m->embed : m->lm, kEpiArgmax, 1, 0, &m->p_lm, 2))) return rc;
   // rope table, KV cache, decode state
   if ((rc = alloc_t(m, hd / 2, &m->inv_freq))) return rc;
   if (k_rope_inv_freq(m->inv_freq, hd, c.rope_theta, m->ctx->stream) != cudaSuccess)
@@ -423,6 +423,7 @@ int launch_gemv(emx_qwen3* m, const GemvArgs& a, const PgemvPlan& p, bool pdl) {
 int enqueue_step(emx_qwen3* m) {
   const emx_qwen3_config& c = m->c;
   cudaStream_t st = m->ctx->stream;
+  const bool pdl = m->compiled;  // the eager step is plain stream order
   m->step_launches = 0;
   bf16* cur = m->xa;
   bf16* nxt = m->xb;
@@ -468,7 +469,7 @@ int enqueue_step(emx_qwen3* m) {
       a.norm_w = lw.in_norm;
       a.epi = kEpiStore;
       a.y = m->qkvb;
-      if ((rc = launch_gemv(m, a, lw.p_qkv, m->step_launches > 0))) return rc;
+      if ((rc = launch_gemv(m, a, lw.p_qkv, pdl && m->step_launches > 0))) return rc;
       if (pending_add) {
         std::swap(cur, nxt);
         pending_add = false;
@@ -495,7 +496,7 @@ int enqueue_step(emx_qwen3* m) {
       a.ticket = m->attn_ticket;
       a.splits = m->attn_splits;
       a.status = m->ctx->status;
-      cudaError_t e = attn_decode_launch(a, st, true);
+      cudaError_t e = attn_decode_launch(a, st, pdl);
       if (e != cudaSuccess) return fail_cuda(e, "attention launch");
       ++m->step_launches;
     }
@@ -512,7 +513,7 @@ int enqueue_step(emx_qwen3* m) {
         a.res = cur;
         a.y = cur;
       }
-      if ((rc = launch_gemv(m, a, lw.p_o, true))) return rc;
+      if ((rc = launch_gemv(m, a, lw.p_o, pdl))) return rc;
       if (m->tp) {
         if ((rc = comm_all_reduce(m->comm, m->part, (size_t)m->H, EMX_F32, st))) return rc;
         pending_add = true;
@@ -528,7 +529,7 @@ int enqueue_step(emx_qwen3* m) {
       a.norm_w = lw.post_norm;
       a.epi = kEpiSwiglu;
       a.y = m->hb;
-      if ((rc = launch_gemv(m, a, lw.p_gu, true))) return rc;
+      if ((rc = launch_gemv(m, a, lw.p_gu, pdl))) return rc;
       if (pending_add) {
         std::swap(cur, nxt);
         pending_add = false;
@@ -544,7 +545,7 @@ int enqueue_step(emx_qwen3* m) {
         d.res = cur;
         d.y = cur;
       }
-      if ((rc = launch_gemv(m, d, lw.p_down, true))) return rc;
+      if ((rc = launch_gemv(m, d, lw.p_down, pdl))) return rc;
       if (m->tp) {
         if ((rc = comm_all_reduce(m->comm, m->part, (size_t)m->H, EMX_F32, st))) return rc;
         pending_add = true;
@@ -557,9 +558,9 @@ int enqueue_step(emx_qwen3* m) {
       ra.norm_w = lw.post_norm;
       ra.epi = kEpiStore;
       ra.y = m->router_logits;
-      if ((rc = launch_gemv(m, ra, lw.p_router, true))) return rc;
+      if ((rc = launch_gemv(m, ra, lw.p_router, pdl))) return rc;
       cudaError_t e = k_moe_route(m->router_logits, c.n_experts, c.top_k, c.norm_topk, m->e_base, m->E_l,
-                                  m->moe_idx, m->moe_w, m->moe_n, st, true);
+                                  m->moe_idx, m->moe_w, m->moe_n, st, pdl);
       if (e != cudaSuccess) return fail_cuda(e, "moe route");
       ++m->step_launches;
       GemvArgs ga = gemv_base(m, lw.e_gu);
@@ -572,7 +573,7 @@ int enqueue_step(emx_qwen3* m) {
       ga.slot_expert = m->moe_idx;
       ga.n_slots = m->moe_n;
       ga.slot_rows = m->Im;
-      if ((rc = launch_gemv(m, ga, lw.p_egu, true))) return rc;
+      if ((rc = launch_gemv(m, ga, lw.p_egu, pdl))) return rc;
       GemvArgs da = gemv_base(m, lw.e_down);
       da.N = c.top_k * m->H;
       da.pro = kProX;
@@ -583,9 +584,9 @@ int enqueue_step(emx_qwen3* m) {
       da.slot_expert = m->moe_idx;
       da.n_slots = m->moe_n;
       da.slot_rows = m->H;
-      if ((rc = launch_gemv(m, da, lw.p_edown, true))) return rc;
+      if ((rc = launch_gemv(m, da, lw.p_edown, pdl))) return rc;
       if (m->ep) {
-        e = k_moe_combine(m->moe_y, m->moe_w, m->moe_n, m->H, m->part, st, true);
+        e = k_moe_combine(m->moe_y, m->moe_w, m->moe_n, m->H, m->part, st, pdl);
         if (e != cudaSuccess) return fail_cuda(e, "moe combine");
         ++m->step_launches;
         if ((rc = comm_all_reduce(m->comm, m->part, (size_t)m->H, EMX_F32, st))) return rc;
@@ -614,7 +615,7 @@ int enqueue_step(emx_qwen3* m) {
     a.hist_cap = c.kv_cap;
     a.pos = m->pos;
     a.pos_inc = 1;
-    if ((rc = launch_gemv(m, a, m->p_lm, true))) return rc;
+    if ((rc = launch_gemv(m, a, m->p_lm, pdl))) return rc;
   }
   return EMX_OK;
 }
@@ -643,6 +644,12 @@ int ensure_graph(emx_qwen3* m) {
 int run_steps(emx_qwen3* m, int n) {
   int rc = ensure_packed(m);
   if (rc) return rc;
+  if (!m->compiled) {  // eager: the same kernels, launched one by one
+    for (int i = 0; i < n; ++i)
+      if ((rc = enqueue_step(m))) return rc;
+    m->offset += n;
+    return EMX_OK;
+  }
   rc = ensure_graph(m);
   if (rc) return rc;
   for (int i = 0; i < n; ++i) EMX_CHECK_CUDA(cudaGraphLaunch(m->gexec, m->ctx->stream), "graph launch");
@@ -1034,6 +1041,18 @@ int emx_qwen3_decode_device(emx_qwen3* m, int n) {
   if (m->offset + n > m->c.kv_cap)
     return fail(EMX_ERR_STATE, "static KV overflow offset=%d + n=%d > cap=%d", m->offset, n, m->c.kv_cap);
   return run_steps(m, n);
+}
+
+int emx_qwen3_set_compiled(emx_qwen3* m, int compiled) {
+  Q_REQUIRE(m, "emx_qwen3_set_compiled: null model");
+  m->compiled = compiled != 0;
+  return EMX_OK;
+}
+
+int emx_qwen3_is_compiled(emx_qwen3* m, int* compiled) {
+  Q_REQUIRE(m && compiled, "emx_qwen3_is_compiled: null argument");
+  *compiled = m->compiled ? 1 : 0;
+  return EMX_OK;
 }
 
 int emx_qwen3_step_launches(emx_qwen3* m, int* n) {

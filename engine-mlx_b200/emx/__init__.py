@@ -92,6 +92,8 @@ _SIGS = {
     "emx_qwen3_load_tensor": (C.c_int, [C.c_void_p, C.c_char_p, C.c_void_p, C.c_size_t]),
     "emx_qwen3_read_tensor": (C.c_int, [C.c_void_p, C.c_char_p, C.c_void_p, C.c_size_t]),
     "emx_qwen3_read_kv": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_size_t]),
+    "emx_qwen3_set_compiled": (C.c_int, [C.c_void_p, C.c_int]),
+    "emx_qwen3_is_compiled": (C.c_int, [C.c_void_p, C.POINTER(C.c_int)]),
     "emx_qwen3_init_random": (C.c_int, [C.c_void_p, C.c_uint64]),
     "emx_qwen3_reset": (C.c_int, [C.c_void_p]),
     "emx_qwen3_offset": (C.c_int, [C.c_void_p, C.POINTER(C.c_int)]),
@@ -504,6 +506,17 @@ class Qwen3:
         out = np.empty((nkv, c.kv_cap, c.head_dim), dtype=np.uint16)
         _check(lib().emx_qwen3_read_kv(self.h, layer, which, out.ctypes.data, out.nbytes))
         return out
+
+    @property
+    def compiled(self) -> bool:
+        """Decode through the captured CUDA graph (True) or eagerly (False)."""
+        v = C.c_int()
+        _check(lib().emx_qwen3_is_compiled(self.h, C.byref(v)))
+        return bool(v.value)
+
+    @compiled.setter
+    def compiled(self, on: bool):
+        _check(lib().emx_qwen3_set_compiled(self.h, int(bool(on))))
 
     def init_random(self, seed: int):
         _check(lib().emx_qwen3_init_random(self.h, C.c_uint64(seed)))

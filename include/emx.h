@@ -241,6 +241,14 @@ int emx_qwen3_decode(emx_qwen3* m, int32_t token, int n, int32_t* tokens_out);
 int emx_qwen3_prefill_device(emx_qwen3* m, const int32_t* tokens_dev, int T);
 int emx_qwen3_decode_device(emx_qwen3* m, int n);
 /* Number of kernel launches one decode step enqueues. */
+/* Qwen3Engine::is_compiled (crates/serve/src/engine_ext.rs:212-216) and the
+ * choice between the compiled decode closure (decode_compiled.rs:113-120)
+ * and the eager per-op step: compiled (default) replays one captured CUDA
+ * graph per token with programmatically chained kernels; eager launches the
+ * same kernels one by one in plain stream order (for profilers and
+ * debugging). */
+int emx_qwen3_set_compiled(emx_qwen3* m, int compiled);
+int emx_qwen3_is_compiled(emx_qwen3* m, int* compiled);
 int emx_qwen3_step_launches(emx_qwen3* m, int* n);
 
 #if defined(__GNUC__)

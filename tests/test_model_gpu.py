@@ -200,6 +200,11 @@ def test_greedy_decode_paths_agree(ctx):
         steps.append(t)
     assert list(many) == steps
     assert m.step_launches() == 5 * cfg.layers + 1
+    # the eager step (no graph, no programmatic launch) is the same computation
+    m.compiled = False
+    m.reset()
+    assert m.prefill(prompt) == first and list(m.decode(first, 16)) == list(many)
+    m.compiled = True
     m.close()
     # the GPU's greedy chain, replayed through the oracle token by token
     chain = [first] + [int(t) for t in many]
