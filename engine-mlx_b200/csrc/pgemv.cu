@@ -17,7 +17,9 @@
 // (magic-number exponent, exact) and an m16n8k16 MMA per slice adds the
 // four group dot products of rows g, g+8 at once: column j < 4 of B holds x
 // masked to group j, so only the lanes with g == t load x (two adjacent
-// registers per slice from one 8-byte run) and the rest read a zero block.
+// registers per slice from one 8-byte run, a predicated load) and the other
+// lanes keep zero registers; x groups sit 2*gs + 16 bytes apart, so the four
+// loading lanes hit four different bank groups.
 // Then per row s*dot + (b - C*s)*sum(x_g) in fp32 — the MLX qmv
 // factorisation, C being the magic offset — reduced over the lane pair and
 // stored to a per-(row, span, half-span) slot.  After the last stage one
@@ -42,11 +44,14 @@ struct PGeom {
   int lb_total;
   int stage_tiles, nbuf;
   int stage_bytes;
-  int x_slots, xk;
+  int x_slots, xk;  // x elements per slot (whole spans)
+  int gstride;      // bytes per x group in shared memory (2*gs + 16: banks rotate per group)
+  int xslot_bytes;  // bytes per x slot
   int red_rows;
   int nw_bytes;  // room for the norm weights (fetched before the wait)
   unsigned long long lbt_magic;  // ceil(2^32 / (halves * S)): tile -> logical block
-  int off_x, off_nw, off_zero, off_xs, off_red, off_buf;
+  unsigned long long lps_magic;  // ceil(2^32 / (slot rows / 16)): logical block -> x slot
+  int off_x, off_nw, off_xs, off_red, off_buf;
 };
 
 __host__ __device__ inline int ptile_bytes(int bits, int gs) { return 16 * 8 * gs * bits / 8 + 512; }
@@ -55,9 +60,8 @@ __host__ __device__ inline int ptile_bytes(int bits, int gs) { return 16 * 8 * g
 // per-group 1/rms, the abort flag and the norm-weight mbarrier).
 __host__ __device__ inline int pgeom_layout(PGeom& g, int gs) {
   g.off_x = 384;
-  g.off_nw = g.off_x + ((g.x_slots * g.xk * 2 + 15) & ~15);
-  g.off_zero = g.off_nw + g.nw_bytes;
-  g.off_xs = g.off_zero + 2 * gs;
+  g.off_nw = g.off_x + g.x_slots * g.xslot_bytes;
+  g.off_xs = g.off_nw + g.nw_bytes;
   g.off_red = g.off_xs + ((g.x_slots * g.S * 8 * 4 + 15) & ~15);
   g.off_buf = (g.off_red + g.red_rows * g.S * 2 * 4 + 127) & ~127;
   return g.off_buf + g.nbuf * g.stage_bytes;
@@ -65,6 +69,17 @@ __host__ __device__ inline int pgeom_layout(PGeom& g, int gs) {
 
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// 128-bit shared load executed only where `p` holds; elsewhere v keeps its
+// value and the lane makes no shared-memory request.
+__device__ __forceinline__ void lds128_if(bool p, uint4& v, const void* addr) {
+  asm volatile(
+      "{\n\t.reg .pred q;\n\tsetp.ne.u32 q, %4, 0;\n\t"
+      "@q ld.shared.v4.u32 {%0,%1,%2,%3}, [%5];\n\t}"
+      : "+r"(v.x), "+r"(v.y), "+r"(v.z), "+r"(v.w)
+      : "r"((uint32_t)p), "r"(smem_u32(addr))
+      : "memory");
 }
 
 // Bounded wait that also gives up at once when another warp has aborted.
@@ -158,9 +173,8 @@ __global__ void __launch_bounds__(kThreads, 2) pgemv_kernel(const GemvArgs a, co
   float* inv = scratch + 32;                             // 8 floats
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + 320);
   uint64_t* nwbar = reinterpret_cast<uint64_t*>(smem + 336);
-  bf16* xsm = reinterpret_cast<bf16*>(smem + geo.off_x);
+  unsigned char* xsm = smem + geo.off_x;  // x: [slot][group][gs bf16 + 16 pad bytes]
   const bf16* nwsm = reinterpret_cast<const bf16*>(smem + geo.off_nw);
-  const unsigned char* zero = smem + geo.off_zero;
   float* xs = reinterpret_cast<float*>(smem + geo.off_xs);
   float* red = reinterpret_cast<float*>(smem + geo.off_red);
   unsigned char* bufs = smem + geo.off_buf;
@@ -170,6 +184,10 @@ __global__ void __launch_bounds__(kThreads, 2) pgemv_kernel(const GemvArgs a, co
   constexpr int HW = BITS / 4;  // word sets per quad
   constexpr int A_BYTES = 16 * SPAN_K * BITS / 8;
   constexpr int CPG = GS / 8;   // 8-element chunks per group
+  // byte offset of 8-element chunk c of x slot `slot`
+  auto xchunk = [&](int slot, int c) -> unsigned char* {
+    return xsm + (size_t)slot * geo.xslot_bytes + (c / CPG) * geo.gstride + (c % CPG) * 16;
+  };
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const bool gather = a.slot_expert != nullptr;
@@ -273,15 +291,15 @@ __global__ void __launch_bounds__(kThreads, 2) pgemv_kernel(const GemvArgs a, co
     }
   }
 
-  // ---- prologue: x (natural order, zero-padded to whole spans), the group
-  //      sums of x, and the zero block the non-x lanes read as B
+  // ---- prologue: x (padded groups, zero past K to whole spans) and the
+  //      group sums of x
   {
     const int K = geo.K;
     const int nch = K / 8;
     auto emit_raw = [&](int slot, int c, bool valid, uint4 raw, const float (&o)[8]) {
       float ps = 0.f;
       if (valid) {
-        *reinterpret_cast<uint4*>(xsm + (size_t)slot * geo.xk + c * 8) = raw;
+        *reinterpret_cast<uint4*>(xchunk(slot, c)) = raw;
 #pragma unroll
         for (int e = 0; e < 8; ++e) ps += o[e];
       }
@@ -327,7 +345,7 @@ __global__ void __launch_bounds__(kThreads, 2) pgemv_kernel(const GemvArgs a, co
         for (int gi = 0; gi < 8; ++gi)
           if (grp == gi) ssg[gi] += ss;
         const uint4 pk = pack8exact(v);
-        *reinterpret_cast<uint4*>(xsm + c * 8) = pk;
+        *reinterpret_cast<uint4*>(xchunk(0, c)) = pk;
         if (store) *reinterpret_cast<uint4*>(a.x_out + c * 8) = pk;
       }
       for (int gi = 0; gi < groups; ++gi) {
@@ -350,7 +368,7 @@ __global__ void __launch_bounds__(kThreads, 2) pgemv_kernel(const GemvArgs a, co
         float o[8];
         if (valid) {
           float v[8], w[8];
-          unpack8f(*reinterpret_cast<const uint4*>(xsm + c * 8), v);
+          unpack8f(*reinterpret_cast<const uint4*>(xchunk(0, c)), v);
           unpack8f(*reinterpret_cast<const uint4*>(nwsm + c * 8), w);
           const float iv = inv[(c * 8) / gd];
 #pragma unroll
@@ -364,13 +382,12 @@ __global__ void __launch_bounds__(kThreads, 2) pgemv_kernel(const GemvArgs a, co
         emit(0, c, valid, o);
       }
     }
-    // zero padding: x past K, group sums past ng, the zero block
-    const int pad = geo.xk - K;
+    // zero padding: x past K (whole chunks), group sums past ng
+    const int pad = (geo.xk - K) / 8;  // chunks
     for (int i = tid; i < geo.x_slots * pad; i += kThreads)
-      xsm[(size_t)(i / pad) * geo.xk + K + i % pad] = __float2bfloat16_rn(0.f);
+      *reinterpret_cast<uint4*>(xchunk(i / pad, nch + i % pad)) = make_uint4(0u, 0u, 0u, 0u);
     const int gpad = S * 8 - geo.ng;
     for (int i = tid; i < geo.x_slots * gpad; i += kThreads) xs[(i / gpad) * S * 8 + geo.ng + i % gpad] = 0.f;
-    for (int i = tid; i < GS / 2; i += kThreads) reinterpret_cast<uint32_t*>(smem + geo.off_zero)[i] = 0u;
   }
   __syncthreads();
 
@@ -380,6 +397,8 @@ __global__ void __launch_bounds__(kThreads, 2) pgemv_kernel(const GemvArgs a, co
   if (warp < kConsumers) {
     const int g = lane >> 2, t = lane & 3;
     const bool has_x = g == t;  // the lanes whose B column carries x
+    // B registers (two sets, alternate slice quads); zero for the other lanes
+    uint4 xa0 = make_uint4(0u, 0u, 0u, 0u), xa1 = xa0, xb0 = xa0, xb1 = xa0;
     const uint32_t MASK = 0x000F000Fu;
     const uint32_t MAGIC_LO = 0x43004300u;  // bf16 128 + nibble
     const uint32_t MAGIC_HI = 0x45004500u;  // bf16 2048 + 16 * nibble
@@ -403,9 +422,10 @@ __global__ void __launch_bounds__(kThreads, 2) pgemv_kernel(const GemvArgs a, co
           const int h = rem >= S ? 1 : 0;
           const int sp = rem - h * S;
           const unsigned char* tile = sbase + (size_t)ti * geo.tile_bytes;
-          const int xsl = geo.x_slots > 1 ? lb / lps : 0;
-          const bf16* xv = xsm + (size_t)xsl * geo.xk + sp * SPAN_K + (hs * 4 + t) * GS;
-          const unsigned char* pbx = has_x ? reinterpret_cast<const unsigned char*>(xv) : zero;
+          const int xsl = (int)(((unsigned long long)lb * geo.lps_magic) >> 32);  // 0 unless x_slots > 1
+          // only the lanes whose B column carries x read it (a predicated
+          // load: the other lanes' registers stay zero and cost no bandwidth)
+          const unsigned char* pbx = xsm + (size_t)xsl * geo.xslot_bytes + (size_t)(sp * 8 + hs * 4 + t) * geo.gstride;
           const unsigned char* aw = tile + hs * (A_BYTES / 2) + lane * 16;
           float d[4][4];
 #pragma unroll
@@ -415,8 +435,10 @@ __global__ void __launch_bounds__(kThreads, 2) pgemv_kernel(const GemvArgs a, co
             uint4 wa[HW];
 #pragma unroll
             for (int hw = 0; hw < HW; ++hw) wa[hw] = *reinterpret_cast<const uint4*>(aw + (q * HW + hw) * 512);
-            const uint4 X0 = *reinterpret_cast<const uint4*>(pbx + q * 32);
-            const uint4 X1 = *reinterpret_cast<const uint4*>(pbx + q * 32 + 16);
+            uint4& X0 = (q & 1) ? xb0 : xa0;
+            uint4& X1 = (q & 1) ? xb1 : xa1;
+            lds128_if(has_x, X0, pbx + q * 32);
+            lds128_if(has_x, X1, pbx + q * 32 + 16);
             const uint32_t bx[8] = {X0.x, X0.y, X0.z, X0.w, X1.x, X1.y, X1.z, X1.w};
             const uint32_t w0v[4] = {wa[0].x, wa[0].y, wa[0].z, wa[0].w};
             const uint32_t w1v[4] = {wa[HW - 1].x, wa[HW - 1].y, wa[HW - 1].z, wa[HW - 1].w};
@@ -679,10 +701,13 @@ void make_pgeom(int N, int K, int bits, int gs, int epi, const PgemvPlan& p, PGe
   g->stage_bytes = p.stage_tiles * g->tile_bytes;
   g->x_slots = p.x_slots;
   g->xk = g->S * 8 * gs;
+  g->gstride = 2 * gs + 16;
+  g->xslot_bytes = g->S * 8 * g->gstride;
   g->red_rows = p.lbs_max * g->halves * 16;
   g->nw_bytes = (p.x_slots == 1 && K <= 8192) ? ((K * 2 + 15) & ~15) : 0;
   const unsigned long long lbt = (unsigned long long)g->halves * g->S;
   g->lbt_magic = (0x100000000ull + lbt - 1) / lbt;
+  g->lps_magic = 0;
   (void)N;
   pgeom_layout(*g, gs);
 }
@@ -773,6 +798,11 @@ cudaError_t pgemv_launch(const GemvArgs& a, const PgemvPlan& p, cudaStream_t st,
   if (a.pro != kProX && p.x_slots > 1) return cudaErrorInvalidValue;
   PGeom g;
   make_pgeom(a.N, a.K, a.bits, a.gs, a.epi, p, &g);
+  if (p.x_slots > 1) {
+    if (a.slot_rows < 16 || a.slot_rows % 16 != 0) return cudaErrorInvalidValue;
+    const unsigned long long lps = (unsigned long long)(a.slot_rows / 16);
+    g.lps_magic = (0x100000000ull + lps - 1) / lps;
+  }
   if (a.pro != kProX && (g.nw_bytes < a.K * 2 || (reinterpret_cast<uintptr_t>(a.norm_w) & 15) != 0))
     return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};
