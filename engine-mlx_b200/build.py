@@ -68,7 +68,7 @@ def build(force=False, jobs=None, verbose=False):
         raise RuntimeError("nvcc failed:\n" + "\n".join(errors))
     if force or not os.path.exists(LIB) or os.path.getmtime(LIB) < max(os.path.getmtime(o) for o in objs):
         # visibility: only the extern "C" entry points (marked default below) are exported
-        cmd = [nvcc()] + ARCH + ["-shared", "-o", LIB] + objs + ["-lcublas", "-ldl", "-Xcompiler", "-fPIC"]
+        cmd = [nvcc()] + ARCH + ["-shared", "-o", LIB] + objs + ["-ldl", "-Xcompiler", "-fPIC"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError("link failed:\n" + r.stdout + r.stderr)

@@ -26,7 +26,7 @@ struct GemmArgs {
 struct GemmCtx;  // per-context scratch + library handles
 GemmCtx* gemm_ctx_create(size_t scratch_bytes);
 void gemm_ctx_destroy(GemmCtx* c);
-// Returns 0 on success, a cuda/cublas error code otherwise.
+// Returns 0 on success, a CUDA error code (or a negative shape error) otherwise.
 int gemm_run(GemmCtx* c, const GemmArgs& a, cudaStream_t st);
 
 }  // namespace emx
