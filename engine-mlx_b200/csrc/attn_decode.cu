@@ -57,9 +57,11 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const AttnDecodeA
   __shared__ float qn[HPG + 1][kHD];   // normed q heads (+ k) before rope
   __shared__ float sc[HPG][kTile];     // scores -> probabilities for one tile
   __shared__ float stat_m[HPG], stat_l[HPG], stat_a[HPG];
-  __shared__ float sacc[4][HPG][kHD];  // per-warp partial outputs
+  __shared__ __align__(16) float sacc[4][HPG][kHD];  // per-warp partial outputs (float4 stores)
   __shared__ float swt[HPG][64];       // merge weights of the splits
   __shared__ float nwq[kHD], nwk[kHD], invf[kHD / 2];
+  __shared__ float2 rcs[kHD / 2];  // (cos, sin) of this step's angles
+  __shared__ int rcs_pos;          // position rcs was loaded for (-1: none)
   __shared__ __align__(16) bf16 knew[kHD];  // the new row (owner split)
   __shared__ __align__(16) bf16 vnew[kHD];
   __shared__ int base_use[kNBuf];  // completed uses of each buffer before this plan
@@ -78,6 +80,7 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const AttnDecodeA
       base_use[i] = 0;
     }
     fence_mbar_init();
+    rcs_pos = -1;
   }
   // static inputs (weights, RoPE table) before the wait
   if (!a.q_in) {
@@ -107,6 +110,15 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const AttnDecodeA
   };
   auto parity = [&](int t) -> uint32_t { return (uint32_t)((base_use[t % kNBuf] + t / kNBuf) & 1); };
 
+  // this step's RoPE angles: every row of the table is final before the
+  // kernel starts, so fetch the row of the (pre-wait) position now
+  {
+    const int pg = a.pos ? *reinterpret_cast<const volatile int*>(a.pos) : a.pos_host;
+    if (!a.q_in && a.rope_cs && pg >= 0 && pg < a.cap) {
+      if (tid < kHD / 2) rcs[tid] = a.rope_cs[(size_t)pg * (kHD / 2) + tid];
+      if (tid == 0) rcs_pos = pg;
+    }
+  }
   int n_issued = 0;  // thread 0: tiles issued under the current plan
   if (tid == 0) {
     plan_p = -1;
@@ -152,6 +164,8 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const AttnDecodeA
     plan_p = p;
   }
   const bool owns_new = (p >= p0 && p < p1) && a.q_in == nullptr;
+  __syncthreads();  // rcs / rcs_pos visible
+  const bool have_rcs = rcs_pos == p;
 
   // ---- q heads (and k/v of the new row when owned): rms_norm + rope -------
   const int nhead_prep = a.q_in ? 0 : HPG + (owns_new ? 1 : 0);
@@ -187,9 +201,14 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const AttnDecodeA
     for (int e = 0; e < 4; ++e) {
       const int d = lane * 4 + e;
       const int i = d & (kHD / 2 - 1);
-      const float th = __fmul_rn(fp, invf[i]);
       float sn, cs;
-      sincosf(th, &sn, &cs);
+      if (have_rcs) {
+        const float2 t2 = rcs[i];
+        cs = t2.x;
+        sn = t2.y;
+      } else {
+        sincosf(__fmul_rn(fp, invf[i]), &sn, &cs);
+      }
       const float x1 = qn[hh][i], x2 = qn[hh][i + kHD / 2];
       float o;
       if (d < kHD / 2) o = __fsub_rn(__fmul_rn(x1, cs), __fmul_rn(x2, sn));
@@ -215,19 +234,18 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const AttnDecodeA
   }
   __syncthreads();
 
-  // per-lane q slice: 8 dims starting at dl, for every head of the group
-  const int half = lane >> 4, dl = (lane & 15) * 8;
-  float qreg[HPG][8];
+  // lane l owns dims [4l, 4l+4) of every head of the group
+  float qreg[HPG][4];
 #pragma unroll
   for (int h = 0; h < HPG; ++h)
 #pragma unroll
-    for (int e = 0; e < 8; ++e) qreg[h][e] = qs[h][dl + e];
+    for (int e = 0; e < 4; ++e) qreg[h][e] = qs[h][lane * 4 + e];
 
-  float acc[HPG][8];
+  float acc[HPG][4];
 #pragma unroll
   for (int h = 0; h < HPG; ++h)
 #pragma unroll
-    for (int e = 0; e < 8; ++e) acc[h][e] = 0.f;
+    for (int e = 0; e < 4; ++e) acc[h][e] = 0.f;
 
   for (int t = 0; t < ntile; ++t) {
     const int buf = t % kNBuf;
@@ -245,28 +263,63 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const AttnDecodeA
       }
       __syncthreads();
     }
-    // QK^T: two rows per warp step, 16 lanes x 8 dims per row
-    for (int jb = warp * 2; jb < tn; jb += 8) {
-      const int jj = jb + half;
-      const bool valid = jj < tn;
-      const uint4 kv = valid ? *reinterpret_cast<const uint4*>(kt + (size_t)jj * kHD + dl) : make_uint4(0u, 0u, 0u, 0u);
-      const uint32_t kw[4] = {kv.x, kv.y, kv.z, kv.w};
-      float kf[8];
+    // QK^T: warp w scores rows [16w, 16w + 16) in batches of eight.  Each
+    // lane forms its 4-dim partial of all eight rows, then a transpose-
+    // reduction (xor 16, 8, 4: halve the rows a lane keeps; xor 2, 1: plain
+    // sums) leaves row k's score in lanes 4k..4k+3 — 9 shuffles per head for
+    // eight rows.
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        kf[2 * e] = __uint_as_float(kw[e] << 16);
-        kf[2 * e + 1] = __uint_as_float(kw[e] & 0xffff0000u);
+    for (int bt = 0; bt < 2; ++bt) {
+      const int r0 = warp * 16 + bt * 8;
+      if (r0 >= tn) break;
+      float kf[8][4];
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        const uint2 kv = r0 + r < tn ? *reinterpret_cast<const uint2*>(kt + (size_t)(r0 + r) * kHD + lane * 4)
+                                     : make_uint2(0u, 0u);
+        kf[r][0] = __uint_as_float(kv.x << 16);
+        kf[r][1] = __uint_as_float(kv.x & 0xffff0000u);
+        kf[r][2] = __uint_as_float(kv.y << 16);
+        kf[r][3] = __uint_as_float(kv.y & 0xffff0000u);
       }
 #pragma unroll
       for (int h = 0; h < HPG; ++h) {
-        float s = 0.f;
+        float v[8];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) s = fmaf(qreg[h][e], kf[e], s);
-        s += __shfl_xor_sync(0xffffffffu, s, 8);
-        s += __shfl_xor_sync(0xffffffffu, s, 4);
-        s += __shfl_xor_sync(0xffffffffu, s, 2);
-        s += __shfl_xor_sync(0xffffffffu, s, 1);
-        if (valid && (lane & 15) == 0) sc[h][jj] = s;
+        for (int r = 0; r < 8; ++r) {
+          float s2 = 0.f;
+#pragma unroll
+          for (int e = 0; e < 4; ++e) s2 = fmaf(qreg[h][e], kf[r][e], s2);
+          v[r] = s2;
+        }
+        // xor 16: lanes < 16 keep rows 0-3, the others rows 4-7
+        const bool up16 = (lane & 16) != 0;
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          const float send = up16 ? v[r] : v[r + 4];
+          const float keep = up16 ? v[r + 4] : v[r];
+          v[r] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+        }
+        // xor 8: keep 2 of the 4
+        const bool up8 = (lane & 8) != 0;
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+          const float send = up8 ? v[r] : v[r + 2];
+          const float keep = up8 ? v[r + 2] : v[r];
+          v[r] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+        }
+        // xor 4: keep 1 of the 2
+        const bool up4 = (lane & 4) != 0;
+        {
+          const float send = up4 ? v[0] : v[1];
+          const float keep = up4 ? v[1] : v[0];
+          v[0] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+        }
+        v[0] += __shfl_xor_sync(0xffffffffu, v[0], 2);
+        v[0] += __shfl_xor_sync(0xffffffffu, v[0], 1);
+        // lane 4k holds row k' where k' = 4*bit16 + 2*bit8 + bit4 of the lane
+        const int k = ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1);
+        if ((lane & 3) == 0 && r0 + k < tn) sc[h][r0 + k] = v[0];
       }
     }
     __syncthreads();
@@ -293,27 +346,23 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const AttnDecodeA
       }
     }
     __syncthreads();
-    // P.V: 8 row slots (4 warps x 2 halves), 8 dims per lane
+    // P.V: warp w accumulates rows [16w, 16w + 16) into its 4 dims per lane
 #pragma unroll
     for (int h = 0; h < HPG; ++h) {
       const float al = stat_a[h];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) acc[h][e] *= al;
+      for (int e = 0; e < 4; ++e) acc[h][e] *= al;
     }
-    for (int jj = warp * 2 + half; jj < tn; jj += 8) {
-      const uint4 vv = *reinterpret_cast<const uint4*>(vt + (size_t)jj * kHD + dl);
-      const uint32_t vw[4] = {vv.x, vv.y, vv.z, vv.w};
-      float vf[8];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        vf[2 * e] = __uint_as_float(vw[e] << 16);
-        vf[2 * e + 1] = __uint_as_float(vw[e] & 0xffff0000u);
-      }
+    const int rend = min(tn, warp * 16 + 16);
+    for (int jj = warp * 16; jj < rend; ++jj) {
+      const uint2 vv = *reinterpret_cast<const uint2*>(vt + (size_t)jj * kHD + lane * 4);
+      const float vf[4] = {__uint_as_float(vv.x << 16), __uint_as_float(vv.x & 0xffff0000u),
+                           __uint_as_float(vv.y << 16), __uint_as_float(vv.y & 0xffff0000u)};
 #pragma unroll
       for (int h = 0; h < HPG; ++h) {
         const float pr = sc[h][jj];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) acc[h][e] = fmaf(pr, vf[e], acc[h][e]);
+        for (int e = 0; e < 4; ++e) acc[h][e] = fmaf(pr, vf[e], acc[h][e]);
       }
     }
     __syncthreads();
@@ -324,17 +373,10 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const AttnDecodeA
     }
   }
 
-  // ---- merge the 8 row slots, publish this split's partial ---------------
+  // ---- the four warps' row slots, then this split's partial ---------------
 #pragma unroll
   for (int h = 0; h < HPG; ++h)
-#pragma unroll
-    for (int e = 0; e < 8; ++e) acc[h][e] += __shfl_xor_sync(0xffffffffu, acc[h][e], 16);
-  if (half == 0) {
-#pragma unroll
-    for (int h = 0; h < HPG; ++h)
-#pragma unroll
-      for (int e = 0; e < 8; ++e) sacc[warp][h][dl + e] = acc[h][e];
-  }
+    *reinterpret_cast<float4*>(&sacc[warp][h][lane * 4]) = make_float4(acc[h][0], acc[h][1], acc[h][2], acc[h][3]);
   __syncthreads();
   if (splits == 1) {
     // a single split needs no merge: normalise and store
@@ -412,7 +454,22 @@ cudaError_t launch_t(const AttnDecodeArgs& a, cudaStream_t st, bool pdl) {
   return cudaLaunchKernelEx(&cfg, kern, a);
 }
 
+__global__ void rope_table_kernel(float2* cs, const float* inv_freq, int cap, int half) {
+  const size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (i >= (size_t)cap * half) return;
+  const int p = (int)(i / half), k = (int)(i % half);
+  float sn, c;
+  sincosf(__fmul_rn((float)p, inv_freq[k]), &sn, &c);
+  cs[i] = make_float2(c, sn);
+}
+
 }  // namespace
+
+cudaError_t rope_table_fill(float2* cs, const float* inv_freq, int cap, int half, cudaStream_t st) {
+  const size_t n = (size_t)cap * half;
+  rope_table_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(cs, inv_freq, cap, half);
+  return cudaGetLastError();
+}
 
 int attn_decode_splits(int nkv, int num_sms) {
   int s = num_sms / (nkv > 0 ? nkv : 1);

@@ -10,6 +10,7 @@ struct AttnDecodeArgs {
   const bf16* k_norm;     // [head_dim] or nullptr
   float eps;
   const float* inv_freq;  // rope inverse frequencies [head_dim/2]
+  const float2* rope_cs;  // optional (cos, sin) table [cap][head_dim/2] of the same angles
   bf16* kc;               // this layer's K cache [nkv, cap, head_dim]
   bf16* vc;               // this layer's V cache
   int cap;
@@ -26,6 +27,9 @@ struct AttnDecodeArgs {
 };
 
 int attn_decode_splits(int nkv, int num_sms);
+// (cos, sin) of pos * inv_freq[i] for pos < cap, i < head_dim/2, with the
+// exact fp32 steps the decode kernel would take.
+cudaError_t rope_table_fill(float2* cs, const float* inv_freq, int cap, int half, cudaStream_t st);
 cudaError_t attn_decode_launch(const AttnDecodeArgs& a, cudaStream_t st, bool pdl);
 
 }  // namespace emx

@@ -17,9 +17,10 @@
 // (magic-number exponent, exact) and an m16n8k16 MMA per slice adds the
 // four group dot products of rows g, g+8 at once: column j < 4 of B holds x
 // masked to group j, so only the lanes with g == t load x (two adjacent
-// registers per slice from one 8-byte run, a predicated load) and the other
-// lanes keep zero registers; x groups sit 2*gs + 16 bytes apart, so the four
-// loading lanes hit four different bank groups.
+// registers per slice from one 8-byte run) and the other lanes read a zero
+// block; x groups sit 2*gs + 16 bytes apart, so the four loading lanes hit
+// four different bank groups.  Each warp runs two units at once, interleaved
+// quad by quad, so one unit's accumulator drain overlaps the other's math.
 // Then per row s*dot + (b - C*s)*sum(x_g) in fp32 — the MLX qmv
 // factorisation, C being the magic offset — reduced over the lane pair and
 // stored to a per-(row, span, half-span) slot.  After the last stage one
@@ -51,7 +52,7 @@ struct PGeom {
   int nw_bytes;  // room for the norm weights (fetched before the wait)
   unsigned long long lbt_magic;  // ceil(2^32 / (halves * S)): tile -> logical block
   unsigned long long lps_magic;  // ceil(2^32 / (slot rows / 16)): logical block -> x slot
-  int off_x, off_nw, off_xs, off_red, off_buf;
+  int off_x, off_nw, off_zero, off_xs, off_red, off_buf;
 };
 
 __host__ __device__ inline int ptile_bytes(int bits, int gs) { return 16 * 8 * gs * bits / 8 + 512; }
@@ -61,7 +62,8 @@ __host__ __device__ inline int ptile_bytes(int bits, int gs) { return 16 * 8 * g
 __host__ __device__ inline int pgeom_layout(PGeom& g, int gs) {
   g.off_x = 384;
   g.off_nw = g.off_x + g.x_slots * g.xslot_bytes;
-  g.off_xs = g.off_nw + g.nw_bytes;
+  g.off_zero = g.off_nw + g.nw_bytes;
+  g.off_xs = g.off_zero + 2 * gs;
   g.off_red = g.off_xs + ((g.x_slots * g.S * 8 * 4 + 15) & ~15);
   g.off_buf = (g.off_red + g.red_rows * g.S * 2 * 4 + 127) & ~127;
   return g.off_buf + g.nbuf * g.stage_bytes;
@@ -69,17 +71,6 @@ __host__ __device__ inline int pgeom_layout(PGeom& g, int gs) {
 
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-
-// 128-bit shared load executed only where `p` holds; elsewhere v keeps its
-// value and the lane makes no shared-memory request.
-__device__ __forceinline__ void lds128_if(bool p, uint4& v, const void* addr) {
-  asm volatile(
-      "{\n\t.reg .pred q;\n\tsetp.ne.u32 q, %4, 0;\n\t"
-      "@q ld.shared.v4.u32 {%0,%1,%2,%3}, [%5];\n\t}"
-      : "+r"(v.x), "+r"(v.y), "+r"(v.z), "+r"(v.w)
-      : "r"((uint32_t)p), "r"(smem_u32(addr))
-      : "memory");
 }
 
 // Bounded wait that also gives up at once when another warp has aborted.
@@ -174,6 +165,7 @@ __global__ void __launch_bounds__(kThreads, 2) pgemv_kernel(const GemvArgs a, co
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + 320);
   uint64_t* nwbar = reinterpret_cast<uint64_t*>(smem + 336);
   unsigned char* xsm = smem + geo.off_x;  // x: [slot][group][gs bf16 + 16 pad bytes]
+  const unsigned char* zero = smem + geo.off_zero;  // read as B by the lanes that carry no x
   const bf16* nwsm = reinterpret_cast<const bf16*>(smem + geo.off_nw);
   float* xs = reinterpret_cast<float*>(smem + geo.off_xs);
   float* red = reinterpret_cast<float*>(smem + geo.off_red);
@@ -386,6 +378,7 @@ __global__ void __launch_bounds__(kThreads, 2) pgemv_kernel(const GemvArgs a, co
     const int pad = (geo.xk - K) / 8;  // chunks
     for (int i = tid; i < geo.x_slots * pad; i += kThreads)
       *reinterpret_cast<uint4*>(xchunk(i / pad, nch + i % pad)) = make_uint4(0u, 0u, 0u, 0u);
+    for (int i = tid; i < GS / 2; i += kThreads) reinterpret_cast<uint32_t*>(smem + geo.off_zero)[i] = 0u;
     const int gpad = S * 8 - geo.ng;
     for (int i = tid; i < geo.x_slots * gpad; i += kThreads) xs[(i / gpad) * S * 8 + geo.ng + i % gpad] = 0.f;
   }
@@ -395,10 +388,8 @@ __global__ void __launch_bounds__(kThreads, 2) pgemv_kernel(const GemvArgs a, co
   int best_i = 0x7fffffff;
 
   if (warp < kConsumers) {
-    const int g = lane >> 2, t = lane & 3;
+    const int g = lane >> 2, t = lane & 3, t1 = t & 1;
     const bool has_x = g == t;  // the lanes whose B column carries x
-    // B registers (two sets, alternate slice quads); zero for the other lanes
-    uint4 xa0 = make_uint4(0u, 0u, 0u, 0u), xa1 = xa0, xb0 = xa0, xb1 = xa0;
     const uint32_t MASK = 0x000F000Fu;
     const uint32_t MAGIC_LO = 0x43004300u;  // bf16 128 + nibble
     const uint32_t MAGIC_HI = 0x45004500u;  // bf16 2048 + 16 * nibble
@@ -408,84 +399,120 @@ __global__ void __launch_bounds__(kThreads, 2) pgemv_kernel(const GemvArgs a, co
     // (the magic is 2^32 itself for d == 1, hence 64 bits; the host computes
     // it, a 64-bit division here would cost the critical path ~0.5 us)
     const unsigned long long lbt_magic = geo.lbt_magic;
+    // one unit = (tile, half-span): where its codes, x, scales and output
+    // slot are
+    struct Unit {
+      const unsigned char* aw;   // this lane's code words
+      const unsigned char* px;   // x of the unit's group for this lane (or the zero block)
+      const unsigned char* sbp;  // this lane's scale/bias record
+      const float* xg;           // the group sums
+      int slot;                  // red index of row g (row g+8 is 8 rows on)
+    };
+    auto unit = [&](int u, int a0, const unsigned char* sbase) -> Unit {
+      const int ti = u >> 1, hs = u & 1;
+      const int gt = a0 + ti;
+      const int lb = (int)(((unsigned long long)gt * lbt_magic) >> 32);
+      const int rem = gt - lb * lb_tiles;
+      const int h = rem >= S ? 1 : 0;
+      const int sp = rem - h * S;
+      const int xsl = (int)(((unsigned long long)lb * geo.lps_magic) >> 32);  // 0 unless x_slots > 1
+      const unsigned char* tile = sbase + (size_t)ti * geo.tile_bytes;
+      Unit r;
+      r.aw = tile + hs * (A_BYTES / 2) + lane * 16;
+      r.px = has_x ? xsm + (size_t)xsl * geo.xslot_bytes + (size_t)(sp * 8 + hs * 4 + t) * geo.gstride : zero;
+      r.sbp = tile + A_BYTES + hs * 256 + (g * 2 + t1) * 16;
+      r.xg = xs + xsl * S * 8 + sp * 8 + hs * 4 + 2 * t1;
+      r.slot = (((lb - lb0) * halves + h) * 16 + g) * SKP + sp * 2 + hs;
+      return r;
+    };
+    // slice quad q of a unit: HW code loads, two x loads, four (int4) or
+    // eight (int8) MMAs into four independent accumulators
+    auto quad = [&](const Unit& U, int q, float (&d)[4][4]) {
+      uint4 wa[HW];
+#pragma unroll
+      for (int hw = 0; hw < HW; ++hw) wa[hw] = *reinterpret_cast<const uint4*>(U.aw + (q * HW + hw) * 512);
+      const uint4 X0 = *reinterpret_cast<const uint4*>(U.px + q * 32);
+      const uint4 X1 = *reinterpret_cast<const uint4*>(U.px + q * 32 + 16);
+      const uint32_t bx[8] = {X0.x, X0.y, X0.z, X0.w, X1.x, X1.y, X1.z, X1.w};
+      const uint32_t w0v[4] = {wa[0].x, wa[0].y, wa[0].z, wa[0].w};
+      const uint32_t w1v[4] = {wa[HW - 1].x, wa[HW - 1].y, wa[HW - 1].z, wa[HW - 1].w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (BITS == 4) {
+          const uint32_t w = w0v[j];
+          mma_bf16_16816(d[j], lop3_and_or(w, MASK, MAGIC_LO), lop3_and_or(w >> 4, MASK, MAGIC_LO),
+                         lop3_and_or(w >> 8, MASK, MAGIC_LO), lop3_and_or(w >> 12, MASK, MAGIC_LO), bx[2 * j],
+                         bx[2 * j + 1]);
+        } else {
+          const uint32_t u0 = w0v[j], u1 = w1v[j];
+          mma_bf16_16816(d[(j & 1) * 2], lop3_and_or(u0, MASK, MAGIC_LO), lop3_and_or(u0 >> 8, MASK, MAGIC_LO),
+                         lop3_and_or(u1, MASK, MAGIC_LO), lop3_and_or(u1 >> 8, MASK, MAGIC_LO), bx[2 * j],
+                         bx[2 * j + 1]);
+          mma_bf16_16816(d[(j & 1) * 2 + 1], lop3_and_or(u0 >> 4, MASK, MAGIC_HI),
+                         lop3_and_or(u0 >> 12, MASK, MAGIC_HI), lop3_and_or(u1 >> 4, MASK, MAGIC_HI),
+                         lop3_and_or(u1 >> 12, MASK, MAGIC_HI), bx[2 * j], bx[2 * j + 1]);
+        }
+      }
+    };
+    // d: [g][2t] [g][2t+1] [g+8][2t] [g+8][2t+1]; columns 0-3 are the
+    // half-span's groups, so lanes t < 2 hold all of them
+    auto finish = [&](const Unit& U, const float (&d)[4][4]) {
+      float dv[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) dv[e] = (d[0][e] + d[1][e]) + (d[2][e] + d[3][e]);
+      const uint4 sb = *reinterpret_cast<const uint4*>(U.sbp);
+      const float2 xg = *reinterpret_cast<const float2*>(U.xg);
+      const float s0 = __uint_as_float(sb.x << 16), s1 = __uint_as_float(sb.x & 0xffff0000u);
+      const float s2 = __uint_as_float(sb.y << 16), s3 = __uint_as_float(sb.y & 0xffff0000u);
+      const float b0 = __uint_as_float(sb.z << 16), b1 = __uint_as_float(sb.z & 0xffff0000u);
+      const float b2 = __uint_as_float(sb.w << 16), b3 = __uint_as_float(sb.w & 0xffff0000u);
+      float pa = fmaf(s0, dv[0], 0.f), pb = fmaf(s2, dv[2], 0.f);
+      pa = fmaf(fmaf(-C, s0, b0), xg.x, pa);
+      pa = fmaf(s1, dv[1], pa);
+      pa = fmaf(fmaf(-C, s1, b1), xg.y, pa);
+      pb = fmaf(fmaf(-C, s2, b2), xg.x, pb);
+      pb = fmaf(s3, dv[3], pb);
+      pb = fmaf(fmaf(-C, s3, b3), xg.y, pb);
+      pa += __shfl_xor_sync(0xffffffffu, pa, 1);
+      pb += __shfl_xor_sync(0xffffffffu, pb, 1);
+      if (t == 0) {
+        red[U.slot] = pa;
+        red[U.slot + 8 * SKP] = pb;
+      }
+    };
     for (int st = 0; st < nst; ++st) {
       const int buf = st % geo.nbuf;
       const int a0 = T0 + st * geo.stage_tiles, a1 = min(T1, a0 + geo.stage_tiles);
       if (wait_or_abort(&full[buf], (uint32_t)((st / geo.nbuf) & 1), abort_flag, a.status)) {
         const int units = (a1 - a0) * 2;  // (tile, half-span)
         const unsigned char* sbase = bufs + (size_t)buf * geo.stage_bytes;
-        for (int u = warp; u < units; u += kConsumers) {
-          const int ti = u >> 1, hs = u & 1;
-          const int gt = a0 + ti;
-          const int lb = (int)(((unsigned long long)gt * lbt_magic) >> 32);
-          const int rem = gt - lb * lb_tiles;
-          const int h = rem >= S ? 1 : 0;
-          const int sp = rem - h * S;
-          const unsigned char* tile = sbase + (size_t)ti * geo.tile_bytes;
-          const int xsl = (int)(((unsigned long long)lb * geo.lps_magic) >> 32);  // 0 unless x_slots > 1
-          // only the lanes whose B column carries x read it (a predicated
-          // load: the other lanes' registers stay zero and cost no bandwidth)
-          const unsigned char* pbx = xsm + (size_t)xsl * geo.xslot_bytes + (size_t)(sp * 8 + hs * 4 + t) * geo.gstride;
-          const unsigned char* aw = tile + hs * (A_BYTES / 2) + lane * 16;
-          float d[4][4];
+        // two units at a time, interleaved quad by quad: eight independent
+        // accumulator chains, and one unit's drain overlaps the other's math
+        int u = warp;
+        for (; u + kConsumers < units; u += 2 * kConsumers) {
+          const Unit A = unit(u, a0, sbase), B = unit(u + kConsumers, a0, sbase);
+          float dA[4][4], dB[4][4];
 #pragma unroll
-          for (int i = 0; i < 4; ++i) d[i][0] = d[i][1] = d[i][2] = d[i][3] = 0.f;
+          for (int i = 0; i < 4; ++i) {
+            dA[i][0] = dA[i][1] = dA[i][2] = dA[i][3] = 0.f;
+            dB[i][0] = dB[i][1] = dB[i][2] = dB[i][3] = 0.f;
+          }
 #pragma unroll
           for (int q = 0; q < QH; ++q) {
-            uint4 wa[HW];
-#pragma unroll
-            for (int hw = 0; hw < HW; ++hw) wa[hw] = *reinterpret_cast<const uint4*>(aw + (q * HW + hw) * 512);
-            uint4& X0 = (q & 1) ? xb0 : xa0;
-            uint4& X1 = (q & 1) ? xb1 : xa1;
-            lds128_if(has_x, X0, pbx + q * 32);
-            lds128_if(has_x, X1, pbx + q * 32 + 16);
-            const uint32_t bx[8] = {X0.x, X0.y, X0.z, X0.w, X1.x, X1.y, X1.z, X1.w};
-            const uint32_t w0v[4] = {wa[0].x, wa[0].y, wa[0].z, wa[0].w};
-            const uint32_t w1v[4] = {wa[HW - 1].x, wa[HW - 1].y, wa[HW - 1].z, wa[HW - 1].w};
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              if (BITS == 4) {
-                const uint32_t w = w0v[j];
-                mma_bf16_16816(d[j], lop3_and_or(w, MASK, MAGIC_LO), lop3_and_or(w >> 4, MASK, MAGIC_LO),
-                               lop3_and_or(w >> 8, MASK, MAGIC_LO), lop3_and_or(w >> 12, MASK, MAGIC_LO), bx[2 * j],
-                               bx[2 * j + 1]);
-              } else {
-                const uint32_t u0 = w0v[j], u1 = w1v[j];
-                mma_bf16_16816(d[(j & 1) * 2], lop3_and_or(u0, MASK, MAGIC_LO), lop3_and_or(u0 >> 8, MASK, MAGIC_LO),
-                               lop3_and_or(u1, MASK, MAGIC_LO), lop3_and_or(u1 >> 8, MASK, MAGIC_LO), bx[2 * j],
-                               bx[2 * j + 1]);
-                mma_bf16_16816(d[(j & 1) * 2 + 1], lop3_and_or(u0 >> 4, MASK, MAGIC_HI),
-                               lop3_and_or(u0 >> 12, MASK, MAGIC_HI), lop3_and_or(u1 >> 4, MASK, MAGIC_HI),
-                               lop3_and_or(u1 >> 12, MASK, MAGIC_HI), bx[2 * j], bx[2 * j + 1]);
-              }
-            }
+            quad(A, q, dA);
+            quad(B, q, dB);
           }
-          // d: [g][2t] [g][2t+1] [g+8][2t] [g+8][2t+1]; columns 0-3 are the
-          // half-span's groups, so lanes t < 2 hold all of them
-          float dv[4];
+          finish(A, dA);
+          finish(B, dB);
+        }
+        if (u < units) {
+          const Unit A = unit(u, a0, sbase);
+          float dA[4][4];
 #pragma unroll
-          for (int e = 0; e < 4; ++e) dv[e] = (d[0][e] + d[1][e]) + (d[2][e] + d[3][e]);
-          const int t1 = t & 1;
-          const uint4 sb = *reinterpret_cast<const uint4*>(tile + A_BYTES + hs * 256 + (g * 2 + t1) * 16);
-          const float2 xg = *reinterpret_cast<const float2*>(xs + xsl * S * 8 + sp * 8 + hs * 4 + 2 * t1);
-          const float s0 = __uint_as_float(sb.x << 16), s1 = __uint_as_float(sb.x & 0xffff0000u);
-          const float s2 = __uint_as_float(sb.y << 16), s3 = __uint_as_float(sb.y & 0xffff0000u);
-          const float b0 = __uint_as_float(sb.z << 16), b1 = __uint_as_float(sb.z & 0xffff0000u);
-          const float b2 = __uint_as_float(sb.w << 16), b3 = __uint_as_float(sb.w & 0xffff0000u);
-          float pa = fmaf(s0, dv[0], 0.f), pb = fmaf(s2, dv[2], 0.f);
-          pa = fmaf(fmaf(-C, s0, b0), xg.x, pa);
-          pa = fmaf(s1, dv[1], pa);
-          pa = fmaf(fmaf(-C, s1, b1), xg.y, pa);
-          pb = fmaf(fmaf(-C, s2, b2), xg.x, pb);
-          pb = fmaf(s3, dv[3], pb);
-          pb = fmaf(fmaf(-C, s3, b3), xg.y, pb);
-          pa += __shfl_xor_sync(0xffffffffu, pa, 1);
-          pb += __shfl_xor_sync(0xffffffffu, pb, 1);
-          if (t == 0) {
-            const int prow = ((lb - lb0) * halves + h) * 16 + g;
-            red[prow * SKP + sp * 2 + hs] = pa;
-            red[(prow + 8) * SKP + sp * 2 + hs] = pb;
-          }
+          for (int i = 0; i < 4; ++i) dA[i][0] = dA[i][1] = dA[i][2] = dA[i][3] = 0.f;
+#pragma unroll
+          for (int q = 0; q < QH; ++q) quad(A, q, dA);
+          finish(A, dA);
         }
       }
       __syncwarp();

@@ -94,6 +94,7 @@ struct emx_qwen3 {
   QW embed, lm;
   bf16* final_norm = nullptr;
   float* inv_freq = nullptr;
+  float2* rope_cs = nullptr;  // (cos, sin) per position and frequency
   PgemvPlan p_lm{};
   bool packed_ok = false;  // packed copies match the loaded weights
   bool compiled = true;    // decode through the captured graph (PDL chain) or eagerly
@@ -371,6 +372,9 @@ int build(emx_qwen3* m) {
   if ((rc = alloc_t(m, hd / 2, &m->inv_freq))) return rc;
   if (k_rope_inv_freq(m->inv_freq, hd, c.rope_theta, m->ctx->stream) != cudaSuccess)
     return fail(EMX_ERR_CUDA, "rope table");
+  if ((rc = alloc_t(m, (size_t)c.kv_cap * (hd / 2), &m->rope_cs))) return rc;
+  if (rope_table_fill(m->rope_cs, m->inv_freq, c.kv_cap, hd / 2, m->ctx->stream) != cudaSuccess)
+    return fail(EMX_ERR_CUDA, "rope table");
   m->kv_layer = (size_t)m->nkv * c.kv_cap * hd;
   if ((rc = alloc_t(m, m->kv_layer * 2 * c.layers, &m->kv))) return rc;
   if ((rc = alloc_t(m, H, &m->xa)) || (rc = alloc_t(m, H, &m->xb)) || (rc = alloc_t(m, m->Nqkv, &m->qkvb)) ||
@@ -483,6 +487,7 @@ int enqueue_step(emx_qwen3* m) {
       a.k_norm = lw.k_norm;
       a.eps = c.eps;
       a.inv_freq = m->inv_freq;
+      a.rope_cs = m->rope_cs;
       a.kc = kc;
       a.vc = vc;
       a.cap = c.kv_cap;
