@@ -278,6 +278,48 @@ int ensure_packed(emx_qwen3* m) {
   return EMX_OK;
 }
 
+// The slice of checkpoint tensor `name` that rank `rank` of `world` keeps:
+// o = {row0, n_rows, col0, n_cols, block0, blocks} over the tensor's logical
+// [blocks x rows, cols] shape (cols = unpacked columns; quantized parts share
+// the weight's slice).  Dense models shard by tensor parallelism: q/k/v rows
+// by heads, gate/up rows by intermediate, o/down columns likewise; MoE models
+// by expert parallelism: expert blocks.  Everything else is replicated.
+// Returns 1 when the name is unknown.
+int shard_rule(const emx_qwen3_config& c, int world, int rank, const std::string& name, int32_t o[6]) {
+  const int hd = c.head_dim, H = c.hidden;
+  const bool moe = c.n_experts > 0, tp = world > 1 && !moe, ep = world > 1 && moe;
+  const int W = tp ? world : 1, r = tp ? rank : 0;
+  auto set = [&](int row0, int nrows, int col0, int ncols, int b0, int nb) {
+    o[0] = row0, o[1] = nrows, o[2] = col0, o[3] = ncols, o[4] = b0, o[5] = nb;
+    return 0;
+  };
+  auto ends = [&](const char* suf) {
+    const size_t n = strlen(suf);
+    if (name.size() < n || name.compare(name.size() - n, n, suf) != 0) return false;
+    return true;
+  };
+  std::string stem = name;
+  for (const char* part : {".weight", ".scales", ".biases"})
+    if (ends(part)) stem = name.substr(0, name.size() - strlen(part));
+  auto is = [&](const char* suf) {
+    const size_t n = strlen(suf);
+    return stem.size() >= n && stem.compare(stem.size() - n, n, suf) == 0;
+  };
+  if (stem == "model.embed_tokens" || stem == "lm_head") return set(0, c.vocab, 0, H, 0, 1);
+  if (stem == "model.norm" || is("input_layernorm") || is("post_attention_layernorm")) return set(0, 1, 0, H, 0, 1);
+  if (is("self_attn.q_norm") || is("self_attn.k_norm")) return set(0, 1, 0, hd, 0, 1);
+  if (is("self_attn.q_proj")) return set(r * (c.n_q / W) * hd, (c.n_q / W) * hd, 0, H, 0, 1);
+  if (is("self_attn.k_proj") || is("self_attn.v_proj")) return set(r * (c.n_kv / W) * hd, (c.n_kv / W) * hd, 0, H, 0, 1);
+  if (is("self_attn.o_proj")) return set(0, H, r * (c.n_q / W) * hd, (c.n_q / W) * hd, 0, 1);
+  if (!moe && (is("mlp.gate_proj") || is("mlp.up_proj"))) return set(r * (c.inter / W), c.inter / W, 0, H, 0, 1);
+  if (!moe && is("mlp.down_proj")) return set(0, H, r * (c.inter / W), c.inter / W, 0, 1);
+  if (moe && is("mlp.gate")) return set(0, c.n_experts, 0, H, 0, 1);
+  const int El = ep ? c.n_experts / world : c.n_experts, e0 = ep ? rank * El : 0;
+  if (moe && (is("mlp.switch_mlp.gate_proj") || is("mlp.switch_mlp.up_proj"))) return set(0, c.moe_inter, 0, H, e0, El);
+  if (moe && is("mlp.switch_mlp.down_proj")) return set(0, H, 0, c.moe_inter, e0, El);
+  return 1;
+}
+
 int build(emx_qwen3* m) {
   const emx_qwen3_config& c = m->c;
   const int W = m->world, r = m->rank;
@@ -412,6 +454,16 @@ int build(emx_qwen3* m) {
   if ((m->tp || m->ep) && (rc = alloc_t(m, T * H, &m->ppart))) return rc;
   if (cudaMallocHost(reinterpret_cast<void**>(&m->pinned), sizeof(int32_t) * ((size_t)c.kv_cap + 8)) != cudaSuccess)
     return fail(EMX_ERR_OOM, "pinned staging buffer");
+  // every registered slice is the one the shard rule states
+  for (const auto& kv : m->specs) {
+    const Spec& sp = kv.second;
+    int32_t o[6];
+    if (shard_rule(c, m->world, m->rank, kv.first, o)) return fail(EMX_ERR_STATE, "no shard rule for '%s'", kv.first.c_str());
+    const bool ok = sp.kind == 1 ? (o[3] == sp.norm_len)
+                                 : (o[0] == sp.row0 && o[1] == sp.n_rows && o[2] == sp.col0 && o[3] == sp.n_cols &&
+                                    o[4] == sp.gen_block0 && o[5] == sp.blocks);
+    if (!ok) return fail(EMX_ERR_STATE, "shard rule disagrees with the layout of '%s'", kv.first.c_str());
+  }
   return ctx_sync_check(m->ctx, "emx_qwen3_create");
 }
 
@@ -1046,6 +1098,19 @@ int emx_qwen3_decode_device(emx_qwen3* m, int n) {
   if (m->offset + n > m->c.kv_cap)
     return fail(EMX_ERR_STATE, "static KV overflow offset=%d + n=%d > cap=%d", m->offset, n, m->c.kv_cap);
   return run_steps(m, n);
+}
+
+int emx_qwen3_shard(const emx_qwen3_config* cfg, int world, int rank, const char* name, int32_t* out6) {
+  Q_REQUIRE(cfg && name && out6, "emx_qwen3_shard: null argument");
+  Q_REQUIRE(world >= 1 && rank >= 0 && rank < world, "emx_qwen3_shard: rank %d of %d", rank, world);
+  if (world > 1) {
+    const bool moe = cfg->n_experts > 0;
+    Q_REQUIRE(moe ? cfg->n_experts % world == 0
+                  : (cfg->n_q % world == 0 && cfg->n_kv % world == 0 && cfg->inter % world == 0),
+              "emx_qwen3_shard: not divisible across %d ranks", world);
+  }
+  Q_REQUIRE(shard_rule(*cfg, world, rank, name, out6) == 0, "emx_qwen3_shard: unknown tensor '%s'", name);
+  return EMX_OK;
 }
 
 int emx_qwen3_set_compiled(emx_qwen3* m, int compiled) {

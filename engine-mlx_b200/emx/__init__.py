@@ -93,6 +93,7 @@ _SIGS = {
     "emx_qwen3_read_tensor": (C.c_int, [C.c_void_p, C.c_char_p, C.c_void_p, C.c_size_t]),
     "emx_qwen3_read_kv": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_size_t]),
     "emx_qwen3_set_compiled": (C.c_int, [C.c_void_p, C.c_int]),
+    "emx_qwen3_shard": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_char_p, C.POINTER(C.c_int32)]),
     "emx_qwen3_is_compiled": (C.c_int, [C.c_void_p, C.POINTER(C.c_int)]),
     "emx_qwen3_init_random": (C.c_int, [C.c_void_p, C.c_uint64]),
     "emx_qwen3_reset": (C.c_int, [C.c_void_p]),
@@ -429,6 +430,14 @@ CONFIGS: Dict[str, Qwen3Config] = {
     "c5": Qwen3Config(hidden=5120, layers=64, n_q=64, n_kv=8, inter=25600, vocab=151936, tied=False,
                       kv_cap=32768, max_prefill=4096),
 }
+
+
+def shard(cfg: "Qwen3Config", world: int, rank: int, name: str):
+    """(row0, n_rows, col0, n_cols, block0, blocks) of tensor `name` kept by rank (host only)."""
+    out = (C.c_int32 * 6)()
+    c = cfg.c_struct()
+    _check(lib().emx_qwen3_shard(C.byref(c), world, rank, name.encode(), out))
+    return tuple(out)
 
 
 def quant_shapes(N: int, K: int, bits: int, gs: int, blocks: int = 0):

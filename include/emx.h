@@ -241,6 +241,14 @@ int emx_qwen3_decode(emx_qwen3* m, int32_t token, int n, int32_t* tokens_out);
 int emx_qwen3_prefill_device(emx_qwen3* m, const int32_t* tokens_dev, int T);
 int emx_qwen3_decode_device(emx_qwen3* m, int n);
 /* Number of kernel launches one decode step enqueues. */
+/* Host only (no device needed): the slice of checkpoint tensor `name` that
+ * rank `rank` of `world` keeps under the engine's partitioning — tensor
+ * parallel for dense models (q/k/v and gate/up rows, o/down columns),
+ * expert parallel for MoE (expert blocks) — as out6 = {row0, n_rows, col0,
+ * n_cols, block0, blocks}.  What load_weights_from_manifest would hand each
+ * rank (crates/serve/src/loader/weights.rs:17-284; no reference counterpart
+ * for the partitioning itself, which is new in this build). */
+int emx_qwen3_shard(const emx_qwen3_config* cfg, int world, int rank, const char* name, int32_t* out6);
 /* Qwen3Engine::is_compiled (crates/serve/src/engine_ext.rs:212-216) and the
  * choice between the compiled decode closure (decode_compiled.rs:113-120)
  * and the eager per-op step: compiled (default) replays one captured CUDA
