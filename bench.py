@@ -193,6 +193,8 @@ def run_engine(args, cfg, rank, world, dist):
     m = emx.Qwen3(ctx, cfg)
     m.init_random(args.seed)
     m.compiled = not args.eager
+    if args.per_op:
+        m.fused = False
 
     def barrier():
         if dist is not None:
@@ -268,6 +270,7 @@ def run_engine(args, cfg, rank, world, dist):
     achieved = step_bytes / (ms / args.steps / 1000.0) / 1e9
     # ---- the dominant kernel alone: the gate_up GEMV shape over rotating copies (> L2)
     kern = gemv_kernel_roofline(ctx, st, cfg, torch, hbm)
+    fused = m.fused
     m.close()
     if rank != 0:
         ctx.close()
@@ -286,6 +289,8 @@ def run_engine(args, cfg, rank, world, dist):
                     "api": "emx_qwen3_decode_step", "steps": n_e2e},
             "gpu_launches": launches * args.steps, "launches_per_step": launches,
             "clocks": clk.summary()}
+    line["config"]["decode_path"] = ("one persistent kernel per decode step" if fused
+                                     else "one kernel per operation, CUDA graph")
     if world == 1 and not args.no_cpu_baseline:
         v, cores = cpu_baseline(cfg, args.seed, args.cpu_steps)
         line["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": cores, "kind": "port",
@@ -352,6 +357,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--eager", action="store_true",
                     help="decode without the CUDA graph (kernels in plain stream order): for profilers")
+    ap.add_argument("--per-op", action="store_true",
+                    help="decode with one kernel per operation instead of the persistent step kernel")
     ap.add_argument("--kernel-only", action="store_true",
                     help="time only the dominant kernel (packed GEMV, gate|up shape) and print its roofline")
     args = ap.parse_args()

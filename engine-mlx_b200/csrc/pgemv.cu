@@ -30,130 +30,16 @@
 
 #include <algorithm>
 
+#include "pgemv_dev.cuh"
+
 namespace emx {
 
 namespace {
 
+using namespace pg;
+
 constexpr int kConsumers = 8;
 constexpr int kThreads = (kConsumers + 1) * 32;
-constexpr int kMaxBuf = 8;
-
-struct PGeom {
-  int K, ng, S;
-  int tile_bytes, a_bytes;
-  int halves;
-  int lb_total;
-  int stage_tiles, nbuf;
-  int stage_bytes;
-  int x_slots, xk;  // x elements per slot (whole spans)
-  int gstride;      // bytes per x group in shared memory (2*gs + 16: banks rotate per group)
-  int xslot_bytes;  // bytes per x slot
-  int red_rows;
-  int nw_bytes;  // room for the norm weights (fetched before the wait)
-  unsigned long long lbt_magic;  // ceil(2^32 / (halves * S)): tile -> logical block
-  unsigned long long lps_magic;  // ceil(2^32 / (slot rows / 16)): logical block -> x slot
-  int off_x, off_nw, off_zero, off_xs, off_red, off_buf;
-};
-
-__host__ __device__ inline int ptile_bytes(int bits, int gs) { return 16 * 8 * gs * bits / 8 + 512; }
-
-// Shared-memory carve-up (the first 384 bytes: mbarriers, reduction scratch,
-// per-group 1/rms, the abort flag and the norm-weight mbarrier).
-__host__ __device__ inline int pgeom_layout(PGeom& g, int gs) {
-  g.off_x = 384;
-  g.off_nw = g.off_x + g.x_slots * g.xslot_bytes;
-  g.off_zero = g.off_nw + g.nw_bytes;
-  g.off_xs = g.off_zero + 2 * gs;
-  g.off_red = g.off_xs + ((g.x_slots * g.S * 8 * 4 + 15) & ~15);
-  g.off_buf = (g.off_red + g.red_rows * g.S * 2 * 4 + 127) & ~127;
-  return g.off_buf + g.nbuf * g.stage_bytes;
-}
-
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-
-// Bounded wait that also gives up at once when another warp has aborted.
-__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* status) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = globaltimer_ns();
-  for (uint32_t i = 0; i < kSpinLimit; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 63u) == 63u) {
-      if (*abort_flag) return false;
-      if (globaltimer_ns() - t0 > kWaitLimitNs) break;
-    }
-  }
-  report_status(status, kDevTimeoutMbar);
-  *abort_flag = 1;
-  return false;
-}
-
-__device__ __forceinline__ void unpack8f(uint4 v, float (&f)[8]) {
-  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    f[2 * i] = __uint_as_float(w[i] << 16);
-    f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
-  }
-}
-
-// Eight floats that are bf16 values already (no rounding needed).
-__device__ __forceinline__ uint4 pack8exact(const float (&f)[8]) {
-  uint4 r;
-  r.x = (__float_as_uint(f[0]) >> 16) | (__float_as_uint(f[1]) & 0xffff0000u);
-  r.y = (__float_as_uint(f[2]) >> 16) | (__float_as_uint(f[3]) & 0xffff0000u);
-  r.z = (__float_as_uint(f[4]) >> 16) | (__float_as_uint(f[5]) & 0xffff0000u);
-  r.w = (__float_as_uint(f[6]) >> 16) | (__float_as_uint(f[7]) & 0xffff0000u);
-  return r;
-}
-
-
-// The pre-norm source values of elements [8c, 8c+8) (bf16 values as float).
-__device__ __forceinline__ void src8(const GemvArgs& a, int c, int tok, float (&v)[8]) {
-  const int k0 = c * 8;
-  if (a.pro == kProEmbedNorm) {
-    const int per = 32 / a.emb_bits;
-    const int ngk = a.K / a.emb_gs;
-    const uint32_t* row = a.emb_w + (size_t)tok * (a.K / per);
-    const bf16 sv = a.emb_s[(size_t)tok * ngk + k0 / a.emb_gs];
-    const bf16 bv = a.emb_b[(size_t)tok * ngk + k0 / a.emb_gs];
-#pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const int k = k0 + e;
-      const uint32_t q = (row[k / per] >> (a.emb_bits * (k % per))) & ((1u << a.emb_bits) - 1u);
-      v[e] = bf2f(dequant1(q, sv, bv));
-    }
-    return;
-  }
-  unpack8f(*reinterpret_cast<const uint4*>(a.x + k0), v);
-  if (a.pro == kProAddNorm) {
-    float add[8];
-    if (a.moe_y) {
-#pragma unroll
-      for (int e = 0; e < 8; ++e) add[e] = 0.f;
-      const int n = *a.moe_n;
-      for (int s = 0; s < n; ++s) {
-        float y[8];
-        unpack8f(*reinterpret_cast<const uint4*>(a.moe_y + (size_t)s * a.K + k0), y);
-        const float w = a.moe_w[s];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) add[e] = __fadd_rn(add[e], __fmul_rn(y[e], w));
-      }
-    } else {
-      const float4 p0 = *reinterpret_cast<const float4*>(a.add_f32 + k0);
-      const float4 p1 = *reinterpret_cast<const float4*>(a.add_f32 + k0 + 4);
-      add[0] = p0.x, add[1] = p0.y, add[2] = p0.z, add[3] = p0.w;
-      add[4] = p1.x, add[5] = p1.y, add[6] = p1.z, add[7] = p1.w;
-      if (a.add_round) {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) add[e] = bfround(add[e]);
-      }
-    }
-#pragma unroll
-    for (int e = 0; e < 8; ++e) v[e] = bfround(__fadd_rn(v[e], add[e]));
-  }
-}
 
 template <int BITS, int GS>
 __global__ void __launch_bounds__(kThreads, 2) pgemv_kernel(const GemvArgs a, const PGeom geo) {
@@ -164,27 +50,12 @@ __global__ void __launch_bounds__(kThreads, 2) pgemv_kernel(const GemvArgs a, co
   float* inv = scratch + 32;                             // 8 floats
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + 320);
   uint64_t* nwbar = reinterpret_cast<uint64_t*>(smem + 336);
-  unsigned char* xsm = smem + geo.off_x;  // x: [slot][group][gs bf16 + 16 pad bytes]
-  const unsigned char* zero = smem + geo.off_zero;  // read as B by the lanes that carry no x
-  const bf16* nwsm = reinterpret_cast<const bf16*>(smem + geo.off_nw);
-  float* xs = reinterpret_cast<float*>(smem + geo.off_xs);
-  float* red = reinterpret_cast<float*>(smem + geo.off_red);
+  const PgSmem sm = pg_smem(smem, geo);
   unsigned char* bufs = smem + geo.off_buf;
-
-  constexpr int SPAN_K = 8 * GS;
-  constexpr int QH = GS / 16;   // slice quads per half-span (4 groups)
-  constexpr int HW = BITS / 4;  // word sets per quad
-  constexpr int A_BYTES = 16 * SPAN_K * BITS / 8;
-  constexpr int CPG = GS / 8;   // 8-element chunks per group
-  // byte offset of 8-element chunk c of x slot `slot`
-  auto xchunk = [&](int slot, int c) -> unsigned char* {
-    return xsm + (size_t)slot * geo.xslot_bytes + (c / CPG) * geo.gstride + (c % CPG) * 16;
-  };
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const bool gather = a.slot_expert != nullptr;
-  const int halves = geo.halves, S = geo.S, SKP = S * 2;  // partial slots per row: span x half-span
-  const int lb_tiles = halves * S;
+  const int lb_tiles = geo.halves * geo.S;
   const size_t lb_bytes = (size_t)lb_tiles * geo.tile_bytes;
   const int lps = gather ? a.slot_rows / 16 : 1;  // logical blocks per slot
   const bool producer = warp == kConsumers && lane == 0;
@@ -264,15 +135,8 @@ __global__ void __launch_bounds__(kThreads, 2) pgemv_kernel(const GemvArgs a, co
     }
   }
 
-  // residual rows of this CTA's epilogue, loaded now so that their latency
-  // overlaps the prologue's
-  float res_pre[2] = {0.f, 0.f};
-  const bool res_early = a.epi == kEpiResid && (lb1 - lb0) * 16 <= 2 * kThreads;
-  if (res_early) {
-    const int nlog = (lb1 - lb0) * 16;
-    if (tid < nlog) res_pre[0] = bf2f(a.res[lb0 * 16 + tid]);
-    if (tid + kThreads < nlog) res_pre[1] = bf2f(a.res[lb0 * 16 + tid + kThreads]);
-  }
+  float res_pre[2];
+  const bool res_early = pg_res_early(a, lb0, lb1, tid, kThreads, res_pre);
 
   int tok = 0;
   if (a.pro == kProEmbedNorm) {
@@ -283,238 +147,19 @@ __global__ void __launch_bounds__(kThreads, 2) pgemv_kernel(const GemvArgs a, co
     }
   }
 
-  // ---- prologue: x (padded groups, zero past K to whole spans) and the
-  //      group sums of x
-  {
-    const int K = geo.K;
-    const int nch = K / 8;
-    auto emit_raw = [&](int slot, int c, bool valid, uint4 raw, const float (&o)[8]) {
-      float ps = 0.f;
-      if (valid) {
-        *reinterpret_cast<uint4*>(xchunk(slot, c)) = raw;
-#pragma unroll
-        for (int e = 0; e < 8; ++e) ps += o[e];
-      }
-#pragma unroll
-      for (int off = 1; off < CPG; off <<= 1) ps += __shfl_xor_sync(0xffffffffu, ps, off);
-      if (valid && (c % CPG) == 0) xs[slot * S * 8 + c / CPG] = ps;
-    };
-    // o holds bf16 values (the norm output is rounded per element)
-    auto emit = [&](int slot, int c, bool valid, const float (&o)[8]) {
-      emit_raw(slot, c, valid, valid ? pack8exact(o) : make_uint4(0u, 0u, 0u, 0u), o);
-    };
-    if (a.pro == kProX) {
-      for (int slot = 0; slot < geo.x_slots; ++slot) {
-#pragma unroll 1
-        for (int it = 0; it * kThreads < nch; ++it) {
-          const int c = it * kThreads + tid;
-          const bool valid = c < nch;
-          const uint4 raw = valid ? *reinterpret_cast<const uint4*>(a.x + (size_t)slot * K + c * 8)
-                                  : make_uint4(0u, 0u, 0u, 0u);
-          float v[8];
-          unpack8f(raw, v);
-          emit_raw(slot, c, valid, raw, v);
-        }
-      }
-    } else {
-      // pass 1: pre-norm source staged in the x buffer, sums of squares per
-      // norm group
-      const int groups = a.norm_groups > 0 ? a.norm_groups : 1;
-      const int gd = K / groups;
-      const bool store = (a.pro == kProEmbedNorm || a.pro == kProAddNorm) && blockIdx.x == 0 && a.x_out;
-      float ssg[8];
-#pragma unroll
-      for (int gi = 0; gi < 8; ++gi) ssg[gi] = 0.f;
-#pragma unroll 1
-      for (int c = tid; c < nch; c += kThreads) {
-        float v[8];
-        src8(a, c, tok, v);
-        float ss = 0.f;
-#pragma unroll
-        for (int e = 0; e < 8; ++e) ss = fmaf(v[e], v[e], ss);
-        const int grp = (c * 8) / gd;
-#pragma unroll
-        for (int gi = 0; gi < 8; ++gi)
-          if (grp == gi) ssg[gi] += ss;
-        const uint4 pk = pack8exact(v);
-        *reinterpret_cast<uint4*>(xchunk(0, c)) = pk;
-        if (store) *reinterpret_cast<uint4*>(a.x_out + c * 8) = pk;
-      }
-      for (int gi = 0; gi < groups; ++gi) {
-        float sv = 0.f;
-#pragma unroll
-        for (int q = 0; q < 8; ++q)
-          if (q == gi) sv = ssg[q];
-        const float ss = block_sum(sv, scratch);
-        if (tid == 0) inv[gi] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)gd), a.eps)));
-      }
-      __syncthreads();
-      // pass 2: scale and weight in place (each thread rewrites its own chunks)
-      if (!wait_or_abort(nwbar, 0u, abort_flag, a.status)) {
-        // no weights: the outputs are garbage and the status word says so
-      }
-#pragma unroll 1
-      for (int it = 0; it * kThreads < nch; ++it) {
-        const int c = it * kThreads + tid;
-        const bool valid = c < nch;
-        float o[8];
-        if (valid) {
-          float v[8], w[8];
-          unpack8f(*reinterpret_cast<const uint4*>(xchunk(0, c)), v);
-          unpack8f(*reinterpret_cast<const uint4*>(nwsm + c * 8), w);
-          const float iv = inv[(c * 8) / gd];
-#pragma unroll
-          for (int e = 0; e < 8; ++e)
-            o[e] = groups == 1 ? bfround(__fmul_rn(bfround(__fmul_rn(v[e], iv)), w[e]))
-                               : bfround(__fmul_rn(__fmul_rn(v[e], iv), w[e]));
-        } else {
-#pragma unroll
-          for (int e = 0; e < 8; ++e) o[e] = 0.f;
-        }
-        emit(0, c, valid, o);
-      }
-    }
-    // zero padding: x past K (whole chunks), group sums past ng
-    const int pad = (geo.xk - K) / 8;  // chunks
-    for (int i = tid; i < geo.x_slots * pad; i += kThreads)
-      *reinterpret_cast<uint4*>(xchunk(i / pad, nch + i % pad)) = make_uint4(0u, 0u, 0u, 0u);
-    for (int i = tid; i < GS / 2; i += kThreads) reinterpret_cast<uint32_t*>(smem + geo.off_zero)[i] = 0u;
-    const int gpad = S * 8 - geo.ng;
-    for (int i = tid; i < geo.x_slots * gpad; i += kThreads) xs[(i / gpad) * S * 8 + geo.ng + i % gpad] = 0.f;
-  }
+  pg_prologue<GS, SyncCta>(a, geo, sm, reinterpret_cast<const bf16*>(smem + geo.off_nw), norm_pre ? nwbar : nullptr,
+                           0u, scratch, inv, abort_flag, tok, tid, kThreads, blockIdx.x == 0);
   __syncthreads();
 
   float best_v = -INFINITY;
   int best_i = 0x7fffffff;
 
   if (warp < kConsumers) {
-    const int g = lane >> 2, t = lane & 3, t1 = t & 1;
-    const bool has_x = g == t;  // the lanes whose B column carries x
-    const uint32_t MASK = 0x000F000Fu;
-    const uint32_t MAGIC_LO = 0x43004300u;  // bf16 128 + nibble
-    const uint32_t MAGIC_HI = 0x45004500u;  // bf16 2048 + 16 * nibble
-    constexpr float C = BITS == 4 ? 128.0f : 2176.0f;
-    // tile -> (logical block, half, span) by a 64-bit multiply, not a
-    // division: floor(n / d) == (n * ceil(2^32 / d)) >> 32 for n < 2^32 / d
-    // (the magic is 2^32 itself for d == 1, hence 64 bits; the host computes
-    // it, a 64-bit division here would cost the critical path ~0.5 us)
-    const unsigned long long lbt_magic = geo.lbt_magic;
-    // one unit = (tile, half-span): where its codes, x, scales and output
-    // slot are
-    struct Unit {
-      const unsigned char* aw;   // this lane's code words
-      const unsigned char* px;   // x of the unit's group for this lane (or the zero block)
-      const unsigned char* sbp;  // this lane's scale/bias record
-      const float* xg;           // the group sums
-      int slot;                  // red index of row g (row g+8 is 8 rows on)
-    };
-    auto unit = [&](int u, int a0, const unsigned char* sbase) -> Unit {
-      const int ti = u >> 1, hs = u & 1;
-      const int gt = a0 + ti;
-      const int lb = (int)(((unsigned long long)gt * lbt_magic) >> 32);
-      const int rem = gt - lb * lb_tiles;
-      const int h = rem >= S ? 1 : 0;
-      const int sp = rem - h * S;
-      const int xsl = (int)(((unsigned long long)lb * geo.lps_magic) >> 32);  // 0 unless x_slots > 1
-      const unsigned char* tile = sbase + (size_t)ti * geo.tile_bytes;
-      Unit r;
-      r.aw = tile + hs * (A_BYTES / 2) + lane * 16;
-      r.px = has_x ? xsm + (size_t)xsl * geo.xslot_bytes + (size_t)(sp * 8 + hs * 4 + t) * geo.gstride : zero;
-      r.sbp = tile + A_BYTES + hs * 256 + (g * 2 + t1) * 16;
-      r.xg = xs + xsl * S * 8 + sp * 8 + hs * 4 + 2 * t1;
-      r.slot = (((lb - lb0) * halves + h) * 16 + g) * SKP + sp * 2 + hs;
-      return r;
-    };
-    // slice quad q of a unit: HW code loads, two x loads, four (int4) or
-    // eight (int8) MMAs into four independent accumulators
-    auto quad = [&](const Unit& U, int q, float (&d)[4][4]) {
-      uint4 wa[HW];
-#pragma unroll
-      for (int hw = 0; hw < HW; ++hw) wa[hw] = *reinterpret_cast<const uint4*>(U.aw + (q * HW + hw) * 512);
-      const uint4 X0 = *reinterpret_cast<const uint4*>(U.px + q * 32);
-      const uint4 X1 = *reinterpret_cast<const uint4*>(U.px + q * 32 + 16);
-      const uint32_t bx[8] = {X0.x, X0.y, X0.z, X0.w, X1.x, X1.y, X1.z, X1.w};
-      const uint32_t w0v[4] = {wa[0].x, wa[0].y, wa[0].z, wa[0].w};
-      const uint32_t w1v[4] = {wa[HW - 1].x, wa[HW - 1].y, wa[HW - 1].z, wa[HW - 1].w};
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        if (BITS == 4) {
-          const uint32_t w = w0v[j];
-          mma_bf16_16816(d[j], lop3_and_or(w, MASK, MAGIC_LO), lop3_and_or(w >> 4, MASK, MAGIC_LO),
-                         lop3_and_or(w >> 8, MASK, MAGIC_LO), lop3_and_or(w >> 12, MASK, MAGIC_LO), bx[2 * j],
-                         bx[2 * j + 1]);
-        } else {
-          const uint32_t u0 = w0v[j], u1 = w1v[j];
-          mma_bf16_16816(d[(j & 1) * 2], lop3_and_or(u0, MASK, MAGIC_LO), lop3_and_or(u0 >> 8, MASK, MAGIC_LO),
-                         lop3_and_or(u1, MASK, MAGIC_LO), lop3_and_or(u1 >> 8, MASK, MAGIC_LO), bx[2 * j],
-                         bx[2 * j + 1]);
-          mma_bf16_16816(d[(j & 1) * 2 + 1], lop3_and_or(u0 >> 4, MASK, MAGIC_HI),
-                         lop3_and_or(u0 >> 12, MASK, MAGIC_HI), lop3_and_or(u1 >> 4, MASK, MAGIC_HI),
-                         lop3_and_or(u1 >> 12, MASK, MAGIC_HI), bx[2 * j], bx[2 * j + 1]);
-        }
-      }
-    };
-    // d: [g][2t] [g][2t+1] [g+8][2t] [g+8][2t+1]; columns 0-3 are the
-    // half-span's groups, so lanes t < 2 hold all of them
-    auto finish = [&](const Unit& U, const float (&d)[4][4]) {
-      float dv[4];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) dv[e] = (d[0][e] + d[1][e]) + (d[2][e] + d[3][e]);
-      const uint4 sb = *reinterpret_cast<const uint4*>(U.sbp);
-      const float2 xg = *reinterpret_cast<const float2*>(U.xg);
-      const float s0 = __uint_as_float(sb.x << 16), s1 = __uint_as_float(sb.x & 0xffff0000u);
-      const float s2 = __uint_as_float(sb.y << 16), s3 = __uint_as_float(sb.y & 0xffff0000u);
-      const float b0 = __uint_as_float(sb.z << 16), b1 = __uint_as_float(sb.z & 0xffff0000u);
-      const float b2 = __uint_as_float(sb.w << 16), b3 = __uint_as_float(sb.w & 0xffff0000u);
-      float pa = fmaf(s0, dv[0], 0.f), pb = fmaf(s2, dv[2], 0.f);
-      pa = fmaf(fmaf(-C, s0, b0), xg.x, pa);
-      pa = fmaf(s1, dv[1], pa);
-      pa = fmaf(fmaf(-C, s1, b1), xg.y, pa);
-      pb = fmaf(fmaf(-C, s2, b2), xg.x, pb);
-      pb = fmaf(s3, dv[3], pb);
-      pb = fmaf(fmaf(-C, s3, b3), xg.y, pb);
-      pa += __shfl_xor_sync(0xffffffffu, pa, 1);
-      pb += __shfl_xor_sync(0xffffffffu, pb, 1);
-      if (t == 0) {
-        red[U.slot] = pa;
-        red[U.slot + 8 * SKP] = pb;
-      }
-    };
     for (int st = 0; st < nst; ++st) {
       const int buf = st % geo.nbuf;
       const int a0 = T0 + st * geo.stage_tiles, a1 = min(T1, a0 + geo.stage_tiles);
-      if (wait_or_abort(&full[buf], (uint32_t)((st / geo.nbuf) & 1), abort_flag, a.status)) {
-        const int units = (a1 - a0) * 2;  // (tile, half-span)
-        const unsigned char* sbase = bufs + (size_t)buf * geo.stage_bytes;
-        // two units at a time, interleaved quad by quad: eight independent
-        // accumulator chains, and one unit's drain overlaps the other's math
-        int u = warp;
-        for (; u + kConsumers < units; u += 2 * kConsumers) {
-          const Unit A = unit(u, a0, sbase), B = unit(u + kConsumers, a0, sbase);
-          float dA[4][4], dB[4][4];
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            dA[i][0] = dA[i][1] = dA[i][2] = dA[i][3] = 0.f;
-            dB[i][0] = dB[i][1] = dB[i][2] = dB[i][3] = 0.f;
-          }
-#pragma unroll
-          for (int q = 0; q < QH; ++q) {
-            quad(A, q, dA);
-            quad(B, q, dB);
-          }
-          finish(A, dA);
-          finish(B, dB);
-        }
-        if (u < units) {
-          const Unit A = unit(u, a0, sbase);
-          float dA[4][4];
-#pragma unroll
-          for (int i = 0; i < 4; ++i) dA[i][0] = dA[i][1] = dA[i][2] = dA[i][3] = 0.f;
-#pragma unroll
-          for (int q = 0; q < QH; ++q) quad(A, q, dA);
-          finish(A, dA);
-        }
-      }
+      if (wait_or_abort(&full[buf], (uint32_t)((st / geo.nbuf) & 1), abort_flag, a.status))
+        pg_stage<BITS, GS>(geo, sm, bufs + (size_t)buf * geo.stage_bytes, a0, a1, lb0, warp, lane, kConsumers, 0);
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[buf]);
     }
@@ -536,116 +181,13 @@ __global__ void __launch_bounds__(kThreads, 2) pgemv_kernel(const GemvArgs a, co
   }
   __syncthreads();
 
-  // ---- epilogue: each logical row sums its slots in order ---------------
-  const int nlog = (lb1 - lb0) * 16;
-  for (int i = tid; i < nlog; i += kThreads) {
-    const int lbl = i >> 4, r = i & 15;
-    const int n = lb0 * 16 + i;
-    const int prow = lbl * halves * 16 + r;
-    float acc = 0.f;
-    for (int j = 0; j < SKP; ++j) acc += red[prow * SKP + j];
-    switch (a.epi) {
-      case kEpiStore:
-        a.y[n] = f2bf(acc);
-        break;
-      case kEpiResid: {
-        const float rv = !res_early ? bf2f(a.res[n]) : (i < kThreads ? res_pre[0] : res_pre[1]);
-        a.y[n] = f2bf(__fadd_rn(rv, bfround(acc)));
-        break;
-      }
-      case kEpiSwiglu: {
-        float accu = 0.f;
-        for (int j = 0; j < SKP; ++j) accu += red[(prow + 16) * SKP + j];
-        const float gv = bfround(acc), uv = bfround(accu);
-        const float sg = bfround(sigmoid_f(gv));
-        const float sv = bfround(__fmul_rn(gv, sg));
-        a.y[n] = f2bf(__fmul_rn(sv, uv));
-        break;
-      }
-      case kEpiArgmax: {
-        const float v = bfround(acc);
-        if (a.y) a.y[n] = f2bf(v);
-        if (v == v && (v > best_v || (v == best_v && n < best_i))) {
-          best_v = v;
-          best_i = n;
-        }
-        break;
-      }
-      default:
-        a.yf[n] = acc;
-        break;
-    }
-  }
+  pg_epilogue(a, geo, sm.red, lb0, lb1, tid, kThreads, res_early, res_pre, best_v, best_i);
 
   if (a.epi == kEpiArgmax) {
-    // CTA-level (max, first index), then the last CTA to finish reduces all
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, best_v, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, best_i, o);
-      if (ov > best_v || (ov == best_v && oi < best_i)) {
-        best_v = ov;
-        best_i = oi;
-      }
-    }
     __shared__ float wv[kConsumers + 1];
     __shared__ int wi[kConsumers + 1];
     __shared__ unsigned last;
-    if (lane == 0) {
-      wv[warp] = best_v;
-      wi[warp] = best_i;
-    }
-    __syncthreads();
-    if (tid == 0) {
-      float bv = wv[0];
-      int bi = wi[0];
-      for (int w = 1; w <= kConsumers; ++w)
-        if (wv[w] > bv || (wv[w] == bv && wi[w] < bi)) {
-          bv = wv[w];
-          bi = wi[w];
-        }
-      a.am_val[blockIdx.x] = bv;
-      a.am_idx[blockIdx.x] = bi;
-      __threadfence();
-      last = (atomicAdd(a.am_ticket, 1u) == gridDim.x - 1) ? 1u : 0u;
-    }
-    __syncthreads();
-    if (last) {
-      __threadfence();
-      // all CTAs' partials, one warp, all loads in flight at once
-      if (warp == 0) {
-        float bv = -INFINITY;
-        int bi = 0x7fffffff;
-        for (int c = lane; c < (int)gridDim.x; c += 32) {
-          const float v = __ldcg(a.am_val + c);
-          const int i = __ldcg(a.am_idx + c);
-          if (v > bv || (v == bv && i < bi)) {
-            bv = v;
-            bi = i;
-          }
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-          const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-          const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-          if (ov > bv || (ov == bv && oi < bi)) {
-            bv = ov;
-            bi = oi;
-          }
-        }
-        if (lane == 0) {
-          if (bi == 0x7fffffff) bi = 0;
-          *a.tok_out = bi;
-          if (a.hist && a.hist_n) {
-            const int hn = *a.hist_n;
-            a.hist[hn % a.hist_cap] = bi;
-            *a.hist_n = hn + 1;
-          }
-          if (a.pos) *a.pos += a.pos_inc;
-          *a.am_ticket = 0u;
-        }
-      }
-    }
+    pg_argmax_merge<SyncCta>(a, best_v, best_i, blockIdx.x, gridDim.x, tid, kConsumers + 1, wv, wi, &last);
   }
 }
 
@@ -716,26 +258,9 @@ __global__ void pack_kernel(const uint32_t* __restrict__ w, const bf16* __restri
 }
 
 void make_pgeom(int N, int K, int bits, int gs, int epi, const PgemvPlan& p, PGeom* g) {
-  g->K = K;
-  g->ng = K / gs;
-  g->S = (g->ng + 7) / 8;
-  g->tile_bytes = ptile_bytes(bits, gs);
-  g->a_bytes = g->tile_bytes - 512;
-  g->halves = epi == kEpiSwiglu ? 2 : 1;
-  g->lb_total = p.lb_total;
-  g->stage_tiles = p.stage_tiles;
-  g->nbuf = p.nbuf;
-  g->stage_bytes = p.stage_tiles * g->tile_bytes;
-  g->x_slots = p.x_slots;
-  g->xk = g->S * 8 * gs;
-  g->gstride = 2 * gs + 16;
-  g->xslot_bytes = g->S * 8 * g->gstride;
-  g->red_rows = p.lbs_max * g->halves * 16;
-  g->nw_bytes = (p.x_slots == 1 && K <= 8192) ? ((K * 2 + 15) & ~15) : 0;
-  const unsigned long long lbt = (unsigned long long)g->halves * g->S;
-  g->lbt_magic = (0x100000000ull + lbt - 1) / lbt;
-  g->lps_magic = 0;
   (void)N;
+  pgeom_make(g, K, bits, gs, epi, p.lb_total, p.stage_tiles, p.nbuf, p.x_slots, p.lbs_max,
+             p.x_slots == 1 && K <= 8192);
   pgeom_layout(*g, gs);
 }
 

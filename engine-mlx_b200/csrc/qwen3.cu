@@ -25,6 +25,7 @@
 #include "misc.cuh"
 #include "qgemm.cuh"
 #include "pgemv.cuh"
+#include "step.cuh"
 #include "qgemv.cuh"
 
 namespace emx {
@@ -120,6 +121,12 @@ struct emx_qwen3 {
   cudaGraphExec_t gexec = nullptr;
   int step_launches = 0;
   int32_t* pinned = nullptr;  // pinned host staging [kv_cap + 4]
+  // persistent decode step (dense model on one GPU)
+  bool step_ok = false;    // the shape has a plan and it fits
+  bool fused = false;      // decode through the persistent step kernel
+  bool step_coop = true;   // launch it cooperatively
+  StepPlan sp{};
+  StepArgs sa{};
 };
 
 namespace {
@@ -320,6 +327,98 @@ int shard_rule(const emx_qwen3_config& c, int world, int rank, const std::string
   return 1;
 }
 
+// Shared memory of the persistent step's CTA (one per SM).
+constexpr int kStepBudget1 = 227 * 1024;
+
+// Plans the persistent decode step when the model qualifies (dense, one GPU,
+// group size 64 everywhere, head_dim 128, 1/2/4 q heads per KV head) and
+// sets up its argument block; otherwise the per-kernel chain stays in use.
+int setup_step(emx_qwen3* m) {
+  const emx_qwen3_config& c = m->c;
+  if (m->moe || m->world > 1) return EMX_OK;
+  const QW& lmw = c.tied ? m->embed : m->lm;
+  const LayerW& l0 = m->L[0];
+  if (l0.qkv.gs != 64 || l0.o.gs != 64 || l0.gate_up.gs != 64 || l0.down.gs != 64 || lmw.gs != 64) return EMX_OK;
+  StepShape sh{};
+  sh.H = m->H;
+  sh.I = m->I;
+  sh.nq = m->nq;
+  sh.nkv = m->nkv;
+  sh.hd = m->hd;
+  sh.vocab = c.vocab;
+  sh.gs = 64;
+  sh.layers = c.layers;
+  sh.cap = c.kv_cap;
+  const int bits[5] = {l0.qkv.bits, l0.o.bits, l0.gate_up.bits, l0.down.bits, lmw.bits};
+  for (int i = 0; i < 5; ++i) sh.bits[i] = bits[i];
+  StepPlan p{};
+  const int nsm = m->ctx->num_sms;
+  if (step_make_plan(sh, nsm, 1, kStepBudget1, &p) || step_occupancy(p) < 1) {
+    cudaGetLastError();
+    return EMX_OK;
+  }
+  int rc;
+  StepLayer* d_layers = nullptr;
+  unsigned* sync = nullptr;
+  float* part = nullptr;
+  if ((rc = alloc_t(m, (size_t)c.layers, &d_layers)) || (rc = alloc_t(m, step_sync_words(nsm), &sync)) ||
+      (rc = alloc_t(m, (size_t)m->nkv * p.tmpl.max_splits * p.hpg * (m->hd + 4), &part)))
+    return rc;
+  std::vector<StepLayer> hl(c.layers);
+  for (int l = 0; l < c.layers; ++l) {
+    const LayerW& lw = m->L[l];
+    StepLayer& s = hl[l];
+    s.w[0] = lw.qkv.pk;
+    s.w[1] = lw.o.pk;
+    s.w[2] = lw.gate_up.pk;
+    s.w[3] = lw.down.pk;
+    s.in_norm = lw.in_norm;
+    s.post_norm = lw.post_norm;
+    s.q_norm = lw.q_norm;
+    s.k_norm = lw.k_norm;
+    s.kc = m->kv + m->kv_layer * (2 * (size_t)l);
+    s.vc = s.kc + m->kv_layer;
+  }
+  EMX_CHECK_CUDA(cudaMemcpyAsync(d_layers, hl.data(), sizeof(StepLayer) * hl.size(), cudaMemcpyHostToDevice,
+                                 m->ctx->stream),
+                 "step layer table");
+  EMX_CHECK_CUDA(cudaMemsetAsync(sync, 0, step_sync_words(nsm) * sizeof(unsigned), m->ctx->stream), "step sync");
+  EMX_CHECK_CUDA(cudaStreamSynchronize(m->ctx->stream), "step setup");
+  StepArgs a = p.tmpl;
+  a.layers = d_layers;
+  a.lm_w = lmw.pk;
+  a.final_norm = m->final_norm;
+  a.emb_w = m->embed.w;
+  a.emb_s = m->embed.s;
+  a.emb_b = m->embed.b;
+  a.emb_bits = m->embed.bits;
+  a.emb_gs = m->embed.gs;
+  a.token = m->token;
+  a.eps = c.eps;
+  a.h = m->xa;
+  a.qkvb = m->qkvb;
+  a.attnb = m->attnb;
+  a.act = m->hb;
+  a.logits = m->logits;
+  a.rope_cs = m->rope_cs;
+  a.attn_part = part;
+  a.pos = m->pos;
+  a.hist = m->hist;
+  a.hist_n = m->hist_n;
+  a.hist_cap = c.kv_cap;
+  a.am_val = m->am_val;
+  a.am_idx = m->am_idx;
+  a.am_ticket = m->am_ticket;
+  a.sync = sync;
+  a.status = m->ctx->status;
+  step_finish_args(&a);
+  m->sp = p;
+  m->sa = a;
+  m->step_ok = true;
+  m->fused = false;  // measured slower than the programmatically chained kernels; opt in with set_fused
+  return EMX_OK;
+}
+
 int build(emx_qwen3* m) {
   const emx_qwen3_config& c = m->c;
   const int W = m->world, r = m->rank;
@@ -454,6 +553,7 @@ int build(emx_qwen3* m) {
   if ((m->tp || m->ep) && (rc = alloc_t(m, T * H, &m->ppart))) return rc;
   if (cudaMallocHost(reinterpret_cast<void**>(&m->pinned), sizeof(int32_t) * ((size_t)c.kv_cap + 8)) != cudaSuccess)
     return fail(EMX_ERR_OOM, "pinned staging buffer");
+  if ((rc = setup_step(m))) return rc;
   // every registered slice is the one the shard rule states
   for (const auto& kv : m->specs) {
     const Spec& sp = kv.second;
@@ -481,6 +581,12 @@ int enqueue_step(emx_qwen3* m) {
   cudaStream_t st = m->ctx->stream;
   const bool pdl = m->compiled;  // the eager step is plain stream order
   m->step_launches = 0;
+  if (m->fused) {
+    cudaError_t e = step_launch(m->sa, m->sp, st, m->step_coop);
+    if (e != cudaSuccess) return fail_cuda(e, "decode step launch");
+    m->step_launches = 1;
+    return EMX_OK;
+  }
   bf16* cur = m->xa;
   bf16* nxt = m->xb;
   bool pending_add = false;  // the previous block's output still has to be added to `cur`
@@ -1122,6 +1228,23 @@ int emx_qwen3_set_compiled(emx_qwen3* m, int compiled) {
 int emx_qwen3_is_compiled(emx_qwen3* m, int* compiled) {
   Q_REQUIRE(m && compiled, "emx_qwen3_is_compiled: null argument");
   *compiled = m->compiled ? 1 : 0;
+  return EMX_OK;
+}
+
+int emx_qwen3_set_fused(emx_qwen3* m, int fused) {
+  Q_REQUIRE(m, "emx_qwen3_set_fused: null model");
+  Q_REQUIRE(!fused || m->step_ok, "emx_qwen3_set_fused: this model has no persistent step (MoE, sharded or shape)");
+  if (m->fused != (fused != 0) && m->gexec) {
+    cudaGraphExecDestroy(m->gexec);
+    m->gexec = nullptr;
+  }
+  m->fused = fused != 0;
+  return EMX_OK;
+}
+
+int emx_qwen3_is_fused(emx_qwen3* m, int* fused) {
+  Q_REQUIRE(m && fused, "emx_qwen3_is_fused: null argument");
+  *fused = m->fused ? 1 : 0;
   return EMX_OK;
 }
 

@@ -95,6 +95,8 @@ _SIGS = {
     "emx_qwen3_set_compiled": (C.c_int, [C.c_void_p, C.c_int]),
     "emx_qwen3_shard": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_char_p, C.POINTER(C.c_int32)]),
     "emx_qwen3_is_compiled": (C.c_int, [C.c_void_p, C.POINTER(C.c_int)]),
+    "emx_qwen3_set_fused": (C.c_int, [C.c_void_p, C.c_int]),
+    "emx_qwen3_is_fused": (C.c_int, [C.c_void_p, C.POINTER(C.c_int)]),
     "emx_qwen3_init_random": (C.c_int, [C.c_void_p, C.c_uint64]),
     "emx_qwen3_reset": (C.c_int, [C.c_void_p]),
     "emx_qwen3_offset": (C.c_int, [C.c_void_p, C.POINTER(C.c_int)]),
@@ -526,6 +528,17 @@ class Qwen3:
     @compiled.setter
     def compiled(self, on: bool):
         _check(lib().emx_qwen3_set_compiled(self.h, int(bool(on))))
+
+    @property
+    def fused(self) -> bool:
+        """Decode through the persistent step kernel (True) or one kernel per op."""
+        v = C.c_int()
+        _check(lib().emx_qwen3_is_fused(self.h, C.byref(v)))
+        return bool(v.value)
+
+    @fused.setter
+    def fused(self, on: bool):
+        _check(lib().emx_qwen3_set_fused(self.h, int(bool(on))))
 
     def init_random(self, seed: int):
         _check(lib().emx_qwen3_init_random(self.h, C.c_uint64(seed)))

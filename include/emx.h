@@ -257,6 +257,15 @@ int emx_qwen3_shard(const emx_qwen3_config* cfg, int world, int rank, const char
  * debugging). */
 int emx_qwen3_set_compiled(emx_qwen3* m, int compiled);
 int emx_qwen3_is_compiled(emx_qwen3* m, int* compiled);
+/* No reference counterpart (the reference's decode step is one traced MLX
+ * closure, crates/serve/src/compiled.rs:79-287, whatever its kernels):
+ * set_fused(m, 1) runs the whole decode step of a dense model on one GPU as
+ * one persistent kernel (grid barriers between phases) instead of one kernel
+ * per operation (the default).  It fails with EMX_ERR_INVALID when the model
+ * has no such plan (MoE, sharded, group size != 64, head_dim != 128, more
+ * than 4 q heads per KV head). */
+int emx_qwen3_set_fused(emx_qwen3* m, int fused);
+int emx_qwen3_is_fused(emx_qwen3* m, int* fused);
 int emx_qwen3_step_launches(emx_qwen3* m, int* n);
 
 #if defined(__GNUC__)

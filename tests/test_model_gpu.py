@@ -134,12 +134,14 @@ def test_tiny_model_matches_golden(ctx, tag):
     m.close()
 
 
-def test_kv_cache_matches_oracle(ctx):
+@pytest.mark.parametrize("fused", [False, True], ids=["per_op", "persistent"])
+def test_kv_cache_matches_oracle(ctx, fused):
     """Layer 0's K/V rows (k_norm + RoPE at each position, v as projected)
     after a prefill and three decode steps, read back with emx_qwen3_read_kv."""
     cfg = TINY_CFGS["mixed_int8"]
     m = emx.Qwen3(ctx, cfg)
     m.init_random(7)
+    m.fused = fused
     o = oracle.Model(cfg, oracle.make_checkpoint(cfg, 7))
     prompt = np.arange(3, 33, dtype=np.int32)
     m.prefill(prompt)
@@ -157,10 +159,11 @@ def test_kv_cache_matches_oracle(ctx):
     o.close()
 
 
-def _run_both(ctx, cfg, seed, prompt, n_forced, rng, what):
+def _run_both(ctx, cfg, seed, prompt, n_forced, rng, what, fused=False):
     forced = rng.integers(0, cfg.vocab, n_forced)
     m = emx.Qwen3(ctx, cfg)
     m.init_random(seed)
+    m.fused = fused
     gpu = [m.prefill(prompt, want_logits=True)]
     for t in forced:
         gpu.append(m.decode_step(int(t), want_logits=True))
@@ -176,10 +179,56 @@ def test_moe_model_matches_oracle(ctx):
     _run_both(ctx, MOE_CFG, 21, prompt, 6, rng, "moe")
 
 
-def test_deeper_model_matches_oracle(ctx):
+@pytest.mark.parametrize("fused", [False, True], ids=["per_op", "persistent"])
+def test_deeper_model_matches_oracle(ctx, fused):
     rng = np.random.default_rng(4)
     prompt = rng.integers(0, DEEP_CFG.vocab, 100).astype(np.int32)
-    _run_both(ctx, DEEP_CFG, 22, prompt, 10, rng, "deep")
+    _run_both(ctx, DEEP_CFG, 22, prompt, 10, rng, "deep", fused)
+
+
+@pytest.mark.parametrize("name", sorted(TINY_CFGS))
+def test_persistent_step_matches_oracle(ctx, name):
+    """The persistent decode-step kernel (one launch per token, grid barriers
+    between phases) against the oracle, teacher-forced over 12 steps."""
+    cfg = TINY_CFGS[name]
+    rng = np.random.default_rng(5)
+    prompt = rng.integers(0, cfg.vocab, 40).astype(np.int32)
+    _run_both(ctx, cfg, 24, prompt, 12, rng, "persistent " + name, fused=True)
+
+
+def test_persistent_step_greedy_chain(ctx):
+    """Greedy decode through the persistent kernel: graph replays == eager
+    launches == step by step, one launch per token, and the chain replayed
+    through the oracle; MoE models have no persistent plan."""
+    cfg = DEEP_CFG
+    rng = np.random.default_rng(9)
+    prompt = rng.integers(0, cfg.vocab, 60).astype(np.int32)
+    m = emx.Qwen3(ctx, cfg)
+    m.init_random(25)
+    m.fused = True
+    first = m.prefill(prompt)
+    many = m.decode(first, 20)
+    assert m.step_launches() == 1
+    m.reset()
+    assert m.prefill(prompt) == first
+    t, steps = first, []
+    for _ in range(20):
+        t = m.decode_step(t)
+        steps.append(t)
+    assert list(many) == steps
+    m.compiled = False
+    m.reset()
+    assert m.prefill(prompt) == first and list(m.decode(first, 20)) == list(many)
+    m.close()
+    chain = [first] + [int(x) for x in many]
+    ref = oracle_run(cfg, 25, prompt, chain[:-1])
+    noise = noise_floor(ref, oracle_run(cfg, 25, prompt, chain[:-1], reverse=True))
+    check_steps([(tk, ref_l) for tk, (_, ref_l) in zip(chain, ref)], ref, noise, "persistent greedy chain")
+    moe = emx.Qwen3(ctx, MOE_CFG)
+    assert not moe.fused
+    with pytest.raises(emx.EmxError):
+        moe.fused = True
+    moe.close()
 
 
 def test_greedy_decode_paths_agree(ctx):
@@ -199,7 +248,8 @@ def test_greedy_decode_paths_agree(ctx):
         t = m.decode_step(t)
         steps.append(t)
     assert list(many) == steps
-    assert m.step_launches() == 5 * cfg.layers + 1
+    # one persistent kernel per step, or five kernels per layer + the lm_head
+    assert m.step_launches() == (1 if m.fused else 5 * cfg.layers + 1)
     # the eager step (no graph, no programmatic launch) is the same computation
     m.compiled = False
     m.reset()
