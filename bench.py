@@ -190,7 +190,14 @@ def run_engine(args, cfg, rank, world, dist):
             print(json.dumps(dict(gemv_kernel_roofline(ctx, st, cfg, torch, hbm), peak_kind=kind)), flush=True)
         ctx.close()
         return
-    m = emx.Qwen3(ctx, cfg)
+    comm = None
+    if args.shard and world > 1:
+        # one model split across the ranks (tensor parallel for dense, expert
+        # parallel for MoE): the NCCL id travels over the bench's own group
+        obj = [emx.Comm.unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        comm = emx.Comm(ctx, obj[0], world, rank)
+    m = emx.Qwen3(ctx, cfg, comm)
     m.init_random(args.seed)
     m.compiled = not args.eager
     if args.per_op:
@@ -200,7 +207,9 @@ def run_engine(args, cfg, rank, world, dist):
         if dist is not None:
             dist.barrier()
 
-    rng = np.random.default_rng(args.seed + rank)
+    sharded = comm is not None
+    streams = 1 if sharded else world  # decode streams: one sharded model, or one replica per rank
+    rng = np.random.default_rng(args.seed + (0 if sharded else rank))
     prompt = rng.integers(0, cfg.vocab, args.prompt).astype(np.int32)
     ids = ctx.put(prompt)
     # ---- prefill tok/s (device-resident ids), a few repetitions
@@ -246,7 +255,7 @@ def run_engine(args, cfg, rank, world, dist):
         t = torch.tensor([ms], device=f"cuda:{dev}")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms_max = float(t.item())
-    value = world * args.steps / (ms_max / 1000.0)
+    value = streams * args.steps / (ms_max / 1000.0)
     # ---- end to end through the public API: host token in, host token out
     m.reset()
     tok = m.prefill(prompt)
@@ -262,22 +271,24 @@ def run_engine(args, cfg, rank, world, dist):
     if dist is not None:
         t = torch.tensor([e2e_s], device=f"cuda:{dev}")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e = world * n_e2e / float(t.item())
+        e2e = streams * n_e2e / float(t.item())
     # ---- roofline of the decode step (all GEMVs + attention + lm_head)
     hbm, _, kind = peaks()
     mean_ctx = start_ctx + (args.steps - 1) / 2.0
-    step_bytes = decode_bytes(cfg, mean_ctx)
-    achieved = step_bytes / (ms / args.steps / 1000.0) / 1e9
+    step_bytes = decode_bytes(cfg, mean_ctx) / (world if sharded else 1)  # per GPU
+    achieved = step_bytes / (ms_max / args.steps / 1000.0) / 1e9
     # ---- the dominant kernel alone: the gate_up GEMV shape over rotating copies (> L2)
     kern = gemv_kernel_roofline(ctx, st, cfg, torch, hbm)
     fused = m.fused
     m.close()
+    if comm is not None:
+        comm.close()
     if rank != 0:
         ctx.close()
         return
     line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": max(args.warmup, 3), "ms_per_step": ms_max / args.steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "bf16 activations, int4/int8 affine weights",
+            "scaling": "strong" if sharded else "weak", "vs_baseline": None, "dtype": "bf16 activations, int4/int8 affine weights",
             "data": "synthetic (seeded random-init weights and token ids)", "config": workload(args, cfg),
             "prefill_tok_s": pre, "decode_context": [start_ctx, start_ctx + args.steps],
             "roofline": dict(kern, peak_kind=kind),
@@ -289,6 +300,9 @@ def run_engine(args, cfg, rank, world, dist):
                     "api": "emx_qwen3_decode_step", "steps": n_e2e},
             "gpu_launches": launches * args.steps, "launches_per_step": launches,
             "clocks": clk.summary()}
+    if sharded:
+        line["config"]["parallelism"] = (f"expert parallel x{world}" if cfg.n_experts else f"tensor parallel x{world}")
+        line["step_roofline"]["scope"] += ", per GPU (1/world of the weights)"
     line["config"]["decode_path"] = ("one persistent kernel per decode step" if fused
                                      else "one kernel per operation, CUDA graph")
     if world == 1 and not args.no_cpu_baseline:
@@ -357,6 +371,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--eager", action="store_true",
                     help="decode without the CUDA graph (kernels in plain stream order): for profilers")
+    ap.add_argument("--shard", action="store_true",
+                    help="with N > 1: one model split across the N GPUs (tensor parallel for dense, expert "
+                         "parallel for MoE; NCCL all-reduce) instead of N replicas")
     ap.add_argument("--per-op", action="store_true",
                     help="decode with one kernel per operation instead of the persistent step kernel")
     ap.add_argument("--kernel-only", action="store_true",
