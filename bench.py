@@ -185,9 +185,15 @@ def run_engine(args, cfg, rank, world, dist):
     emx.lib().emx_ctx_stream(ctx.h, emx.C.byref(stream_ptr))
     st = torch.cuda.ExternalStream(stream_ptr.value, device=dev)
     if args.kernel_only:
-        hbm, _, kind = peaks()
+        hbm, tf, kind = peaks()
         if rank == 0:
-            print(json.dumps(dict(gemv_kernel_roofline(ctx, st, cfg, torch, hbm), peak_kind=kind)), flush=True)
+            if args.kernel_only == "gemm":
+                r = gemm_kernel_roofline(ctx, st, cfg, torch, tf)
+            elif args.kernel_only == "attn":
+                r = attn_kernel_roofline(ctx, st, cfg, torch, hbm)
+            else:
+                r = gemv_kernel_roofline(ctx, st, cfg, torch, hbm)
+            print(json.dumps(dict(r, peak_kind=kind)), flush=True)
         ctx.close()
         return
     comm = None
@@ -357,6 +363,86 @@ def gemv_kernel_roofline(ctx, st, cfg, torch, hbm):
             "us_per_launch": us, "bytes_per_launch": per, "traffic": None}
 
 
+def gemm_kernel_roofline(ctx, st, cfg, torch, tflops, M=2048):
+    """The prefill GEMM alone: emx_quantized_matmul on the gate|up shape
+    [2*inter, hidden] with M = 2048 rows of x (dequantize the weights into
+    scratch, then tc_gemm_kernel: TMA-fed tcgen05 MMAs into a TMEM
+    accumulator).  Algorithmic work: 2*M*N*K FLOP per call; the time is the
+    whole call (dequant + GEMM), CUDA events over 20 calls."""
+    import emx
+
+    N, K = 2 * cfg.inter, cfg.hidden
+    bits, gs = cfg.mlp_bits, cfg.mlp_group
+    wsz, ssz = N * K * bits // 8, N * (K // gs) * 2
+    w, s, b = ctx.alloc(wsz), ctx.alloc(ssz), ctx.alloc(ssz)
+    x, y = ctx.alloc(M * K * 2), ctx.alloc(M * N * 2)
+    L = emx.lib()
+    L.emx_memset(ctx.h, w.ptr, 0x5A, wsz)
+    L.emx_memset(ctx.h, s.ptr, 0x3C, ssz)
+    L.emx_memset(ctx.h, b.ptr, 0x00, ssz)
+    L.emx_memset(ctx.h, x.ptr, 0x3C, M * K * 2)
+    for _ in range(3):
+        ctx.quantized_matmul(x, w, s, b, M, N, K, gs, bits, out=y)
+    ctx.synchronize()
+    n = 20
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(n):
+        ctx.quantized_matmul(x, w, s, b, M, N, K, gs, bits, out=y)
+    e1.record(st)
+    e1.synchronize()
+    us = e0.elapsed_time(e1) * 1000.0 / n
+    for a in (w, s, b, x, y):
+        a.free()
+    ach = 2.0 * M * N * K / (us * 1e-6) / 1e12
+    return {"kernel": "emx_quantized_matmul = dequantize + tc_gemm_kernel (tcgen05, TMEM accumulator)",
+            "shape": [M, N, K], "bound": "tensor", "achieved": ach, "peak": tflops, "unit": "TFLOP/s",
+            "frac": ach / tflops, "us_per_call": us, "traffic": None}
+
+
+def attn_kernel_roofline(ctx, st, cfg, torch, hbm, L=8192):
+    """Decode attention alone (split-KV flash-decode, emx_sdpa_decode_noalloc)
+    at L valid rows of the static cache: 8 K/V cache copies (> L2) rotated
+    over 64 calls.  Algorithmic bytes per call: the L K and V rows of every
+    KV head + q in + the output."""
+    import numpy as np
+
+    import emx
+
+    nq, nkv, hd = cfg.n_q, cfg.n_kv, cfg.head_dim
+    cap = L
+    copies = 8
+    kv = [(ctx.alloc(nkv * cap * hd * 2), ctx.alloc(nkv * cap * hd * 2)) for _ in range(copies)]
+    for k, v in kv:
+        emx.lib().emx_memset(ctx.h, k.ptr, 0x3C, nkv * cap * hd * 2)
+        emx.lib().emx_memset(ctx.h, v.ptr, 0x3C, nkv * cap * hd * 2)
+    q = ctx.put(np.full(nq * hd, 0x3F80, np.uint16))
+    out = ctx.alloc(nq * hd * 2)
+    scale = 1.0 / float(np.sqrt(hd))
+    for i in range(4):
+        ctx.sdpa_decode_noalloc(q, kv[i][0], kv[i][1], out, nq, nkv, cap, hd, L, scale)
+    ctx.synchronize()
+    n = 64
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for i in range(n):
+        k, v = kv[i % copies]
+        ctx.sdpa_decode_noalloc(q, k, v, out, nq, nkv, cap, hd, L, scale)
+    e1.record(st)
+    e1.synchronize()
+    us = e0.elapsed_time(e1) * 1000.0 / n
+    for k, v in kv:
+        k.free()
+        v.free()
+    q.free()
+    out.free()
+    per = 2 * nkv * L * hd * 2 + 2 * nq * hd * 2
+    ach = per / (us * 1e-6) / 1e9
+    return {"kernel": "attn_decode_kernel (split-KV flash-decode)", "shape": {"n_q": nq, "n_kv": nkv, "rows": L},
+            "bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s", "frac": ach / hbm, "us_per_call": us,
+            "bytes_per_call": per, "traffic": None}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -376,8 +462,9 @@ def main():
                          "parallel for MoE; NCCL all-reduce) instead of N replicas")
     ap.add_argument("--per-op", action="store_true",
                     help="decode with one kernel per operation instead of the persistent step kernel")
-    ap.add_argument("--kernel-only", action="store_true",
-                    help="time only the dominant kernel (packed GEMV, gate|up shape) and print its roofline")
+    ap.add_argument("--kernel-only", nargs="?", const="gemv", default=None, choices=["gemv", "gemm", "attn"],
+                    help="time one kernel alone and print its roofline: the packed decode GEMV (gate|up shape, "
+                         "default), the prefill GEMM (gate|up shape, 2048 rows) or decode attention (8192 rows)")
     args = ap.parse_args()
 
     import emx

@@ -30,12 +30,22 @@ namespace emx {
 namespace {
 
 constexpr int kHD = 128;
-constexpr int kThreads = 128;
+constexpr int kWarps = 8;
+constexpr int kThreads = kWarps * 32;
 constexpr int kTile = 64;     // rows per K / V tile
-constexpr int kNBuf = 2;      // tiles in flight
+// tiles in flight (a buffer is refilled with the tile kNBuf ahead): three,
+// or two with eight q heads per KV head, whose larger per-warp partials
+// would otherwise keep the kernel from sharing an SM with a decode GEMV
+template <int HPG>
+constexpr int nbuf_for() {
+  return HPG >= 8 ? 2 : 3;
+}
 constexpr int kMinRows = 64;  // fewest rows a split is given
 constexpr int kTileBytes = kTile * kHD * 2;
-constexpr int kDynSmem = 128 + 2 * kNBuf * kTileBytes;
+template <int HPG>
+constexpr int dyn_smem() {
+  return 128 + 2 * nbuf_for<HPG>() * kTileBytes;
+}
 
 __device__ __forceinline__ int active_splits(int L, int grid) {
   const int s = (L + kMinRows - 1) / kMinRows;
@@ -49,6 +59,7 @@ __device__ __forceinline__ void split_range(int L, int splits, int split, int& p
 
 template <int HPG>
 __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const AttnDecodeArgs a) {
+  constexpr int kNBuf = nbuf_for<HPG>();
   extern __shared__ __align__(128) unsigned char dsm[];
   uint64_t* mbar = reinterpret_cast<uint64_t*>(dsm);
   bf16* kb = reinterpret_cast<bf16*>(dsm + 128);  // [kNBuf][kTile][kHD]
@@ -57,7 +68,7 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const AttnDecodeA
   __shared__ float qn[HPG + 1][kHD];   // normed q heads (+ k) before rope
   __shared__ float sc[HPG][kTile];     // scores -> probabilities for one tile
   __shared__ float stat_m[HPG], stat_l[HPG], stat_a[HPG];
-  __shared__ __align__(16) float sacc[4][HPG][kHD];  // per-warp partial outputs (float4 stores)
+  __shared__ __align__(16) float sacc[kWarps][HPG][kHD];  // per-warp partial outputs (float4 stores)
   __shared__ float swt[HPG][64];       // merge weights of the splits
   __shared__ float nwq[kHD], nwk[kHD], invf[kHD / 2];
   __shared__ float2 rcs[kHD / 2];  // (cos, sin) of this step's angles
@@ -173,7 +184,7 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const AttnDecodeA
     for (int i = tid; i < HPG * kHD; i += kThreads)
       qs[i / kHD][i % kHD] = __fmul_rn(bf2f(a.q_in[(size_t)kvh * HPG * kHD + i]), a.scale);
   }
-  for (int hh = warp; hh < nhead_prep; hh += 4) {
+  for (int hh = warp; hh < nhead_prep; hh += kWarps) {
     const bool is_k = hh == HPG;
     const bf16* src = is_k ? a.qkv + (size_t)a.nq * kHD + (size_t)kvh * kHD
                            : a.qkv + (size_t)(kvh * HPG + hh) * kHD;
@@ -263,15 +274,12 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const AttnDecodeA
       }
       __syncthreads();
     }
-    // QK^T: warp w scores rows [16w, 16w + 16) in batches of eight.  Each
-    // lane forms its 4-dim partial of all eight rows, then a transpose-
-    // reduction (xor 16, 8, 4: halve the rows a lane keeps; xor 2, 1: plain
-    // sums) leaves row k's score in lanes 4k..4k+3 — 9 shuffles per head for
-    // eight rows.
-#pragma unroll
-    for (int bt = 0; bt < 2; ++bt) {
-      const int r0 = warp * 16 + bt * 8;
-      if (r0 >= tn) break;
+    // QK^T: warp w scores rows [8w, 8w + 8).  Each lane forms its 4-dim
+    // partial of all eight rows, then a transpose-reduction (xor 16, 8, 4:
+    // halve the rows a lane keeps; xor 2, 1: plain sums) leaves row k's
+    // score in lanes 4k..4k+3 — 9 shuffles per head for eight rows.
+    if (warp * 8 < tn) {
+      const int r0 = warp * 8;
       float kf[8][4];
 #pragma unroll
       for (int r = 0; r < 8; ++r) {
@@ -324,7 +332,7 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const AttnDecodeA
     }
     __syncthreads();
     // online softmax update at tile granularity (one warp per head)
-    for (int h = warp; h < HPG; h += 4) {
+    for (int h = warp; h < HPG; h += kWarps) {
       float m = -INFINITY;
       for (int j = lane; j < tn; j += 32) m = fmaxf(m, sc[h][j]);
       m = warp_max(m);
@@ -346,15 +354,15 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const AttnDecodeA
       }
     }
     __syncthreads();
-    // P.V: warp w accumulates rows [16w, 16w + 16) into its 4 dims per lane
+    // P.V: warp w accumulates rows [8w, 8w + 8) into its 4 dims per lane
 #pragma unroll
     for (int h = 0; h < HPG; ++h) {
       const float al = stat_a[h];
 #pragma unroll
       for (int e = 0; e < 4; ++e) acc[h][e] *= al;
     }
-    const int rend = min(tn, warp * 16 + 16);
-    for (int jj = warp * 16; jj < rend; ++jj) {
+    const int rend = min(tn, warp * 8 + 8);
+    for (int jj = warp * 8; jj < rend; ++jj) {
       const uint2 vv = *reinterpret_cast<const uint2*>(vt + (size_t)jj * kHD + lane * 4);
       const float vf[4] = {__uint_as_float(vv.x << 16), __uint_as_float(vv.x & 0xffff0000u),
                            __uint_as_float(vv.y << 16), __uint_as_float(vv.y & 0xffff0000u)};
@@ -373,16 +381,23 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const AttnDecodeA
     }
   }
 
-  // ---- the four warps' row slots, then this split's partial ---------------
+  // ---- the warps' row slots, then this split's partial --------------------
 #pragma unroll
   for (int h = 0; h < HPG; ++h)
     *reinterpret_cast<float4*>(&sacc[warp][h][lane * 4]) = make_float4(acc[h][0], acc[h][1], acc[h][2], acc[h][3]);
   __syncthreads();
+  // the warps' row slots of one output element, in warp order
+  auto warp_total = [&](int h, int d) -> float {
+    float num = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) num += sacc[w][h][d];
+    return num;
+  };
   if (splits == 1) {
     // a single split needs no merge: normalise and store
     for (int i = tid; i < HPG * kHD; i += kThreads) {
       const int h = i / kHD, d = i % kHD;
-      const float num = sacc[0][h][d] + sacc[1][h][d] + sacc[2][h][d] + sacc[3][h][d];
+      const float num = warp_total(h, d);
       a.out[(size_t)(kvh * HPG + h) * kHD + d] = f2bf(__fmul_rn(num, __fdiv_rn(1.0f, stat_l[h])));
     }
     return;
@@ -391,7 +406,7 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const AttnDecodeA
   float* part = a.part + ((size_t)kvh * splits + split) * part_stride;
   for (int i = tid; i < HPG * kHD; i += kThreads) {
     const int h = i / kHD, d = i % kHD;
-    part[h * (kHD + 2) + 2 + d] = sacc[0][h][d] + sacc[1][h][d] + sacc[2][h][d] + sacc[3][h][d];
+    part[h * (kHD + 2) + 2 + d] = warp_total(h, d);
   }
   if (tid < HPG) {
     part[tid * (kHD + 2) + 0] = stat_m[tid];
@@ -407,7 +422,7 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const AttnDecodeA
   // every output element sums its splits with all loads in flight at once
   // (L2-coherent loads: the partials were written by other CTAs)
   const float* pb = a.part + (size_t)kvh * splits * part_stride;
-  for (int h = warp; h < HPG; h += 4) {
+  for (int h = warp; h < HPG; h += kWarps) {
     float ms = -INFINITY, ls = 0.f;
     if (lane < splits) {
       ms = __ldcg(pb + (size_t)lane * part_stride + h * (kHD + 2));
@@ -439,6 +454,7 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const AttnDecodeA
 template <int HPG>
 cudaError_t launch_t(const AttnDecodeArgs& a, cudaStream_t st, bool pdl) {
   auto kern = attn_decode_kernel<HPG>;
+  constexpr int kDynSmem = dyn_smem<HPG>();
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kDynSmem);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};

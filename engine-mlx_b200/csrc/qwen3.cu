@@ -242,11 +242,13 @@ GemvArgs gemv_base(const emx_qwen3* m, const QW& q) {
   return a;
 }
 
-// Shared memory a decode GEMV may claim: two CTAs per SM, so that the next
-// kernel of the step is resident (and streaming its weights) while this one
-// computes.  The lm_head streams far more than it can hold and its dequant
-// is the longest compute of the step: it runs two CTAs per SM.
-constexpr int kGemvBudget = 110 * 1024;
+// Shared memory a decode GEMV may claim: small enough that the next kernel of
+// the step (another GEMV, or decode attention with its 128 KB ring of K/V
+// tiles) is resident beside it (228 KB per SM, 1 KB reserved per CTA) and
+// streams its weights while this one computes.  The lm_head streams far more
+// than it can hold and its dequant is the longest compute of the step: it
+// runs two CTAs per SM.
+constexpr int kGemvBudget = 94 * 1024;
 
 int plan(emx_qwen3* m, const QW& q, int epi, int x_slots, int n_rows_override, PgemvPlan* p, int ctas_per_sm = 1) {
   const int N = n_rows_override > 0 ? n_rows_override : q.N;
