@@ -184,6 +184,26 @@ def run_engine(args, cfg, rank, world, dist):
     stream_ptr = emx.C.c_void_p()
     emx.lib().emx_ctx_stream(ctx.h, emx.C.byref(stream_ptr))
     st = torch.cuda.ExternalStream(stream_ptr.value, device=dev)
+    if args.kernel_only == "prefill":
+        # one warm prefill, then one timed: the launch list of a whole prefill
+        m = emx.Qwen3(ctx, cfg)
+        m.init_random(args.seed)
+        ids = ctx.put(np.random.default_rng(args.seed).integers(0, cfg.vocab, args.prompt).astype(np.int32))
+        m.prefill_device(ids, args.prompt)
+        m.reset()
+        ctx.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        m.prefill_device(ids, args.prompt)
+        e1.record(st)
+        e1.synchronize()
+        ms = e0.elapsed_time(e1)
+        if rank == 0:
+            print(json.dumps({"prefill_tokens": args.prompt, "ms": ms, "tok_s": args.prompt / (ms / 1000.0)}),
+                  flush=True)
+        m.close()
+        ctx.close()
+        return
     if args.kernel_only:
         hbm, tf, kind = peaks()
         if rank == 0:
@@ -462,9 +482,11 @@ def main():
                          "parallel for MoE; NCCL all-reduce) instead of N replicas")
     ap.add_argument("--per-op", action="store_true",
                     help="decode with one kernel per operation instead of the persistent step kernel")
-    ap.add_argument("--kernel-only", nargs="?", const="gemv", default=None, choices=["gemv", "gemm", "attn"],
+    ap.add_argument("--kernel-only", nargs="?", const="gemv", default=None,
+                    choices=["gemv", "gemm", "attn", "prefill"],
                     help="time one kernel alone and print its roofline: the packed decode GEMV (gate|up shape, "
-                         "default), the prefill GEMM (gate|up shape, 2048 rows) or decode attention (8192 rows)")
+                         "default), the prefill GEMM (gate|up shape, 2048 rows), decode attention (8192 rows), "
+                         "or one whole prefill of --prompt tokens")
     args = ap.parse_args()
 
     import emx

@@ -11,6 +11,10 @@
 // m16n8k16 tensor-core fragments with the online softmax kept in registers.
 #include "attn_prefill.cuh"
 
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
 namespace emx {
 
 namespace {
@@ -220,11 +224,430 @@ __global__ void __launch_bounds__(kThreads) attn_prefill_kernel(const AttnPrefil
   }
 }
 
+// ---------------------------------------------------------------------------
+// tcgen05 flash attention: one CTA per (128-query tile, q head), ten warps.
+//   warp 0 (one thread)  TMA: the Q tile once, then K and V tiles of 128 keys
+//                        into a two-stage ring (128-byte swizzle, 3-D tensor
+//                        maps whose row extent is T: rows past the prompt
+//                        read as zeros);
+//   warp 1 (one thread)  MMA: S_j = Q.K_j^T (M = N = 128, eight K = 16
+//                        steps) into one of two tensor-memory S buffers,
+//                        issued before O += P_{j-1}.V_{j-1} so that the tensor
+//                        pipe computes the next scores while the softmax
+//                        warps work; P from shared memory, V as an MN-major
+//                        operand; owns the 512-column TMEM allocation;
+//   warps 2-9            softmax: two threads per query row (warps w and w+4
+//                        share a TMEM lane quadrant), each with 64 of the 128
+//                        columns; it reads its S half-row with tcgen05.ld,
+//                        masks (the diagonal tile only), keeps the running max in
+//                        the log2 domain and writes P as bf16 hi + lo parts
+//                        (P.V keeps ~16 significant bits of each
+//                        probability) to shared memory.  The max used for the
+//                        exponentials only moves when the tile max exceeds it
+//                        by more than 8 (O and l are then rescaled in place),
+//                        so P <= 2^8 and the final O / l is exact whatever
+//                        max was used.
+constexpr int kTBM = 128, kTBN = 128;
+constexpr int kTcThreads = 320;
+constexpr int kBlk = kTBM * 64 * 2;  // 128 rows x 64 columns (128 B rows, swizzled): 16 KB
+constexpr int kTileB = 2 * kBlk;     // 128 rows x 128 columns
+constexpr int kOffK = kTileB;        // Q | (K V) x 2 | P hi | P lo | barriers
+constexpr int kOffP = kOffK + 4 * kTileB;
+constexpr int kOffBar = kOffP + 2 * kTileB;
+constexpr int kOffX = kOffBar + 128;  // softmax exchange: [2 halves][128 rows] floats
+constexpr int kTcSmem = 1024 + kOffX + 2 * kTBM * 4;
+constexpr float kRescale = 8.0f;     // log2 growth allowed before O is rescaled
+constexpr uint32_t kTmemCols = 512;  // S0 [0,128), O [128,256), S1 [256,384)
+
+__device__ __forceinline__ uint64_t desc_kmajor(const void* p) {
+  const uint64_t a = (smem_u32(p) >> 4) & 0x3FFFu;
+  return a | (1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
+}
+
+// MN-major operand with 128-byte swizzle: 64-element MN blocks kBlk bytes
+// apart (LBO), 8-row K groups 1024 bytes apart (SBO).
+__device__ __forceinline__ uint64_t desc_mnmajor(const void* p) {
+  const uint64_t a = (smem_u32(p) >> 4) & 0x3FFFu;
+  return a | ((uint64_t)(kBlk >> 4) << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
+}
+
+// kind::f16, D fp32, A/B bf16, M = N = 128; A K-major; B K-major or MN-major.
+constexpr uint32_t idesc_128(bool b_mn) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((b_mn ? 1u : 0u) << 16) | ((uint32_t)(128 >> 3) << 17) |
+         ((uint32_t)(128 >> 4) << 24);
+}
+
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int c0, int c1, int c2, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void umma(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tfence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tfence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tst32(uint32_t taddr, const float (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])),
+      "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])),
+      "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+      "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
+      "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
+      "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+      "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
+      "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
+      "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+      : "memory");
+}
+
+// 2^x by the hardware's base-2 exponential (softmax weights; their bf16
+// hi + lo split keeps ~16 bits, well inside its accuracy).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ void tmem_wait_ld_() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_wait_st_() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+__global__ void __launch_bounds__(kTcThreads, 1)
+    attn_prefill_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                           const __grid_constant__ CUtensorMap tv, const AttnPrefillArgs a, int* status) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  unsigned char* sQ = smem;
+  unsigned char* sP = smem + kOffP;  // P hi tile, then P lo tile
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + kOffBar);
+  uint64_t* q_full = bar + 0;
+  uint64_t* kv_full = bar + 1;   // [2] per K/V stage
+  uint64_t* kv_empty = bar + 3;  // [2]
+  uint64_t* s_full = bar + 5;    // [2] per S buffer
+  uint64_t* s_free = bar + 7;    // [2]
+  uint64_t* p_full = bar + 9;
+  uint64_t* pv_done = bar + 11;
+  uint64_t* o_done = bar + 12;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 13);
+  int* issued_slot = reinterpret_cast<int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qt = gridDim.x - 1 - blockIdx.x;  // the longest rows first
+  const int h = blockIdx.y;
+  const int kvh = h / (a.nq / a.nkv);
+  const int nt = qt + 1;  // key tiles at or before the diagonal
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+      mbar_init(&s_full[s], 1);
+      mbar_init(&s_free[s], 256);
+    }
+    mbar_init(p_full, 256);
+    mbar_init(pv_done, 1);
+    mbar_init(o_done, 1);
+    *issued_slot = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tfence_before();
+  __syncthreads();
+  tfence_after();
+  const uint32_t tmem = *tmem_slot;
+  auto s_col = [](int b) -> uint32_t { return b ? 256u : 0u; };
+
+  if (warp == 0 && lane == 0) {
+    // ---- TMA producer
+    mbar_arrive_expect_tx(q_full, (uint32_t)kTileB);
+    tma_load_3d(sQ, &tq, 0, qt * kTBM, h, q_full);
+    tma_load_3d(sQ + kBlk, &tq, 64, qt * kTBM, h, q_full);
+    int issued = 0;
+    for (int j = 0; j < nt; ++j) {
+      const int s = j & 1;
+      if (j >= 2 && !mbar_wait_bounded(&kv_empty[s], (uint32_t)(((j >> 1) - 1) & 1), status)) break;
+      unsigned char* K = smem + kOffK + s * 2 * kTileB;
+      unsigned char* V = K + kTileB;
+      mbar_arrive_expect_tx(&kv_full[s], (uint32_t)(2 * kTileB));
+      tma_load_3d(K, &tk, 0, j * kTBN, kvh, &kv_full[s]);
+      tma_load_3d(K + kBlk, &tk, 64, j * kTBN, kvh, &kv_full[s]);
+      tma_load_3d(V, &tv, 0, j * kTBN, kvh, &kv_full[s]);
+      tma_load_3d(V + kBlk, &tv, 64, j * kTBN, kvh, &kv_full[s]);
+      issued = j + 1;
+    }
+    *issued_slot = issued;
+  } else if (warp == 1 && lane == 0) {
+    // ---- MMA issuer: S_0, then per tile j: S_{j+1} (if any), O += P_j.V_j
+    constexpr uint32_t id_s = idesc_128(false), id_pv = idesc_128(true);
+    auto issue_s = [&](int j) -> bool {
+      const int b = j & 1;
+      if (!mbar_wait_bounded(&kv_full[b], (uint32_t)((j >> 1) & 1), status)) return false;
+      if (j >= 2 && !mbar_wait_bounded(&s_free[b], (uint32_t)(((j >> 1) - 1) & 1), status)) return false;
+      tfence_after();
+      const unsigned char* K = smem + kOffK + b * 2 * kTileB;
+#pragma unroll
+      for (int k = 0; k < 8; ++k)  // 16 head dims per step: block k/4, +32 B per step inside it
+        umma(tmem + s_col(b), desc_kmajor(sQ + (k >> 2) * kBlk) + 2 * (k & 3),
+             desc_kmajor(K + (k >> 2) * kBlk) + 2 * (k & 3), id_s, k > 0 ? 1u : 0u);
+      umma_commit(&s_full[b]);
+      return true;
+    };
+    bool ok = mbar_wait_bounded(q_full, 0u, status) && issue_s(0);
+    for (int j = 0; ok && j < nt; ++j) {
+      if (j + 1 < nt && !issue_s(j + 1)) break;
+      const int b = j & 1;
+      if (!mbar_wait_bounded(p_full, (uint32_t)(j & 1), status)) break;
+      tfence_after();
+      const unsigned char* V = smem + kOffK + b * 2 * kTileB + kTileB;
+#pragma unroll
+      for (int part = 0; part < 2; ++part) {
+        const unsigned char* P = sP + part * kTileB;
+#pragma unroll
+        for (int k = 0; k < 8; ++k)  // 16 keys per step: P block k/4 (+32 B), V rows 16k.. (+2 KB)
+          umma(tmem + 128, desc_kmajor(P + (k >> 2) * kBlk) + 2 * (k & 3), desc_mnmajor(V + k * 2048), id_pv,
+               (j > 0 || part > 0 || k > 0) ? 1u : 0u);
+      }
+      umma_commit(&kv_empty[b]);
+      umma_commit(pv_done);
+    }
+    umma_commit(o_done);
+  } else if (warp >= 2) {
+    // ---- softmax: query row r of the tile, key (and output) columns
+    //      [64 hf, 64 hf + 64); the two threads of a row meet at a named
+    //      barrier of their two warps to combine the tile max
+    const int quad = warp & 3;
+    const int hf = (warp - 2) >> 2;
+    const int r = quad * 32 + lane;
+    const int qrow = qt * kTBM + r;
+    const bool valid_q = qrow < a.T;
+    const uint32_t tl = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(hf * 64);
+    const uint32_t tO = tl + 128;
+    const float sl2 = a.scale * 1.4426950408889634f;
+    float* xch = reinterpret_cast<float*>(smem + kOffX);  // [half][row]
+    auto pair_sync = [&]() { asm volatile("bar.sync %0, 64;" ::"r"(1 + quad) : "memory"); };
+    // barrier of the pair that also ANDs a flag over its 64 threads: both
+    // threads of a row leave the tile loop together (a lone thread left at a
+    // named barrier would wait for ever)
+    auto pair_all = [&](bool v) -> bool {
+      uint32_t res;
+      asm volatile(
+          "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.and.pred q, %2, 64, p;\n\t"
+          "selp.u32 %0, 1, 0, q;\n\t}"
+          : "=r"(res)
+          : "r"((uint32_t)v), "r"(1 + quad)
+          : "memory");
+      return res != 0;
+    };
+    float m_used = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nt; ++j) {
+      const int b = j & 1;
+      ok = mbar_wait_bounded(&s_full[b], (uint32_t)((j >> 1) & 1), status) && ok;
+      tfence_after();
+      float s[64];
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        float v[32];
+        tld32(tl + s_col(b) + c * 32, v);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) s[c * 32 + i] = v[i];
+      }
+      tmem_wait_ld_();
+      tfence_before();
+      mbar_arrive(&s_free[b]);
+      const int kv0 = j * kTBN + hf * 64;
+      float mx = -INFINITY;
+      if (j + 1 < nt) {  // below the diagonal every key is visible
+#pragma unroll
+        for (int c = 0; c < 64; ++c) {
+          s[c] = valid_q ? s[c] * sl2 : -INFINITY;
+          mx = fmaxf(mx, s[c]);
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < 64; ++c) {
+          const bool vis = valid_q && kv0 + c <= qrow;
+          s[c] = vis ? s[c] * sl2 : -INFINITY;
+          mx = fmaxf(mx, s[c]);
+        }
+      }
+      xch[hf * kTBM + r] = mx;
+      if (!pair_all(ok)) {
+        ok = false;
+        break;
+      }
+      mx = fmaxf(mx, xch[(hf ^ 1) * kTBM + r]);
+      pair_sync();  // both read before either writes the next tile's max
+      // the O update of tile j-1 has read P and written O before either is touched
+      if (j > 0) ok = mbar_wait_bounded(pv_done, (uint32_t)((j - 1) & 1), status) && ok;
+      tfence_after();
+      if (mx != -INFINITY && mx > m_used + kRescale) {
+        const float alpha = m_used == -INFINITY ? 0.f : ex2_approx(m_used - mx);
+        if (j > 0 && m_used != -INFINITY) {
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            float v[32];
+            tld32(tO + c * 32, v);
+            tmem_wait_ld_();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] *= alpha;
+            tst32(tO + c * 32, v);
+          }
+          tmem_wait_st_();
+        }
+        l *= alpha;
+        m_used = mx;
+      }
+      // P = exp2(s - m_used) as bf16 hi + lo: keys [64 hf, 64 hf + 64) of row
+      // r are swizzle block hf of the K-major P tiles
+      unsigned char* Pr = sP + hf * kBlk + (r >> 3) * 1024 + (r & 7) * 128;
+#pragma unroll
+      for (int ch = 0; ch < 8; ++ch) {  // 16-byte chunk: 8 keys
+        uint32_t hi[4], lo[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int c = ch * 8 + 2 * e;
+          const float p0 = s[c] == -INFINITY ? 0.f : ex2_approx(s[c] - m_used);
+          const float p1 = s[c + 1] == -INFINITY ? 0.f : ex2_approx(s[c + 1] - m_used);
+          l += p0;
+          l += p1;
+          const float h0 = bfround(p0), h1 = bfround(p1);
+          hi[e] = pack_bf16(h0, h1);
+          lo[e] = pack_bf16(p0 - h0, p1 - h1);
+        }
+        const int off = ((ch ^ (r & 7)) << 4);
+        *reinterpret_cast<uint4*>(Pr + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+        *reinterpret_cast<uint4*>(Pr + kTileB + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+      }
+      fence_proxy_async();
+      tfence_before();
+      mbar_arrive(p_full);
+    }
+    // ---- O / l (the two halves' sums combined), stored as bf16
+    xch[hf * kTBM + r] = l;
+    pair_sync();
+    const float lt = l + xch[(hf ^ 1) * kTBM + r];
+    const bool okd = mbar_wait_bounded(o_done, 0u, status);
+    tfence_after();
+    const float inv = lt > 0.f ? 1.f / lt : 0.f;
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      float v[32];
+      tld32(tO + c * 32, v);
+      tmem_wait_ld_();
+      if (!ok || !okd || !valid_q) continue;
+      bf16* dst = a.out + (a.out_tnd ? (size_t)qrow * a.nq * kD + (size_t)h * kD : ((size_t)h * a.T + qrow) * kD) +
+                  hf * 64 + c * 32;
+#pragma unroll
+      for (int q4 = 0; q4 < 4; ++q4)
+        reinterpret_cast<uint4*>(dst)[q4] = make_uint4(
+            pack_bf16(v[8 * q4 + 0] * inv, v[8 * q4 + 1] * inv), pack_bf16(v[8 * q4 + 2] * inv, v[8 * q4 + 3] * inv),
+            pack_bf16(v[8 * q4 + 4] * inv, v[8 * q4 + 5] * inv), pack_bf16(v[8 * q4 + 6] * inv, v[8 * q4 + 7] * inv));
+    }
+  }
+  tfence_before();
+  __syncthreads();
+  if (warp == 0 && lane == 0) {
+    // the last copies issued into each stage have landed before the CTA exits
+    const int issued = *issued_slot;
+    mbar_wait_bounded(q_full, 0u, status);
+    for (int j = issued > 2 ? issued - 2 : 0; j < issued; ++j)
+      mbar_wait_bounded(&kv_full[j & 1], (uint32_t)((j >> 1) & 1), status);
+  }
+  if (warp == 1) {
+    tfence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+  }
+}
+
 }  // namespace
 
-cudaError_t attn_prefill_launch(const AttnPrefillArgs& a, cudaStream_t st) {
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode3 = nullptr;
+std::once_flag g_encode3_once;
+
+// [heads][rows][128] bf16 with `head_stride` bytes between heads; boxes of
+// 64 columns x 128 rows of one head, 128-byte swizzle; rows past `rows` read
+// as zeros.
+cudaError_t encode_rows(CUtensorMap* map, const void* base, uint64_t rows, uint64_t heads, uint64_t head_stride) {
+  std::call_once(g_encode3_once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_encode3 = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  });
+  if (!g_encode3) return cudaErrorNotSupported;
+  const cuuint64_t dims[3] = {(cuuint64_t)kD, rows, heads};
+  const cuuint64_t strides[2] = {(cuuint64_t)kD * 2, head_stride};
+  const cuuint32_t box[3] = {64, (cuuint32_t)kTBM, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = g_encode3(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box,
+                               estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+}  // namespace
+
+cudaError_t attn_prefill_launch(const AttnPrefillArgs& a, cudaStream_t st, int* status) {
   if (a.head_dim != kD || a.nkv <= 0 || a.nq % a.nkv) return cudaErrorInvalidValue;
   if (a.T <= 0) return cudaSuccess;
+  if (((reinterpret_cast<uintptr_t>(a.q) | reinterpret_cast<uintptr_t>(a.kc) | reinterpret_cast<uintptr_t>(a.vc)) &
+       15) == 0) {
+    CUtensorMap tq, tk, tv;
+    cudaError_t e = encode_rows(&tq, a.q, (uint64_t)a.T, (uint64_t)a.nq, (uint64_t)a.T * kD * 2);
+    if (e == cudaSuccess)
+      e = encode_rows(&tk, a.kc + (size_t)a.offset * kD, (uint64_t)a.T, (uint64_t)a.nkv, (uint64_t)a.cap * kD * 2);
+    if (e == cudaSuccess)
+      e = encode_rows(&tv, a.vc + (size_t)a.offset * kD, (uint64_t)a.T, (uint64_t)a.nkv, (uint64_t)a.cap * kD * 2);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(attn_prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem);
+    if (e != cudaSuccess) return e;
+    dim3 grid((a.T + kTBM - 1) / kTBM, a.nq);
+    attn_prefill_tc_kernel<<<grid, kTcThreads, kTcSmem, st>>>(tq, tk, tv, a, status);
+    return cudaGetLastError();
+  }
   const int smem = (kBM + 4 * kBN) * kD * 2;
   cudaError_t e = cudaFuncSetAttribute(attn_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;

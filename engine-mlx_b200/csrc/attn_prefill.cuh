@@ -15,6 +15,7 @@ struct AttnPrefillArgs {
   int out_tnd;
 };
 
-cudaError_t attn_prefill_launch(const AttnPrefillArgs& a, cudaStream_t st);
+// `status`: device status word for bounded-wait timeouts (may be null).
+cudaError_t attn_prefill_launch(const AttnPrefillArgs& a, cudaStream_t st, int* status = nullptr);
 
 }  // namespace emx

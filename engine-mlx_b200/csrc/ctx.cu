@@ -446,7 +446,7 @@ int emx_sdpa_causal(emx_ctx* c, const void* q, const void* k, const void* v, voi
   a.scale = scale;
   a.out = static_cast<bf16*>(out);
   a.out_tnd = out_tnd;
-  EMX_CHECK_CUDA(attn_prefill_launch(a, c->stream), "emx_sdpa_causal");
+  EMX_CHECK_CUDA(attn_prefill_launch(a, c->stream, c->status), "emx_sdpa_causal");
   return EMX_OK;
 }
 

@@ -105,10 +105,6 @@ __device__ __forceinline__ float part_sum(float v, float* scratch, int tid, int 
   return r;
 }
 
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-
 // Bounded wait that also gives up at once when another warp has aborted.
 __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* status) {
   if (mbar_try_wait(bar, parity)) return true;

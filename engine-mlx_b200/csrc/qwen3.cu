@@ -890,7 +890,7 @@ int prefill_impl(emx_qwen3* m, const int32_t* ids_dev, int T) {
     aa.scale = 1.0f / sqrtf((float)hd);
     aa.out = m->pattn;
     aa.out_tnd = 1;
-    if ((e = attn_prefill_launch(aa, st)) != cudaSuccess) return fail_cuda(e, "prefill attention");
+    if ((e = attn_prefill_launch(aa, st, m->ctx->status)) != cudaSuccess) return fail_cuda(e, "prefill attention");
     // row-split o_proj under TP: fp32 partials, sum over ranks, then the residual add
     auto row_parallel = [&](const QW& q, const bf16* x) -> int {
       if (!m->tp) return gemm(m, q, x, T, kGemmResid, m->px, m->px);

@@ -243,6 +243,19 @@ def test_sdpa_causal(ctx, tnd):
     assert_close(got, OPS["att_y"], what="sdpa causal")
 
 
+@pytest.mark.parametrize("T,nq,nkv", [(128, 2, 1), (300, 4, 2), (1000, 4, 1)])
+def test_sdpa_causal_tiles(ctx, T, nq, nkv):
+    """Several 128-row query and key tiles (diagonal, full and ragged) against the oracle."""
+    rng = np.random.default_rng(T)
+    q = oracle.to_bf16(rng.standard_normal((nq, T, 128)).astype(np.float32))
+    k = oracle.to_bf16(rng.standard_normal((nkv, T, 128)).astype(np.float32))
+    v = oracle.to_bf16(rng.standard_normal((nkv, T, 128)).astype(np.float32))
+    sc = np.float32(1 / np.sqrt(128))
+    ref = oracle.sdpa(q, k, v, nkv, T, T, sc, True)
+    got = ctx.sdpa_causal(ctx.put(q), ctx.put(k), ctx.put(v), nq, nkv, T, 128, float(sc)).read(np.uint16, (nq, T, 128))
+    assert_close(got, ref, what=f"sdpa causal T={T}")
+
+
 def test_sdpa_decode(ctx):
     q, kc, vc = OPS["dec_q"], OPS["dec_k"], OPS["dec_v"]
     L = int(OPS["dec_len"][0])
