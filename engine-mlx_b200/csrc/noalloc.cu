@@ -89,7 +89,7 @@ extern "C" int emx_sdpa_decode_noalloc(emx_ctx* c, const void* q, const void* kc
   NA_REQUIRE((size_t)nkv * sizeof(unsigned) <= kTicketBytes,
              "emx_sdpa_decode_noalloc: n_kv %d exceeds the %zu tickets of the static scratch", nkv,
              kTicketBytes / sizeof(unsigned));
-  const int splits = attn_decode_splits(nkv, c->num_sms);
+  const int splits = attn_decode_splits(nkv, c->num_sms, nq / nkv);
   const size_t part = (size_t)nkv * splits * (nq / nkv) * (hd + 2) * sizeof(float);
   NA_REQUIRE(part <= kNoAllocScratchBytes - kTicketBytes,
              "emx_sdpa_decode_noalloc: n_q %d x %d splits needs %zu bytes of partials; the static scratch holds %zu",

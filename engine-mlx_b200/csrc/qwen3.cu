@@ -243,9 +243,9 @@ GemvArgs gemv_base(const emx_qwen3* m, const QW& q) {
 }
 
 // Shared memory a decode GEMV may claim: small enough that the next kernel of
-// the step (another GEMV, or decode attention with its 128 KB ring of K/V
-// tiles) is resident beside it (228 KB per SM, 1 KB reserved per CTA) and
-// streams its weights while this one computes.  The lm_head streams far more
+// the step (another GEMV, or decode attention with its 64 KB ring of K/V
+// tiles and up to 48 KB of partials) is resident beside it (228 KB per SM,
+// 1 KB reserved per CTA) and streams its inputs while this one computes.  The lm_head streams far more
 // than it can hold and its dequant is the longest compute of the step: it
 // runs two CTAs per SM.
 constexpr int kGemvBudget = 94 * 1024;
@@ -539,7 +539,7 @@ int build(emx_qwen3* m) {
   if ((rc = alloc_t(m, 1024, &m->am_val)) || (rc = alloc_t(m, 1024, &m->am_idx)) ||
       (rc = alloc_t(m, 16, &m->am_ticket)))
     return rc;
-  m->attn_splits = attn_decode_splits(m->nkv, m->ctx->num_sms);
+  m->attn_splits = attn_decode_splits(m->nkv, m->ctx->num_sms, m->nq / m->nkv);
   const int hpg = m->nq / m->nkv;
   if ((rc = alloc_t(m, (size_t)m->nkv * m->attn_splits * hpg * (hd + 2), &m->attn_part)) ||
       (rc = alloc_t(m, (size_t)m->nkv, &m->attn_ticket)))
