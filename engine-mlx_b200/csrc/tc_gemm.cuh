@@ -27,6 +27,13 @@ struct TcGemmArgs {
   const bf16* res;  // [M, N]
   float* yf;        // [M, N]
   int* status;
+  // tc_qgemm: the weights as MLX affine codes, group size 64
+  const uint32_t* wq;  // [N_w, K*bits/32]
+  const bf16* ws;      // [N_w, K/64] scales
+  const bf16* wb;      // [N_w, K/64] biases
+  int bits;            // 4 or 8
+  float* part;         // split-K workspace (tc_qgemm_splits bytes) or nullptr
+  int ksplit;          // splits of K when part is set
 };
 
 // True when the shape is supported (K % 64 == 0, N % 32 == 0, 16-byte
@@ -34,5 +41,16 @@ struct TcGemmArgs {
 bool tc_gemm_supported(const TcGemmArgs& a);
 // Enqueues the GEMM; returns cudaSuccess or the launch / encode error.
 cudaError_t tc_gemm_launch(const TcGemmArgs& a, int num_sms, cudaStream_t st);
+
+// The same GEMM with W given as MLX affine codes (group size 64): the kernel
+// dequantises each k-block of its weight tile into shared memory, bit-exactly
+// as the dequant pass would, so no bf16 copy of W is written.
+bool tc_qgemm_supported(const TcGemmArgs& a);
+// Splits of K that fill the machine when the output has fewer tiles than SMs
+// (1 otherwise) and the workspace they need; with part / ksplit set, the
+// launch writes fp32 partials and a second kernel sums them in split order
+// and applies the output step.
+int tc_qgemm_splits(const TcGemmArgs& a, int num_sms, size_t* part_bytes);
+cudaError_t tc_qgemm_launch(const TcGemmArgs& a, int num_sms, cudaStream_t st);
 
 }  // namespace emx
