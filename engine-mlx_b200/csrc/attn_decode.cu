@@ -94,7 +94,6 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const AttnDecodeA
     for (int i = tid; i < kHD / 2; i += kThreads) invf[i] = a.inv_freq[i];
   }
   __syncthreads();
-  pdl_trigger();
 
   // Tile t of the current plan: rows [p0 + 64t, ...) of this split, minus
   // the new row p when this kernel computes it (never copied); buffer
@@ -143,6 +142,11 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const AttnDecodeA
     }
   }
   pdl_wait();
+  // the next kernel may launch once this one's inputs are final: one kernel
+  // ahead streams its weights beside this one, while an earlier trigger lets
+  // the chain run several kernels ahead and the block scheduler then stacks
+  // two CTAs of one launch on an SM while others hold none
+  pdl_trigger();
 
   const int p = a.pos ? *a.pos : a.pos_host;
   const bool bad = p < 0 || p >= a.cap;

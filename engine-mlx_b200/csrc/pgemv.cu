@@ -81,7 +81,6 @@ __global__ void __launch_bounds__(kThreads, 2) pgemv_kernel(const GemvArgs a, co
     fence_mbar_init();
   }
   __syncthreads();
-  pdl_trigger();
 
   const unsigned char* wsrc = reinterpret_cast<const unsigned char*>(a.w);
   auto src_of = [&](int lb) -> const unsigned char* {
@@ -125,6 +124,11 @@ __global__ void __launch_bounds__(kThreads, 2) pgemv_kernel(const GemvArgs a, co
 
   // ---- wait for the producer of x (the previous kernel) -----------------
   pdl_wait();
+  // the next kernel may launch once this one's inputs are final: one kernel
+  // ahead streams its weights beside this one, while an earlier trigger lets
+  // the chain run several kernels ahead and the block scheduler then stacks
+  // two CTAs of one launch on an SM while others hold none
+  pdl_trigger();
 
   if (gather) {
     lb_total = min(*a.n_slots * lps, geo.lb_total);
@@ -182,6 +186,10 @@ __global__ void __launch_bounds__(kThreads, 2) pgemv_kernel(const GemvArgs a, co
   __syncthreads();
 
   pg_epilogue(a, geo, sm.red, lb0, lb1, tid, kThreads, res_early, res_pre, best_v, best_i);
+  if (a.epi == kEpiF32 && a.peer) {
+    __shared__ unsigned published;
+    pg_peer_publish<SyncCta>(a, tid, &published);
+  }
 
   if (a.epi == kEpiArgmax) {
     __shared__ float wv[kConsumers + 1];

@@ -140,8 +140,31 @@ __device__ __forceinline__ uint4 pack8exact(const float (&f)[8]) {
   return r;
 }
 
+__device__ __forceinline__ unsigned ld_acquire_sys_u32(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_release_sys_u32(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// In rank `dst`'s region: the slot holding rank `src`'s partial of reduction e.
+__device__ __forceinline__ float* peer_slot(const PeerX& P, int dst, unsigned e, int src) {
+  return reinterpret_cast<float*>(P.base[dst] + kPeerHeader +
+                                  ((size_t)(e & 1u) * kPeerMaxRanks + src) * kPeerSlotFloats * 4);
+}
+
+// In rank `dst`'s region: rank `src`'s flag (the last reduction it stored there).
+__device__ __forceinline__ unsigned* peer_flag(const PeerX& P, int dst, int src) {
+  return reinterpret_cast<unsigned*>(P.base[dst]) + src;
+}
+
 // The pre-norm source values of elements [8c, 8c+8) (bf16 values as float).
-__device__ __forceinline__ void src8(const GemvArgs& a, int c, int tok, float (&v)[8]) {
+// `psrc` (kProAddNorm with a peer sum): the world ranks' fp32 partials.
+__device__ __forceinline__ void src8(const GemvArgs& a, int c, int tok, float (&v)[8],
+                                     const float* const* psrc = nullptr, int pworld = 0) {
   const int k0 = c * 8;
   if (a.pro == kProEmbedNorm) {
     const int per = 32 / a.emb_bits;
@@ -171,6 +194,19 @@ __device__ __forceinline__ void src8(const GemvArgs& a, int c, int tok, float (&
 #pragma unroll
         for (int e = 0; e < 8; ++e) add[e] = __fadd_rn(add[e], __fmul_rn(y[e], w));
       }
+    } else if (psrc) {
+      // the ranks' partials summed in rank order (the same bits on every rank),
+      // then rounded like the unsharded projection's bf16 output
+#pragma unroll
+      for (int e = 0; e < 8; ++e) add[e] = 0.f;
+      for (int r = 0; r < pworld; ++r) {
+        const float4 p0 = __ldcg(reinterpret_cast<const float4*>(psrc[r] + k0));
+        const float4 p1 = __ldcg(reinterpret_cast<const float4*>(psrc[r] + k0 + 4));
+        add[0] += p0.x, add[1] += p0.y, add[2] += p0.z, add[3] += p0.w;
+        add[4] += p1.x, add[5] += p1.y, add[6] += p1.z, add[7] += p1.w;
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) add[e] = bfround(add[e]);
     } else {
       const float4 p0 = *reinterpret_cast<const float4*>(a.add_f32 + k0);
       const float4 p1 = *reinterpret_cast<const float4*>(a.add_f32 + k0 + 4);
@@ -279,13 +315,38 @@ __device__ __forceinline__ void pg_prologue(const GemvArgs& a, const PGeom& geo,
     const int groups = a.norm_groups > 0 ? a.norm_groups : 1;
     const int gd = K / groups;
     const bool store = (a.pro == kProEmbedNorm || a.pro == kProAddNorm) && lead && a.x_out;
+    // a peer sum: wait until every rank has published reduction e (bounded),
+    // then read the ranks' slots
+    const float* psrc[kPeerMaxRanks];
+    int pworld = 0;
+    if (a.pro == kProAddNorm && a.peer) {
+      const PeerX& P = *a.peer;
+      const unsigned e = *P.epoch;
+      pworld = P.world;
+      for (int r = 0; r < kPeerMaxRanks; ++r) psrc[r] = r < pworld ? peer_slot(P, P.rank, e, r) : nullptr;
+      if (tid == 0) {
+        for (int r = 0; r < pworld; ++r) {
+          if (r == P.rank) continue;
+          const unsigned* flag = peer_flag(P, P.rank, r);
+          const uint64_t t0 = globaltimer_ns();
+          uint32_t i = 0;
+          while ((int)(ld_acquire_sys_u32(flag) - e) < 0) {
+            if ((++i & 63u) == 0u && globaltimer_ns() - t0 > kWaitLimitNs) {
+              report_status(a.status, kDevTimeoutPeer);
+              break;
+            }
+          }
+        }
+      }
+      Sync::sync();
+    }
     float ssg[8];
 #pragma unroll
     for (int gi = 0; gi < 8; ++gi) ssg[gi] = 0.f;
 #pragma unroll 1
     for (int c = tid; c < nch; c += nthr) {
       float v[8];
-      src8(a, c, tok, v);
+      src8(a, c, tok, v, pworld ? psrc : nullptr, pworld);
       float ss = 0.f;
 #pragma unroll
       for (int e = 0; e < 8; ++e) ss = fmaf(v[e], v[e], ss);
@@ -524,8 +585,38 @@ __device__ __forceinline__ void pg_epilogue(const GemvArgs& a, const PGeom& geo,
         break;
       }
       default:
-        a.yf[n] = acc;
+        if (a.peer) {
+          // this rank's partial into every rank's region (peer stores)
+          const PeerX& P = *a.peer;
+          const unsigned e = *P.epoch + 1u;
+          for (int d = 0; d < P.world; ++d) peer_slot(P, d, e, P.rank)[n] = acc;
+        } else {
+          a.yf[n] = acc;
+        }
         break;
+    }
+  }
+}
+
+// After a peer-sum producer's epilogue (every thread of every CTA): the CTA
+// barrier orders its threads' slot stores before thread 0's system-scope
+// fence (fences are cumulative), which precedes the CTA's ticket; the last
+// CTA through the ticket advances the epoch and sets this rank's flag in
+// every region.
+template <class Sync>
+__device__ __forceinline__ void pg_peer_publish(const GemvArgs& a, int tid, unsigned* flag_last) {
+  Sync::sync();
+  if (tid == 0) {
+    const PeerX& P = *a.peer;
+    __threadfence_system();
+    *flag_last = (atomicAdd(P.ticket, 1u) == gridDim.x - 1) ? 1u : 0u;
+    if (*flag_last) {
+      __threadfence();
+      *P.ticket = 0u;
+      const unsigned e = *P.epoch + 1u;
+      *P.epoch = e;
+      __threadfence_system();
+      for (int d = 0; d < P.world; ++d) st_release_sys_u32(peer_flag(P, d, P.rank), e);
     }
   }
 }

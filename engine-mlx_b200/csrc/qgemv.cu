@@ -205,7 +205,6 @@ __global__ void __launch_bounds__(kThreads, 2) qgemv_kernel(const GemvArgs a, co
     fence_mbar_init();
   }
   __syncthreads();
-  pdl_trigger();
 
   // ---- one round: weight rows + scale/bias rows into ring slot r % nbuf.
   // Called by all 32 lanes of warp 0; copies are spread over the lanes.
@@ -258,6 +257,11 @@ __global__ void __launch_bounds__(kThreads, 2) qgemv_kernel(const GemvArgs a, co
 
   // ---- wait for the producer of x (previous kernel) ---------------------
   pdl_wait();
+  // the next kernel may launch once this one's inputs are final: one kernel
+  // ahead streams its weights beside this one, while an earlier trigger lets
+  // the chain run several kernels ahead and the block scheduler then stacks
+  // two CTAs of one launch on an SM while others hold none
+  pdl_trigger();
 
   if (gather) {
     lrows = min(*a.n_slots * a.slot_rows, geo.lrows);

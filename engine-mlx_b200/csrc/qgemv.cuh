@@ -30,6 +30,25 @@ enum GemvEpi : int {
   kEpiF32 = 4,     // yf[n] = acc (fp32 partial, e.g. before a tensor-parallel sum)
 };
 
+// Decode tensor-parallel sum through NVLink peer memory (comm.cu sets it
+// up).  Each rank owns a region [flags (u32 per source rank) | pad to
+// kPeerHeader | two buffers of kPeerMaxRanks fp32 slots], mapped into every
+// rank.  The producing GEMV (kEpiF32 with `peer`) stores its partial into
+// slot [rank] of buffer (e+1) & 1 of every rank's region (peer stores over
+// NVLink, e = reductions so far), and its last CTA then sets flag [rank] = e+1
+// in every region; the consuming prologue (kProAddNorm with `peer`) waits on
+// its own region's flags and sums the local slots in rank order, so every
+// rank computes the same bits and the partials cross NVLink once.
+constexpr int kPeerMaxRanks = 8;
+constexpr int kPeerSlotFloats = 16384;
+constexpr int kPeerHeader = 256;
+struct PeerX {
+  unsigned char* base[kPeerMaxRanks];  // each rank's region in this process (base[rank] is local)
+  int world, rank;
+  unsigned* epoch;   // local: reductions produced so far
+  unsigned* ticket;  // local: CTAs through the producing GEMV
+};
+
 struct GemvArgs {
   const uint32_t* w;  // [N, K*bits/32] (or [E, rows_per_expert, ...] with slots)
   const bf16* s;      // [N, K/gs]
@@ -72,6 +91,7 @@ struct GemvArgs {
   int* pos;       // optional: *pos += pos_inc after the argmax
   int pos_inc;
   int* status;
+  const PeerX* peer;  // kEpiF32 producer / kProAddNorm consumer of a peer-memory sum (device), or nullptr
 };
 
 // Host-side launch plan (computed once per weight shape).

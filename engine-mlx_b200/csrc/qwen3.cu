@@ -242,18 +242,25 @@ GemvArgs gemv_base(const emx_qwen3* m, const QW& q) {
   return a;
 }
 
-// Shared memory a decode GEMV may claim: small enough that the next kernel of
-// the step (another GEMV, or decode attention with its 64 KB ring of K/V
-// tiles and up to 48 KB of partials) is resident beside it (228 KB per SM,
-// 1 KB reserved per CTA) and streams its inputs while this one computes.  The lm_head streams far more
-// than it can hold and its dequant is the longest compute of the step: it
-// runs two CTAs per SM.
-constexpr int kGemvBudget = 94 * 1024;
+// Shared memory of a decode GEMV CTA: at least half an SM (228 KB, 1 KB
+// reserved per CTA), so two GEMV CTAs never share an SM.  The block scheduler
+// places a pending launch greedily: when a GEMV's CTAs fit two to an SM, the
+// SMs that free up first take two of them and the others none, and the
+// pattern repeats down the chain of launches (half the SMs doing twice the
+// work).  With one GEMV CTA per SM the next GEMV takes each SM as this one
+// leaves it, while decode attention (a 64 KB K/V ring plus up to 32 KB of
+// partials) is still resident beside a GEMV and streams its tiles during it.
+// The lm_head streams far more than it can hold and its dequant is the
+// longest compute of the step: it runs two smaller CTAs per SM.
+constexpr int kGemvSmem = 114 * 1024;
+constexpr int kGemvBudgetPair = 94 * 1024;
 
 int plan(emx_qwen3* m, const QW& q, int epi, int x_slots, int n_rows_override, PgemvPlan* p, int ctas_per_sm = 1) {
   const int N = n_rows_override > 0 ? n_rows_override : q.N;
-  if (pgemv_make_plan(N, q.K, q.bits, q.gs, epi, x_slots, m->ctx->num_sms, kGemvBudget, p, ctas_per_sm))
+  const int budget = ctas_per_sm > 1 ? kGemvBudgetPair : kGemvSmem;
+  if (pgemv_make_plan(N, q.K, q.bits, q.gs, epi, x_slots, m->ctx->num_sms, budget, p, ctas_per_sm))
     return fail(EMX_ERR_INVALID, "no GEMV plan for N=%d K=%d bits=%d group=%d", N, q.K, q.bits, q.gs);
+  if (ctas_per_sm == 1) p->smem = std::max(p->smem, kGemvSmem);
   return EMX_OK;
 }
 
@@ -592,6 +599,10 @@ int enqueue_step(emx_qwen3* m) {
   bf16* cur = m->xa;
   bf16* nxt = m->xb;
   bool pending_add = false;  // the previous block's output still has to be added to `cur`
+  // tensor parallel: the o / down partials are summed through NVLink peer
+  // memory inside the GEMVs (producer epilogue, consumer prologue) when the
+  // communicator could map every rank's exchange region; else NCCL
+  const PeerX* peer = m->tp && m->H <= kPeerSlotFloats ? comm_peer(m->comm) : nullptr;
   auto set_add = [&](GemvArgs& a) {
     // the residual add of the previous block's sharded / expert output, fused here
     a.pro = kProAddNorm;
@@ -601,10 +612,17 @@ int enqueue_step(emx_qwen3* m) {
       a.moe_y = m->moe_y;
       a.moe_w = m->moe_w;
       a.moe_n = m->moe_n;
+    } else if (peer) {
+      a.peer = peer;
     } else {
       a.add_f32 = m->part;
       a.add_round = m->tp ? 1 : 0;
     }
+  };
+  auto tp_sum = [&](GemvArgs& a) {  // a tensor-parallel partial producer
+    a.epi = kEpiF32;
+    if (peer) a.peer = peer;
+    else a.yf = m->part;
   };
   int rc;
   for (int l = 0; l < c.layers; ++l) {
@@ -671,8 +689,7 @@ int enqueue_step(emx_qwen3* m) {
       a.pro = kProX;
       a.x = m->attnb;
       if (m->tp) {
-        a.epi = kEpiF32;
-        a.yf = m->part;
+        tp_sum(a);
       } else {
         a.epi = kEpiResid;
         a.res = cur;
@@ -680,7 +697,7 @@ int enqueue_step(emx_qwen3* m) {
       }
       if ((rc = launch_gemv(m, a, lw.p_o, pdl))) return rc;
       if (m->tp) {
-        if ((rc = comm_all_reduce(m->comm, m->part, (size_t)m->H, EMX_F32, st))) return rc;
+        if (!peer && (rc = comm_all_reduce(m->comm, m->part, (size_t)m->H, EMX_F32, st))) return rc;
         pending_add = true;
       }
     }
@@ -703,8 +720,7 @@ int enqueue_step(emx_qwen3* m) {
       d.pro = kProX;
       d.x = m->hb;
       if (m->tp) {
-        d.epi = kEpiF32;
-        d.yf = m->part;
+        tp_sum(d);
       } else {
         d.epi = kEpiResid;
         d.res = cur;
@@ -712,7 +728,7 @@ int enqueue_step(emx_qwen3* m) {
       }
       if ((rc = launch_gemv(m, d, lw.p_down, pdl))) return rc;
       if (m->tp) {
-        if ((rc = comm_all_reduce(m->comm, m->part, (size_t)m->H, EMX_F32, st))) return rc;
+        if (!peer && (rc = comm_all_reduce(m->comm, m->part, (size_t)m->H, EMX_F32, st))) return rc;
         pending_add = true;
       }
     } else {
