@@ -12,7 +12,7 @@
 // exp(-1e9 - m) == 0).  Work split: grid (splits, n_kv); each CTA owns one KV
 // head (and the q heads that share it) over a contiguous slice of the valid
 // rows, keeps the softmax partial (m, l, acc), and the last CTA of a head
-// merges the slices.  Only ceil(L / kMinRows) splits (at most the grid's) take
+// merges the slices.  Only ceil(L / kAttnMinRows) splits (at most the grid's) take
 // part, so short contexts do not pay for a wide merge; the others return at
 // once.
 //
@@ -36,14 +36,8 @@ constexpr int kTile = 64;     // rows per K / V tile
 // tiles in flight (a buffer is refilled with the tile kNBuf ahead): two, so
 // that two CTAs of the kernel share an SM
 constexpr int kNBuf = 2;
-constexpr int kMinRows = 64;  // fewest rows a split is given
 constexpr int kTileBytes = kTile * kHD * 2;
 constexpr int kDynSmem = 128 + 2 * kNBuf * kTileBytes;
-
-__device__ __forceinline__ int active_splits(int L, int grid) {
-  const int s = (L + kMinRows - 1) / kMinRows;
-  return s < grid ? s : grid;
-}
 
 __device__ __forceinline__ void split_range(int L, int splits, int split, int& p0, int& p1) {
   p0 = (int)((long long)split * L / splits);
@@ -126,7 +120,7 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const AttnDecodeA
     plan_p = -1;
     const int pg = a.pos ? *reinterpret_cast<const volatile int*>(a.pos) : a.pos_host;
     if (pg >= 0 && pg < a.cap) {
-      const int splits = active_splits(pg + 1, gridDim.x);
+      const int splits = attn_active_splits(pg + 1, gridDim.x);
       if (split < splits) {
         int p0, p1;
         split_range(pg + 1, splits, split, p0, p1);
@@ -151,7 +145,7 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const AttnDecodeA
   const int p = a.pos ? *a.pos : a.pos_host;
   const bool bad = p < 0 || p >= a.cap;
   const int L = p + 1;
-  const int splits = bad ? 0 : active_splits(L, gridDim.x);
+  const int splits = bad ? 0 : attn_active_splits(L, gridDim.x);
   int p0 = 0, p1 = 0;
   if (!bad) split_range(L, splits, split, p0, p1);
   const int ntile = (p1 - p0 + kTile - 1) / kTile;
@@ -389,7 +383,8 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const AttnDecodeA
     for (int w = 0; w < kWarps; ++w) num += sacc[w][h][d];
     return num;
   };
-  if (splits == 1) {
+  const bool defer = a.defer_merge && splits <= kAttnDeferSplits;
+  if (splits == 1 && !defer) {
     // a single split needs no merge: normalise and store
     for (int i = tid; i < HPG * kHD; i += kThreads) {
       const int h = i / kHD, d = i % kHD;
@@ -408,6 +403,7 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const AttnDecodeA
     part[tid * (kHD + 2) + 0] = stat_m[tid];
     part[tid * (kHD + 2) + 1] = stat_l[tid];
   }
+  if (defer) return;  // the consumer merges
   __threadfence();
   __syncthreads();
   if (tid == 0) last = (atomicAdd(&a.ticket[kvh], 1u) == (unsigned)splits - 1) ? 1u : 0u;

@@ -24,7 +24,20 @@ struct AttnDecodeArgs {
   unsigned* ticket;       // [nkv], zero between launches
   int splits;
   int* status;
+  // nonzero: when at most kAttnDeferSplits splits are active, every split
+  // stores its partial and returns; the consumer (the o-projection GEMV's
+  // kProMerge prologue) merges them with the same arithmetic
+  int defer_merge;
 };
+
+// Fewest cache rows a split is given, and the splits that take part for L
+// rows on a grid of `grid` splits (the producer and a deferred merge agree).
+constexpr int kAttnMinRows = 64;
+constexpr int kAttnDeferSplits = 4;
+__host__ __device__ __forceinline__ int attn_active_splits(int L, int grid) {
+  const int s = (L + kAttnMinRows - 1) / kAttnMinRows;
+  return s < grid ? s : grid;
+}
 
 // Split grid size for n_kv KV heads with hpg q heads each.
 int attn_decode_splits(int nkv, int num_sms, int hpg);

@@ -108,7 +108,7 @@ __global__ void __launch_bounds__(kThreads, 2) pgemv_kernel(const GemvArgs a, co
   };
 
   // the norm weights do not depend on the previous kernel either
-  const bool norm_pre = a.pro != kProX;
+  const bool norm_pre = a.pro != kProX && a.pro != kProMerge;
   if (norm_pre && producer) {
     mbar_arrive_expect_tx(nwbar, (uint32_t)(geo.K * 2));
     bulk_g2s(smem + geo.off_nw, a.norm_w, (uint32_t)(geo.K * 2), nwbar);
@@ -354,8 +354,12 @@ int pgemv_make_plan(int N, int K, int bits, int gs, int epi, int x_slots, int nu
 }
 
 cudaError_t pgemv_launch(const GemvArgs& a, const PgemvPlan& p, cudaStream_t st, bool pdl) {
-  if (a.pro != kProX && a.norm_groups > 8) return cudaErrorInvalidValue;
+  const bool norm = a.pro != kProX && a.pro != kProMerge;
+  if (norm && a.norm_groups > 8) return cudaErrorInvalidValue;
   if (a.pro != kProX && p.x_slots > 1) return cudaErrorInvalidValue;
+  if (a.pro == kProMerge && (a.K != a.attn_hpg * (a.K / a.attn_hpg) || !a.attn_part || !a.attn_pos ||
+                             a.attn_hpg < 1 || a.attn_grid < 1 || a.K % 128 != 0))
+    return cudaErrorInvalidValue;
   PGeom g;
   make_pgeom(a.N, a.K, a.bits, a.gs, a.epi, p, &g);
   if (p.x_slots > 1) {
@@ -363,7 +367,7 @@ cudaError_t pgemv_launch(const GemvArgs& a, const PgemvPlan& p, cudaStream_t st,
     const unsigned long long lps = (unsigned long long)(a.slot_rows / 16);
     g.lps_magic = (0x100000000ull + lps - 1) / lps;
   }
-  if (a.pro != kProX && (g.nw_bytes < a.K * 2 || (reinterpret_cast<uintptr_t>(a.norm_w) & 15) != 0))
+  if (norm && (g.nw_bytes < a.K * 2 || (reinterpret_cast<uintptr_t>(a.norm_w) & 15) != 0))
     return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.grid);

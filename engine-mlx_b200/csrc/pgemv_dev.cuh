@@ -17,6 +17,7 @@
 //   slots in a fixed order, so the result does not depend on which CTA or
 //   warp computed a unit.
 #pragma once
+#include "attn_decode.cuh"
 #include "qgemv.cuh"
 
 namespace emx {
@@ -279,6 +280,79 @@ __device__ __forceinline__ void pg_pad(const PGeom& geo, const PgSmem& sm, int t
   for (int i = tid; i < geo.x_slots * gpad; i += nthr) sm.xs[(i / gpad) * S * 8 + geo.ng + i % gpad] = 0.f;
 }
 
+// kProMerge: x = the decode attention output, merged from the splits'
+// partials when the attention deferred its merge (1 <= splits <=
+// kAttnDeferSplits), with the attention's own arithmetic (attn_decode.cu):
+// M = max m_s, w_s = exp(m_s - M), den = the butterfly sum of fma(w_s, l_s)
+// over the split lanes, out = bf16(sum_s fma(w_s / den, acc_s)) in split
+// order -- the bits the attention's merge would store.  Returns false when
+// the attention merged itself (x is then read from a.x).
+template <int GS>
+__device__ __forceinline__ bool pg_merge_attn(const GemvArgs& a, const PGeom& geo, const PgSmem& sm, int tid,
+                                              int nthr, bool lead) {
+  const int ns = attn_active_splits(*a.attn_pos + 1, a.attn_grid);
+  if (ns < 1 || ns > kAttnDeferSplits) return false;
+  constexpr int HD = 128, PS = HD + 2;
+  const int hpg = a.attn_hpg;
+  const size_t sstride = (size_t)hpg * PS;  // between the splits of one head
+  const int nch = geo.K / 8;
+  for (int it = 0; it * nthr < nch; ++it) {
+    const int c = it * nthr + tid;
+    const bool valid = c < nch;
+    float o[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) o[e] = 0.f;
+    if (valid) {
+      const int q = c / (HD / 8), d0 = (c % (HD / 8)) * 8;
+      const float* pb = a.attn_part + ((size_t)(q / hpg) * ns * hpg + (q % hpg)) * PS;
+      float ms[kAttnDeferSplits], ls[kAttnDeferSplits];
+      float2 v[kAttnDeferSplits][4];
+#pragma unroll
+      for (int s2 = 0; s2 < kAttnDeferSplits; ++s2) {
+        ms[s2] = -INFINITY;
+        ls[s2] = 0.f;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) v[s2][j] = make_float2(0.f, 0.f);
+        if (s2 < ns) {
+          const float* ps = pb + s2 * sstride;
+          ms[s2] = __ldcg(ps);
+          ls[s2] = __ldcg(ps + 1);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) v[s2][j] = __ldcg(reinterpret_cast<const float2*>(ps + 2 + d0 + 2 * j));
+        }
+      }
+      float M = -INFINITY;
+#pragma unroll
+      for (int s2 = 0; s2 < kAttnDeferSplits; ++s2) M = fmaxf(M, ms[s2]);
+      float w[kAttnDeferSplits], t[kAttnDeferSplits];
+#pragma unroll
+      for (int s2 = 0; s2 < kAttnDeferSplits; ++s2) {
+        w[s2] = ms[s2] == -INFINITY ? 0.f : expf(ms[s2] - M);
+        t[s2] = fmaf(w[s2], ls[s2], 0.f);
+      }
+      static_assert(kAttnDeferSplits == 4, "the butterfly below covers four split lanes");
+      const float den = (t[0] + t[2]) + (t[1] + t[3]);
+#pragma unroll
+      for (int s2 = 0; s2 < kAttnDeferSplits; ++s2) {
+        if (s2 < ns) {
+          const float sw = __fdiv_rn(w[s2], den);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            o[2 * j] = fmaf(sw, v[s2][j].x, o[2 * j]);
+            o[2 * j + 1] = fmaf(sw, v[s2][j].y, o[2 * j + 1]);
+          }
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) o[e] = bfround(o[e]);
+    }
+    const uint4 pk = valid ? pack8exact(o) : make_uint4(0u, 0u, 0u, 0u);
+    pg_emit<GS>(geo, sm, 0, c, valid, pk, o);
+    if (valid && lead && a.x_out) *reinterpret_cast<uint4*>(a.x_out + c * 8) = pk;
+  }
+  return true;
+}
+
 // x prologue: x in padded groups (zero past K to whole spans) and the group
 // sums of x, built by threads [0, nthr).  The `lead` CTA also stores the new
 // residual of embedding / add prologues to a.x_out.  Norm prologues take the
@@ -296,7 +370,9 @@ __device__ __forceinline__ void pg_prologue(const GemvArgs& a, const PGeom& geo,
   auto emit = [&](int slot, int c, bool valid, const float (&o)[8]) {
     pg_emit<GS>(geo, sm, slot, c, valid, valid ? pack8exact(o) : make_uint4(0u, 0u, 0u, 0u), o);
   };
-  if (a.pro == kProX) {
+  const bool merged = a.pro == kProMerge && pg_merge_attn<GS>(a, geo, sm, tid, nthr, lead);
+  if (merged) {
+  } else if (a.pro == kProX || a.pro == kProMerge) {
     for (int slot = 0; slot < geo.x_slots; ++slot) {
 #pragma unroll 1
       for (int it = 0; it * nthr < nch; ++it) {

@@ -19,6 +19,9 @@ enum GemvPro : int {
   kProAddNorm = 3,    // src = bf16(a.x + addend) (CTA 0 stores it to x_out), then norm;
                       //   addend = bf16(add_f32) if add_round else add_f32 (tensor-parallel
                       //   sum), or sum_s moe_w[s]*moe_y[s] in fp32 (MoE combine) when moe_y
+  kProMerge = 4,      // x = the decode attention output: merged here from the splits'
+                      //   partials when the attention deferred its merge (few splits;
+                      //   CTA 0 stores it to x_out), else read from a.x as kProX
 };
 
 // Epilogue: what happens to each finished output row (fp32 accumulator).
@@ -92,6 +95,11 @@ struct GemvArgs {
   int pos_inc;
   int* status;
   const PeerX* peer;  // kEpiF32 producer / kProAddNorm consumer of a peer-memory sum (device), or nullptr
+  // kProMerge: the attention's partials [nkv][splits][hpg][head_dim + 2] (m, l,
+  // unnormalised output), its position word and split grid
+  const float* attn_part;
+  const int* attn_pos;
+  int attn_hpg, attn_grid;
 };
 
 // Host-side launch plan (computed once per weight shape).

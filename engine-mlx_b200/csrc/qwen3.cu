@@ -679,6 +679,7 @@ int enqueue_step(emx_qwen3* m) {
       a.ticket = m->attn_ticket;
       a.splits = m->attn_splits;
       a.status = m->ctx->status;
+      a.defer_merge = 1;  // the o projection's prologue merges a few splits
       cudaError_t e = attn_decode_launch(a, st, pdl);
       if (e != cudaSuccess) return fail_cuda(e, "attention launch");
       ++m->step_launches;
@@ -686,8 +687,12 @@ int enqueue_step(emx_qwen3* m) {
     // ---- o projection (+ residual, or fp32 partial + all-reduce under TP)
     {
       GemvArgs a = gemv_base(m, lw.o);
-      a.pro = kProX;
+      a.pro = kProMerge;
       a.x = m->attnb;
+      a.attn_part = m->attn_part;
+      a.attn_pos = m->pos;
+      a.attn_hpg = m->nq / m->nkv;
+      a.attn_grid = m->attn_splits;
       if (m->tp) {
         tp_sum(a);
       } else {
