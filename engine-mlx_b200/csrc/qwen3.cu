@@ -13,8 +13,12 @@
 //   (compiled.rs:79-287)                        (5 kernels per layer + lm_head, chained by PDL)
 //   prefill (forward_qwen3.rs:12-200)           eager stream-ordered prefill
 //   argmax in-graph + to_vec_u32                argmax fused into the lm_head GEMV; 4-byte D2H
+#include <sys/stat.h>
+
+#include <algorithm>
 #include <cstring>
 #include <map>
+#include <set>
 #include <string>
 #include <vector>
 
@@ -27,6 +31,7 @@
 #include "pgemv.cuh"
 #include "step.cuh"
 #include "qgemv.cuh"
+#include "safetensors.cuh"
 
 namespace emx {
 
@@ -102,6 +107,7 @@ struct emx_qwen3 {
   bf16* kv = nullptr;
   size_t kv_layer = 0;  // elements of one layer's K (or V)
   std::map<std::string, Spec> specs;
+  std::set<std::string> loaded;  // tensors written by load_tensor / init_random
   std::vector<void*> allocs;
   // decode buffers
   bf16 *xa = nullptr, *xb = nullptr, *qkvb = nullptr, *attnb = nullptr, *hb = nullptr, *logits = nullptr;
@@ -1100,7 +1106,194 @@ int emx_qwen3_load_tensor(emx_qwen3* m, const char* name, const void* host, size
                                      cudaMemcpyHostToDevice, m->ctx->stream),
                    "emx_qwen3_load_tensor");
   }
-  return ctx_sync_check(m->ctx, "emx_qwen3_load_tensor");
+  const int rc = ctx_sync_check(m->ctx, "emx_qwen3_load_tensor");
+  if (rc == EMX_OK) m->loaded.insert(name);
+  return rc;
+}
+
+namespace {
+
+// Full (unsharded) MLX shape and dtype of a model tensor: quantized parts are
+// uint32 codes [rows, K*bits/32] or bf16 scales / biases [rows, K/group]
+// (expert tensors [experts, rows, cols]); norms bf16 [len].
+void spec_shape(const std::string& name, const Spec& s, int64_t shape[3], int* ndim, int* dtype) {
+  if (s.kind == 1) {
+    *ndim = 1;
+    shape[0] = s.norm_len;
+    *dtype = EMX_BF16;
+    return;
+  }
+  const int esz = s.part == 0 ? 4 : 2;
+  const int64_t cols = (int64_t)(s.src_pitch / esz);
+  const int64_t blocks_full = (int64_t)(s.src_total / (s.src_pitch * (size_t)s.src_block_rows));
+  *dtype = s.part == 0 ? EMX_U32 : EMX_BF16;
+  if (name.find(".switch_mlp.") != std::string::npos) {
+    *ndim = 3;
+    shape[0] = blocks_full;
+    shape[1] = s.src_block_rows;
+    shape[2] = cols;
+  } else {
+    *ndim = 2;
+    shape[0] = (int64_t)s.src_block_rows * blocks_full;
+    shape[1] = cols;
+  }
+}
+
+const char* dtype_name(int dtype) { return dtype == EMX_U32 ? "U32" : "BF16"; }
+
+// One checkpoint tensor (or one row range of a shipped fused one) into the
+// model: its dtype and trailing dimensions must be the model's.
+int load_checked(emx_qwen3* m, const std::string& name, const StTensor& t, const unsigned char* base,
+                 uint64_t off, uint64_t bytes, int64_t rows) {
+  const Spec& s = m->specs.at(name);
+  int64_t shp[3];
+  int nd, dt;
+  spec_shape(name, s, shp, &nd, &dt);
+  Q_REQUIRE(t.dtype == dtype_name(dt), "load_safetensors: '%s' is %s in the checkpoint, the model takes %s",
+            t.name.c_str(), t.dtype.c_str(), dtype_name(dt));
+  Q_REQUIRE((int)t.shape.size() == nd && t.shape.back() == shp[nd - 1] && (nd < 3 || t.shape[1] == shp[1]) &&
+                (nd == 1 || rows == shp[0]),
+            "load_safetensors: '%s' has a shape the model does not take (trailing dimension %lld, model %lld)",
+            t.name.c_str(), (long long)t.shape.back(), (long long)shp[nd - 1]);
+  return emx_qwen3_load_tensor(m, name.c_str(), base + off, (size_t)bytes);
+}
+
+// A shipped fused projection (the reference prefers them:
+// crates/serve/src/loader/weights.rs:103-118, 166-175): `parts` row counts in
+// concatenation order, each loaded under its separate name.
+int load_fused(emx_qwen3* m, const StTensor& t, const unsigned char* base, const std::string& prefix,
+               const std::string& suffix, const std::vector<std::pair<std::string, int64_t>>& parts) {
+  int64_t total = 0;
+  for (const auto& p : parts) total += p.second;
+  Q_REQUIRE(t.shape.size() == 2 && t.shape[0] == total,
+            "load_safetensors: fused '%s' has %lld rows, expected %lld", t.name.c_str(),
+            t.shape.empty() ? 0LL : (long long)t.shape[0], (long long)total);
+  const uint64_t row_bytes = total ? t.bytes / (uint64_t)total : 0;
+  uint64_t off = t.offset;
+  for (const auto& p : parts) {
+    const std::string name = prefix + p.first + suffix;
+    Q_REQUIRE(m->specs.count(name), "load_safetensors: fused '%s' has no part '%s' in this model", t.name.c_str(),
+              name.c_str());
+    StTensor part = t;
+    part.shape[0] = p.second;
+    const uint64_t bytes = row_bytes * (uint64_t)p.second;
+    const int rc = load_checked(m, name, part, base, off, bytes, p.second);
+    if (rc) return rc;
+    off += bytes;
+  }
+  return EMX_OK;
+}
+
+bool is_dir(const std::string& p) {
+  struct stat st;
+  return stat(p.c_str(), &st) == 0 && S_ISDIR(st.st_mode);
+}
+
+bool is_file(const std::string& p) {
+  struct stat st;
+  return stat(p.c_str(), &st) == 0 && S_ISREG(st.st_mode);
+}
+
+}  // namespace
+
+int emx_qwen3_load_safetensors(emx_qwen3* m, const char* path, int* n_loaded) {
+  Q_REQUIRE(m && path, "emx_qwen3_load_safetensors: null argument");
+  // the files: a directory holds model_fused.safetensors (preferred, as
+  // crates/serve/src/loader/weights.rs:21-41), model.safetensors, or the
+  // shards a model.safetensors.index.json names; else `path` is one file
+  std::vector<std::string> files;
+  const std::string dir = path;
+  if (is_dir(dir)) {
+    const std::string fused = dir + "/model_fused.safetensors", plain = dir + "/model.safetensors",
+                      index = dir + "/model.safetensors.index.json";
+    if (is_file(fused)) {
+      files.push_back(fused);
+    } else if (is_file(plain)) {
+      files.push_back(plain);
+    } else if (is_file(index)) {
+      std::vector<std::string> shards;
+      int rc = st_index_files(index.c_str(), &shards);
+      if (rc) return rc;
+      for (const auto& f : shards) files.push_back(dir + "/" + f);
+    } else {
+      return fail(EMX_ERR_INVALID, "model.safetensors not found at %s", path);
+    }
+  } else {
+    files.push_back(dir);
+  }
+  const emx_qwen3_config& c = m->c;
+  const int hd = c.head_dim > 0 ? c.head_dim : 128;
+  int count = 0;
+  for (const auto& fpath : files) {
+    StFile f;
+    int rc = st_open(fpath.c_str(), &f);
+    if (rc) return rc;
+    for (const StTensor& t : f.tensors) {
+      if (m->specs.count(t.name)) {
+        rc = load_checked(m, t.name, t, f.base, t.offset, t.bytes, t.shape.empty() ? 0 : t.shape[0]);
+        if (rc) return rc;
+        ++count;
+        continue;
+      }
+      // shipped fused projections: model.layers.i.self_attn.qkv_proj.* and
+      // model.layers.i.mlp.gate_up_proj.*
+      const size_t dot = t.name.rfind('.');
+      const std::string stem = dot == std::string::npos ? t.name : t.name.substr(0, dot);
+      const std::string suffix = dot == std::string::npos ? "" : t.name.substr(dot);
+      const std::string kQkv = "self_attn.qkv_proj", kGu = "mlp.gate_up_proj";
+      if (stem.size() > kQkv.size() && stem.compare(stem.size() - kQkv.size(), kQkv.size(), kQkv) == 0) {
+        const std::string pre = stem.substr(0, stem.size() - kQkv.size()) + "self_attn.";
+        rc = load_fused(m, t, f.base, pre, suffix,
+                        {{"q_proj", (int64_t)c.n_q * hd}, {"k_proj", (int64_t)c.n_kv * hd}, {"v_proj", (int64_t)c.n_kv * hd}});
+        if (rc) return rc;
+        ++count;
+        continue;
+      }
+      if (stem.size() > kGu.size() && stem.compare(stem.size() - kGu.size(), kGu.size(), kGu) == 0) {
+        const std::string pre = stem.substr(0, stem.size() - kGu.size()) + "mlp.";
+        rc = load_fused(m, t, f.base, pre, suffix, {{"gate_proj", (int64_t)c.inter}, {"up_proj", (int64_t)c.inter}});
+        if (rc) return rc;
+        ++count;
+        continue;
+      }
+      // a separate lm_head makes the model untied (weights.rs:113-127); a
+      // model created tied cannot take one
+      Q_REQUIRE(t.name.rfind("lm_head.", 0) != 0,
+                "load_safetensors: the checkpoint has '%s' but the model was created with tied embeddings",
+                t.name.c_str());
+      // anything else is not on this path (the reference loads it and never
+      // looks it up)
+    }
+  }
+  // every tensor the model takes must have come from some file
+  for (const auto& kv : m->specs)
+    Q_REQUIRE(m->loaded.count(kv.first), "load_safetensors: missing %s", kv.first.c_str());
+  if (n_loaded) *n_loaded = count;
+  return EMX_OK;
+}
+
+int emx_qwen3_tensor_names(emx_qwen3* m, char* buf, size_t cap, size_t* need) {
+  Q_REQUIRE(m && need, "emx_qwen3_tensor_names: null argument");
+  std::string all;
+  for (const auto& kv : m->specs) {
+    all += kv.first;
+    all += '\n';
+  }
+  *need = all.size() + 1;
+  if (buf && cap > 0) {
+    const size_t n = std::min(cap - 1, all.size());
+    std::memcpy(buf, all.data(), n);
+    buf[n] = 0;
+  }
+  return EMX_OK;
+}
+
+int emx_qwen3_tensor_shape(emx_qwen3* m, const char* name, int64_t* shape3, int* ndim, int* dtype) {
+  Q_REQUIRE(m && name && shape3 && ndim && dtype, "emx_qwen3_tensor_shape: null argument");
+  auto it = m->specs.find(name);
+  Q_REQUIRE(it != m->specs.end(), "emx_qwen3_tensor_shape: unknown tensor '%s'", name);
+  spec_shape(it->first, it->second, shape3, ndim, dtype);
+  return EMX_OK;
 }
 
 int emx_qwen3_read_tensor(emx_qwen3* m, const char* name, void* host, size_t bytes) {
@@ -1134,7 +1327,10 @@ int emx_qwen3_read_kv(emx_qwen3* m, int layer, int which, void* host, size_t byt
 int emx_qwen3_init_random(emx_qwen3* m, uint64_t seed) {
   Q_REQUIRE(m, "emx_qwen3_init_random: null model");
   m->packed_ok = false;
-  return init_random_impl(m, seed);
+  const int rc = init_random_impl(m, seed);
+  if (rc == EMX_OK)
+    for (const auto& kv : m->specs) m->loaded.insert(kv.first);
+  return rc;
 }
 
 int emx_qwen3_reset(emx_qwen3* m) {

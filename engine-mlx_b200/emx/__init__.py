@@ -91,6 +91,11 @@ _SIGS = {
     "emx_qwen3_destroy": (C.c_int, [C.c_void_p]),
     "emx_qwen3_load_tensor": (C.c_int, [C.c_void_p, C.c_char_p, C.c_void_p, C.c_size_t]),
     "emx_qwen3_read_tensor": (C.c_int, [C.c_void_p, C.c_char_p, C.c_void_p, C.c_size_t]),
+    "emx_qwen3_load_safetensors": (C.c_int, [C.c_void_p, C.c_char_p, C.POINTER(C.c_int)]),
+    "emx_qwen3_tensor_names": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.POINTER(C.c_size_t)]),
+    "emx_qwen3_tensor_shape": (C.c_int, [C.c_void_p, C.c_char_p, C.POINTER(C.c_int64), C.POINTER(C.c_int),
+                                         C.POINTER(C.c_int)]),
+    "emx_safetensors_index": (C.c_int, [C.c_char_p, C.c_void_p, C.c_int, C.POINTER(C.c_int)]),
     "emx_qwen3_read_kv": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_size_t]),
     "emx_qwen3_set_compiled": (C.c_int, [C.c_void_p, C.c_int]),
     "emx_qwen3_shard": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_char_p, C.POINTER(C.c_int32)]),
@@ -434,6 +439,52 @@ CONFIGS: Dict[str, Qwen3Config] = {
 }
 
 
+class StTensor(C.Structure):
+    """emx_st_tensor: one tensor of a .safetensors file."""
+    _fields_ = [("name", C.c_char * 256), ("dtype", C.c_char * 12), ("ndim", C.c_int), ("shape", C.c_int64 * 8),
+                ("offset", C.c_uint64), ("bytes", C.c_uint64)]
+
+
+def safetensors_index(path: str):
+    """[{name, dtype, shape, offset, bytes}] of a .safetensors file, validated
+    by the library (host only; no device needed)."""
+    n = C.c_int(0)
+    _check(lib().emx_safetensors_index(path.encode(), None, 0, C.byref(n)))
+    arr = (StTensor * max(1, n.value))()
+    _check(lib().emx_safetensors_index(path.encode(), arr, n.value, C.byref(n)))
+    return [{"name": t.name.decode(), "dtype": t.dtype.decode(), "shape": tuple(t.shape[:t.ndim]),
+             "offset": int(t.offset), "bytes": int(t.bytes)} for t in arr[:n.value]]
+
+
+_ST_DTYPES = {np.dtype(np.uint32): "U32", np.dtype(np.uint16): "BF16", np.dtype(np.float32): "F32",
+              np.dtype(np.int32): "I32", np.dtype(np.uint8): "U8", np.dtype(np.float16): "F16"}
+
+
+def write_safetensors(path: str, tensors, metadata=None):
+    """Writes a .safetensors file: `tensors` maps name -> array (uint16 arrays
+    are written as BF16 bit patterns) or (dtype name, array)."""
+    import json
+    import struct
+
+    header, blobs, off = {}, [], 0
+    for name, v in tensors.items():
+        dt, a = v if isinstance(v, tuple) else (_ST_DTYPES[np.asarray(v).dtype], v)
+        a = np.ascontiguousarray(a)
+        b = a.tobytes()
+        header[name] = {"dtype": dt, "shape": list(a.shape), "data_offsets": [off, off + len(b)]}
+        blobs.append(b)
+        off += len(b)
+    if metadata:
+        header["__metadata__"] = dict(metadata)
+    h = json.dumps(header, separators=(",", ":")).encode()
+    h += b" " * ((8 - len(h) % 8) % 8)  # the format pads the header to 8 bytes
+    with open(path, "wb") as f:
+        f.write(struct.pack("<Q", len(h)))
+        f.write(h)
+        for b in blobs:
+            f.write(b)
+
+
 def shard(cfg: "Qwen3Config", world: int, rank: int, name: str):
     """(row0, n_rows, col0, n_cols, block0, blocks) of tensor `name` kept by rank (host only)."""
     out = (C.c_int32 * 6)()
@@ -504,6 +555,27 @@ class Qwen3:
     def load_tensor(self, name: str, arr: np.ndarray):
         a = np.ascontiguousarray(arr)
         _check(lib().emx_qwen3_load_tensor(self.h, name.encode(), a.ctypes.data, a.nbytes))
+
+    def load_safetensors(self, path: str) -> int:
+        """Loads an MLX checkpoint directory or .safetensors file; returns the
+        number of checkpoint tensors used."""
+        n = C.c_int(0)
+        _check(lib().emx_qwen3_load_safetensors(self.h, path.encode(), C.byref(n)))
+        return n.value
+
+    def tensor_names(self):
+        need = C.c_size_t(0)
+        _check(lib().emx_qwen3_tensor_names(self.h, None, 0, C.byref(need)))
+        buf = C.create_string_buffer(need.value)
+        _check(lib().emx_qwen3_tensor_names(self.h, buf, need.value, C.byref(need)))
+        return [x for x in buf.value.decode().split("\n") if x]
+
+    def tensor_shape(self, name: str):
+        """(full MLX shape, numpy dtype) of a tensor the model takes."""
+        shp = (C.c_int64 * 3)()
+        nd, dt = C.c_int(0), C.c_int(0)
+        _check(lib().emx_qwen3_tensor_shape(self.h, name.encode(), shp, C.byref(nd), C.byref(dt)))
+        return tuple(shp[:nd.value]), (np.uint32 if dt.value == 2 else np.uint16)
 
     def read_tensor(self, name: str, nbytes: int) -> bytes:
         buf = np.empty(nbytes, dtype=np.uint8)

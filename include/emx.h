@@ -214,6 +214,40 @@ int emx_qwen3_destroy(emx_qwen3* m);
 int emx_qwen3_load_tensor(emx_qwen3* m, const char* name, const void* host, size_t bytes);
 /* Copies a loaded tensor (this rank's shard, fused layout) back to the host. */
 int emx_qwen3_read_tensor(emx_qwen3* m, const char* name, void* host, size_t bytes);
+/* load_weights_from_manifest's checkpoint files (crates/serve/src/loader/
+ * weights.rs:17-60, dtypes of loader/tensor.rs:5-16): `path` is a model
+ * directory -- model_fused.safetensors preferred, else model.safetensors,
+ * else the shards named by model.safetensors.index.json -- or one
+ * .safetensors file.  Every tensor the model takes is loaded through
+ * emx_qwen3_load_tensor (this rank's shard); shipped fused
+ * self_attn.qkv_proj / mlp.gate_up_proj tensors are split into their parts
+ * (weights.rs:103-118, 166-175); tensors off this path are skipped, as the
+ * reference never looks them up.  Fails (EMX_ERR_INVALID) on a malformed
+ * container, a dtype or shape the model does not take, an lm_head for a
+ * model created tied, or -- after all files -- "missing <name>" for a
+ * tensor no file held.  *n_loaded (optional): checkpoint tensors used. */
+int emx_qwen3_load_safetensors(emx_qwen3* m, const char* path, int* n_loaded);
+/* The MLX checkpoint names of every tensor the model takes, one per line;
+ * *need = bytes including the terminating NUL (buf may be NULL). */
+int emx_qwen3_tensor_names(emx_qwen3* m, char* buf, size_t cap, size_t* need);
+/* Full (unsharded) MLX shape and dtype (EMX_U32 codes, EMX_BF16 scales /
+ * biases / norms) of one of those tensors; ndim is 1, 2 or 3. */
+int emx_qwen3_tensor_shape(emx_qwen3* m, const char* name, int64_t* shape3, int* ndim, int* dtype);
+
+/* One tensor of a .safetensors file (emx_safetensors_index). */
+typedef struct {
+  char name[256];
+  char dtype[12]; /* as in the header: "BF16", "U32", "F32", ... */
+  int ndim;
+  int64_t shape[8];
+  uint64_t offset; /* byte offset of the data from the start of the file */
+  uint64_t bytes;
+} emx_st_tensor;
+/* Host only (no device needed): validates a .safetensors file the way the
+ * safetensors crate's deserialize does (header fits the file, each tensor's
+ * bytes are prod(shape) * dtype size, the tensors tile the data section)
+ * and lists up to `cap` tensors in header order; *n = the file's count. */
+int emx_safetensors_index(const char* file, emx_st_tensor* out, int cap, int* n);
 /* Copies layer `layer`'s K (which = 0) or V (which = 1) cache of this rank to
  * the host: bf16 [n_kv_local, kv_cap, head_dim], rows >= offset unspecified.
  * The engine's per-layer kv_bufs pair (crates/serve/src/engine_ext.rs:69-90)
