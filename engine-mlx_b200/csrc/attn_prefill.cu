@@ -66,8 +66,9 @@ __global__ void __launch_bounds__(kThreads) attn_prefill_kernel(const AttnPrefil
   const int q0 = qt * kBM;
   const int T = a.T;
   const bf16* Q = a.q + ((size_t)h * T) * kD;
-  const bf16* K = a.kc + ((size_t)kvh * a.cap + a.offset) * kD;
-  const bf16* V = a.vc + ((size_t)kvh * a.cap + a.offset) * kD;
+  const int P = a.prefix, L = P + T;  // keys: P cached rows, then the chunk
+  const bf16* K = a.kc + ((size_t)kvh * a.cap + a.offset - P) * kD;
+  const bf16* V = a.vc + ((size_t)kvh * a.cap + a.offset - P) * kD;
 
   // load Q tile
   for (int i = tid; i < kBM * 16; i += kThreads) {
@@ -78,14 +79,14 @@ __global__ void __launch_bounds__(kThreads) attn_prefill_kernel(const AttnPrefil
     const int k0 = kt * kBN;
     for (int i = tid; i < kBN * 16; i += kThreads) {
       const int r = i >> 4, c = i & 15;
-      const bool ok = k0 + r < T;
-      const size_t row = (size_t)min(k0 + r, T - 1) * kD + c * 8;
+      const bool ok = k0 + r < L;
+      const size_t row = (size_t)min(k0 + r, L - 1) * kD + c * 8;
       cp_async16(sK + buf * kBN * kD + swz(r, c), K + row, ok);
       cp_async16(sV + buf * kBN * kD + swz(r, c), V + row, ok);
     }
   };
   const int last_q = min(q0 + kBM, T) - 1;
-  const int n_kt = last_q / kBN + 1;
+  const int n_kt = (last_q + P) / kBN + 1;
   load_kv(0, 0);
   cp_async_commit();
 
@@ -140,7 +141,7 @@ __global__ void __launch_bounds__(kThreads) attn_prefill_kernel(const AttnPrefil
         const int col = k0 + nt * 8 + tig * 2 + (e & 1);
         const int row = (e < 2) ? row_a : row_b;
         float v = s[nt][e] * sl2;
-        if (col > row || col >= T) v = -INFINITY;
+        if (col > row + P || col >= L) v = -INFINITY;
         s[nt][e] = v;
         mx[e >> 1] = fmaxf(mx[e >> 1], v);
       }
@@ -633,8 +634,12 @@ cudaError_t encode_rows(CUtensorMap* map, const void* base, uint64_t rows, uint6
 cudaError_t attn_prefill_launch(const AttnPrefillArgs& a, cudaStream_t st, int* status) {
   if (a.head_dim != kD || a.nkv <= 0 || a.nq % a.nkv) return cudaErrorInvalidValue;
   if (a.T <= 0) return cudaSuccess;
-  if (((reinterpret_cast<uintptr_t>(a.q) | reinterpret_cast<uintptr_t>(a.kc) | reinterpret_cast<uintptr_t>(a.vc)) &
-       15) == 0) {
+  if (a.prefix < 0 || a.prefix > a.offset) return cudaErrorInvalidValue;
+  const bool aligned =
+      ((reinterpret_cast<uintptr_t>(a.q) | reinterpret_cast<uintptr_t>(a.kc) | reinterpret_cast<uintptr_t>(a.vc)) & 15) == 0;
+  // the tcgen05 kernel covers a chunk attending itself; a chunk that also
+  // attends cached rows before it goes through the mma.sync kernel
+  if (a.prefix == 0 && aligned) {
     CUtensorMap tq, tk, tv;
     cudaError_t e = encode_rows(&tq, a.q, (uint64_t)a.T, (uint64_t)a.nq, (uint64_t)a.T * kD * 2);
     if (e == cudaSuccess)

@@ -16,6 +16,7 @@
 #include <sys/stat.h>
 
 #include <algorithm>
+#include <cmath>
 #include <cstring>
 #include <map>
 #include <set>
@@ -32,6 +33,7 @@
 #include "step.cuh"
 #include "qgemv.cuh"
 #include "safetensors.cuh"
+#include "sample.cuh"
 
 namespace emx {
 
@@ -130,6 +132,12 @@ struct emx_qwen3 {
   // persistent decode step (dense model on one GPU)
   bool step_ok = false;    // the shape has a plan and it fits
   bool fused = false;      // decode through the persistent step kernel
+  // device sampling (Qwen3Engine::set_sampling, crates/serve/src/engine.rs:230-233)
+  bool sampling = false;   // temperature >= 1e-6: sample instead of the in-graph argmax
+  float s_temp = 0.f, s_top_p = 1.f;
+  int s_top_k = 0;
+  unsigned long long* rng = nullptr;  // SimpleRng state
+  float* samp = nullptr;              // [vocab] probabilities
   bool step_coop = true;   // launch it cooperatively
   StepPlan sp{};
   StepArgs sa{};
@@ -545,6 +553,11 @@ int build(emx_qwen3* m) {
       return rc;
   }
   if ((rc = alloc_t(m, 64, &m->state))) return rc;
+  if ((rc = alloc_t(m, 1, &m->rng)) || (rc = alloc_t(m, (size_t)c.vocab, &m->samp))) return rc;
+  {
+    const unsigned long long s0 = sample_rng_seed(42);  // SimpleRng::new(42), engine.rs:218
+    EMX_CHECK_CUDA(cudaMemcpy(m->rng, &s0, sizeof(s0), cudaMemcpyHostToDevice), "sampler state");
+  }
   m->token = m->state + 0;
   m->pos = m->state + 1;
   m->hist_n = m->state + 2;
@@ -591,12 +604,31 @@ int launch_gemv(emx_qwen3* m, const GemvArgs& a, const PgemvPlan& p, bool pdl) {
   return EMX_OK;
 }
 
+// sample_from_logits (crates/serve/src/sampler.rs:84-96) over the lm_head's
+// logits, on the device; the token replaces the argmax in m->token.
+int launch_sampler(emx_qwen3* m, int* hist, cudaStream_t st) {
+  SampleArgs s = {};
+  s.logits = m->logits;
+  s.n = m->c.vocab;
+  s.temperature = m->s_temp;
+  s.top_p = m->s_top_p;
+  s.top_k = m->s_top_k;
+  s.rng = m->rng;
+  s.scratch = m->samp;
+  s.tok_out = m->token;
+  s.hist = hist;
+  s.hist_n = m->hist_n;
+  s.hist_cap = m->c.kv_cap;
+  const cudaError_t e = sample_launch(s, st);
+  return e == cudaSuccess ? EMX_OK : fail_cuda(e, "sampler launch");
+}
+
 int enqueue_step(emx_qwen3* m) {
   const emx_qwen3_config& c = m->c;
   cudaStream_t st = m->ctx->stream;
   const bool pdl = m->compiled;  // the eager step is plain stream order
   m->step_launches = 0;
-  if (m->fused) {
+  if (m->fused && !m->sampling) {
     cudaError_t e = step_launch(m->sa, m->sp, st, m->step_coop);
     if (e != cudaSuccess) return fail_cuda(e, "decode step launch");
     m->step_launches = 1;
@@ -802,12 +834,16 @@ int enqueue_step(emx_qwen3* m) {
     a.am_idx = m->am_idx;
     a.am_ticket = m->am_ticket;
     a.tok_out = m->token;
-    a.hist = m->hist;
+    a.hist = m->sampling ? nullptr : m->hist;  // the sampler records its own token
     a.hist_n = m->hist_n;
     a.hist_cap = c.kv_cap;
     a.pos = m->pos;
     a.pos_inc = 1;
     if ((rc = launch_gemv(m, a, m->p_lm, pdl))) return rc;
+    if (m->sampling) {
+      if ((rc = launch_sampler(m, m->hist, st))) return rc;
+      ++m->step_launches;
+    }
   }
   return EMX_OK;
 }
@@ -871,7 +907,11 @@ int gemm(emx_qwen3* m, const QW& q, const bf16* x, int T, int epi, bf16* y, cons
   return EMX_OK;
 }
 
-int prefill_impl(emx_qwen3* m, const int32_t* ids_dev, int T) {
+// One forward pass over T prompt rows at the current offset.  attend_cache:
+// the rows also attend the cached rows before them (chunked prefill); else
+// the chunk attends only itself, as Qwen3Engine::prefill does
+// (crates/serve/src/forward_qwen3.rs:125-150: sdpa over the chunk's k/v).
+int prefill_impl(emx_qwen3* m, const int32_t* ids_dev, int T, bool attend_cache = false) {
   const emx_qwen3_config& c = m->c;
   cudaStream_t st = m->ctx->stream;
   const int H = m->H, hd = m->hd;
@@ -911,6 +951,7 @@ int prefill_impl(emx_qwen3* m, const int32_t* ids_dev, int T) {
     aa.cap = c.kv_cap;
     aa.offset = off;
     aa.T = T;
+    aa.prefix = attend_cache ? off : 0;
     aa.nq = m->nq;
     aa.nkv = m->nkv;
     aa.head_dim = hd;
@@ -997,6 +1038,10 @@ int prefill_impl(emx_qwen3* m, const int32_t* ids_dev, int T) {
   a.pos_inc = T;
   e = pgemv_launch(a, m->p_lm, st, false);
   if (e != cudaSuccess) return fail_cuda(e, "prefill lm_head");
+  if (m->sampling) {
+    const int rc = launch_sampler(m, nullptr, st);
+    if (rc) return rc;
+  }
   m->offset += T;
   return EMX_OK;
 }
@@ -1375,6 +1420,33 @@ int emx_qwen3_prefill(emx_qwen3* m, const int32_t* tokens, int T, int32_t* next_
   return EMX_OK;
 }
 
+int emx_qwen3_prefill_chunked(emx_qwen3* m, const int32_t* tokens, int T, int chunk, int32_t* next_token,
+                              void* logits) {
+  Q_REQUIRE(m && tokens, "emx_qwen3_prefill_chunked: null argument");
+  Q_REQUIRE(T >= 1 && chunk >= 1, "emx_qwen3_prefill_chunked: T=%d / chunk=%d must be positive", T, chunk);
+  if (m->offset + T > m->c.kv_cap)
+    return fail(EMX_ERR_STATE, "static KV overflow offset=%d + T=%d > cap=%d", m->offset, T, m->c.kv_cap);
+  const int step = std::min(chunk, m->max_T);
+  for (int t0 = 0; t0 < T; t0 += step) {  // make_chunks (crates/prefill/src/chunked_prefill.rs:18-20)
+    const int n = std::min(step, T - t0);
+    EMX_CHECK_CUDA(cudaMemcpyAsync(m->pids, tokens + t0, sizeof(int32_t) * n, cudaMemcpyHostToDevice,
+                                   m->ctx->stream),
+                   "prefill ids");
+    const int rc = prefill_impl(m, m->pids, n, true);
+    if (rc) return rc;
+  }
+  if (logits)
+    EMX_CHECK_CUDA(cudaMemcpyAsync(logits, m->logits, (size_t)m->c.vocab * 2, cudaMemcpyDeviceToHost, m->ctx->stream),
+                   "prefill logits");
+  if (next_token)
+    EMX_CHECK_CUDA(cudaMemcpyAsync(m->pinned, m->token, sizeof(int32_t), cudaMemcpyDeviceToHost, m->ctx->stream),
+                   "prefill token");
+  const int rc = ctx_sync_check(m->ctx, "emx_qwen3_prefill_chunked");
+  if (rc) return rc;
+  if (next_token) *next_token = m->pinned[0];
+  return EMX_OK;
+}
+
 int emx_qwen3_decode_step(emx_qwen3* m, int32_t token, int32_t* next_token, void* logits) {
   Q_REQUIRE(m, "emx_qwen3_decode_step: null model");
   Q_REQUIRE(token >= 0 && token < m->c.vocab, "emx_qwen3_decode_step: token %d outside [0, %d)", token, m->c.vocab);
@@ -1459,6 +1531,24 @@ int emx_qwen3_set_fused(emx_qwen3* m, int fused) {
   }
   m->fused = fused != 0;
   return EMX_OK;
+}
+
+int emx_qwen3_set_sampling(emx_qwen3* m, float temperature, float top_p, int top_k, uint64_t seed) {
+  Q_REQUIRE(m, "emx_qwen3_set_sampling: null model");
+  Q_REQUIRE(std::isfinite(temperature) && temperature >= 0.f && std::isfinite(top_p) && top_k >= 0,
+            "emx_qwen3_set_sampling: temperature %g / top_p %g / top_k %d out of range", temperature, top_p, top_k);
+  m->sampling = temperature >= 1e-6f;  // below: greedy, the in-graph argmax
+  m->s_temp = temperature;
+  m->s_top_p = std::min(1.f, std::max(0.f, top_p));  // SamplingParams::with_top_p clamps
+  m->s_top_k = top_k;
+  const unsigned long long s0 = sample_rng_seed(seed);
+  EMX_CHECK_CUDA(cudaMemcpyAsync(m->rng, &s0, sizeof(s0), cudaMemcpyHostToDevice, m->ctx->stream),
+                 "emx_qwen3_set_sampling");
+  if (m->gexec) {  // the parameters are part of the captured step
+    cudaGraphExecDestroy(m->gexec);
+    m->gexec = nullptr;
+  }
+  return ctx_sync_check(m->ctx, "emx_qwen3_set_sampling");
 }
 
 int emx_qwen3_is_fused(emx_qwen3* m, int* fused) {

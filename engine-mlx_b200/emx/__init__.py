@@ -96,6 +96,11 @@ _SIGS = {
     "emx_qwen3_tensor_shape": (C.c_int, [C.c_void_p, C.c_char_p, C.POINTER(C.c_int64), C.POINTER(C.c_int),
                                          C.POINTER(C.c_int)]),
     "emx_safetensors_index": (C.c_int, [C.c_char_p, C.c_void_p, C.c_int, C.POINTER(C.c_int)]),
+    "emx_qwen3_prefill_chunked": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.POINTER(C.c_int32),
+                                            C.c_void_p]),
+    "emx_qwen3_set_sampling": (C.c_int, [C.c_void_p, C.c_float, C.c_float, C.c_int, C.c_uint64]),
+    "emx_sample_token": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_float, C.c_float, C.c_int, C.c_void_p,
+                                   C.c_void_p]),
     "emx_qwen3_read_kv": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_size_t]),
     "emx_qwen3_set_compiled": (C.c_int, [C.c_void_p, C.c_int]),
     "emx_qwen3_shard": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_char_p, C.POINTER(C.c_int32)]),
@@ -322,6 +327,14 @@ class Ctx:
     def argmax(self, x, rows, n):
         out = self.alloc(rows * 4)
         _check(lib().emx_argmax(self.h, x.ptr, rows, n, out.ptr))
+        return out
+
+    def sample_token(self, logits, n, temperature, top_p, top_k, rng):
+        """sampler.rs sample_token on device bf16 logits; `rng` is a device
+        buffer holding the uint64 generator state (advanced in place).
+        Returns a device int32 buffer with the token."""
+        out = self.alloc(4)
+        _check(lib().emx_sample_token(self.h, logits.ptr, n, temperature, top_p, int(top_k), rng.ptr, out.ptr))
         return out
 
     def softmax(self, x, rows, n):
@@ -556,6 +569,11 @@ class Qwen3:
         a = np.ascontiguousarray(arr)
         _check(lib().emx_qwen3_load_tensor(self.h, name.encode(), a.ctypes.data, a.nbytes))
 
+    def set_sampling(self, temperature: float = 0.0, top_p: float = 1.0, top_k: int = 0, seed: int = 42):
+        """Qwen3Engine::set_sampling: temperature < 1e-6 is greedy; otherwise
+        prefill and decode sample on the device."""
+        _check(lib().emx_qwen3_set_sampling(self.h, temperature, top_p, int(top_k), C.c_uint64(seed)))
+
     def load_safetensors(self, path: str) -> int:
         """Loads an MLX checkpoint directory or .safetensors file; returns the
         number of checkpoint tensors used."""
@@ -630,6 +648,15 @@ class Qwen3:
         logits = np.empty(self.cfg.vocab, dtype=np.uint16) if want_logits else None
         _check(lib().emx_qwen3_prefill(self.h, ids.ctypes.data, len(ids), C.byref(nxt),
                                        logits.ctypes.data if want_logits else None))
+        return (nxt.value, logits) if want_logits else nxt.value
+
+    def prefill_chunked(self, tokens, chunk: int, want_logits=False):
+        """Prefill in chunks of `chunk` tokens, each attending the cache before it."""
+        ids = np.ascontiguousarray(np.asarray(tokens, dtype=np.int32))
+        nxt = C.c_int32()
+        logits = np.empty(self.cfg.vocab, dtype=np.uint16) if want_logits else None
+        _check(lib().emx_qwen3_prefill_chunked(self.h, ids.ctypes.data, len(ids), int(chunk), C.byref(nxt),
+                                               logits.ctypes.data if want_logits else None))
         return (nxt.value, logits) if want_logits else nxt.value
 
     def decode_step(self, token: int, want_logits=False):

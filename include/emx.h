@@ -147,6 +147,17 @@ int emx_add(emx_ctx* ctx, const void* a, const void* b, void* out, size_t n);
 /* MlxCtx::argmax (crates/mlx-ffi/src/ops/real/array.rs:6-10): first index of
  * the maximum of each row; out int32[rows] (device). */
 int emx_argmax(emx_ctx* ctx, const void* x, int rows, int n, int32_t* out);
+/* sample_token (crates/serve/src/sampler.rs:98-202) on the device, for
+ * temperature >= 1e-6: temperature scaling, top-k (0 = off), softmax, top-p
+ * (stable descending order, ties by index), renormalisation, one draw of
+ * SimpleRng (xorshift64*; *rng_state is a device uint64 advanced in place)
+ * and the first index whose running sum exceeds it.  logits: bf16 [n]
+ * (device); token: int32 (device).  Sums the host takes sequentially in fp32
+ * are taken per thread slice, then over the slices in order, so a draw
+ * within a few ulps of a boundary may pick the neighbouring token; with
+ * top_p >= 1 every entry is kept. */
+int emx_sample_token(emx_ctx* ctx, const void* logits, int n, float temperature, float top_p, int top_k,
+                     uint64_t* rng_state, int32_t* token);
 /* MlxCtx::softmax_axis(-1) (crates/mlx-ffi/src/ops/real/elementwise.rs:68-72), bf16. */
 int emx_softmax(emx_ctx* ctx, const void* x, void* out, int rows, int n);
 /* Qwen3Engine::embed = take(dequantize(embed_tokens), ids)
@@ -234,6 +245,16 @@ int emx_qwen3_tensor_names(emx_qwen3* m, char* buf, size_t cap, size_t* need);
  * biases / norms) of one of those tensors; ndim is 1, 2 or 3. */
 int emx_qwen3_tensor_shape(emx_qwen3* m, const char* name, int64_t* shape3, int* ndim, int* dtype);
 
+/* Qwen3Engine::set_sampling (crates/serve/src/engine.rs:230-233) with the
+ * host sampler moved onto the device: temperature < 1e-6 keeps the in-graph
+ * greedy argmax; otherwise every prefill and decode step ends with
+ * emx_sample_token's draw (no logits readback, no host sort).  top_p is
+ * clamped to [0, 1] (SamplingParams::with_top_p); the generator restarts
+ * from `seed` as SimpleRng::new(seed) (0 -> a fixed constant); the engine
+ * starts as SimpleRng::new(42), greedy.  While sampling, the persistent step
+ * (emx_qwen3_set_fused) is not used. */
+int emx_qwen3_set_sampling(emx_qwen3* m, float temperature, float top_p, int top_k, uint64_t seed);
+
 /* One tensor of a .safetensors file (emx_safetensors_index). */
 typedef struct {
   char name[256];
@@ -263,6 +284,15 @@ int emx_qwen3_offset(emx_qwen3* m, int* offset);
  * token ids at the current offset, then the greedy token of the last row.
  * logits (optional) receives bf16[vocab] of that row. */
 int emx_qwen3_prefill(emx_qwen3* m, const int32_t* tokens, int T, int32_t* next_token, void* logits);
+/* Chunked prefill (crates/prefill/src/pipeline.rs:60-117 with
+ * make_chunks, chunked_prefill.rs:18-20): T host tokens in chunks of
+ * min(chunk, max_prefill) at the current offset, each chunk attending the
+ * cached rows before it as well as itself, so T may exceed max_prefill and
+ * the result is that of one causal pass over all T rows (the reference's
+ * forward_fn per chunk, emx_qwen3_prefill above, attends the chunk only).
+ * next_token / logits: the last row's, as emx_qwen3_prefill. */
+int emx_qwen3_prefill_chunked(emx_qwen3* m, const int32_t* tokens, int T, int chunk, int32_t* next_token,
+                              void* logits);
 /* Qwen3Engine::decode_step (forward_qwen3.rs:206-243 -> decode_step_static,
  * decode_compiled.rs:14-65): one greedy step, replayed from a CUDA graph. */
 int emx_qwen3_decode_step(emx_qwen3* m, int32_t token, int32_t* next_token, void* logits);

@@ -407,6 +407,137 @@ int orc_argmax(const uint16_t* x, int n) {
 }
 
 /* ------------------------------------------------------------------------ */
+/* host sampler (crates/serve/src/sampler.rs)                               */
+/* ------------------------------------------------------------------------ */
+
+/* SimpleRng (sampler.rs:50-78): xorshift64*, seed 0 replaced by a constant;
+ * next_f32 = ((next >> 11) as f64 / 2^53) as f32. */
+uint64_t orc_rng_seed(uint64_t seed) { return seed ? seed : 0x9E3779B97F4A7C15ull; }
+
+static uint64_t rng_next_u64(uint64_t* st) {
+    uint64_t x = *st;
+    x ^= x >> 12;
+    x ^= x << 25;
+    x ^= x >> 27;
+    *st = x;
+    return x * 0x2545F4914F6CDD1Dull;
+}
+
+float orc_rng_next_f32(uint64_t* st) {
+    const double div = (double)(1ull << 53);
+    return (float)((double)(rng_next_u64(st) >> 11) / div);
+}
+
+typedef struct {
+    float v;
+    int i;
+} vi_t;
+
+/* descending by value, ties by index: what Rust's stable sort_by with
+ * b.partial_cmp(a) leaves (NaN compares Equal there; none occur here) */
+static int cmp_desc(const void* a, const void* b) {
+    const vi_t* x = (const vi_t*)a;
+    const vi_t* y = (const vi_t*)b;
+    if (x->v > y->v) return -1;
+    if (x->v < y->v) return 1;
+    return (x->i > y->i) - (x->i < y->i);
+}
+
+/* Iterator::max_by(partial_cmp): the LAST index of the maximum. */
+static int last_argmax(const float* x, int n) {
+    int best = 0;
+    for (int i = 1; i < n; ++i)
+        if (!(x[i] < x[best])) best = i;
+    return best;
+}
+
+/* sample_token (sampler.rs:98-202), step for step in f32: temperature
+ * scaling; top-k keeps values >= the k-th largest; softmax over the finite
+ * values with a sequential sum; top-p keeps the largest probabilities (stable
+ * descending order) until their running f32 sum reaches top_p; renormalise
+ * with a sequential sum over index order; draw r = next_f32 and return the
+ * first index whose running sum (index order, all entries) exceeds r, else
+ * the last kept index.  Advances *rng by one draw (only when sampling). */
+int orc_sample_token(const float* logits, int n, float temperature, float top_p, int top_k, uint64_t* rng) {
+    if (n <= 0) return -1;
+    if (temperature < 1e-6f) return last_argmax(logits, n);
+    const float temp = temperature > 1e-6f ? temperature : 1e-6f;
+    float* f = (float*)malloc(sizeof(float) * (size_t)n);
+    vi_t* srt = (vi_t*)malloc(sizeof(vi_t) * (size_t)n);
+    float* probs = (float*)malloc(sizeof(float) * (size_t)n);
+    char* keep = (char*)calloc((size_t)n, 1);
+    int tok = 0;
+    for (int i = 0; i < n; ++i) f[i] = logits[i] / temp;
+    if (top_k > 0 && top_k < n) {
+        for (int i = 0; i < n; ++i) {
+            srt[i].v = f[i];
+            srt[i].i = i;
+        }
+        qsort(srt, (size_t)n, sizeof(vi_t), cmp_desc);
+        const float kth = srt[top_k - 1].v;
+        for (int i = 0; i < n; ++i)
+            if (f[i] < kth) f[i] = -INFINITY;
+    }
+    float mx = -INFINITY;
+    for (int i = 0; i < n; ++i)
+        if (isfinite(f[i])) mx = fmaxf(mx, f[i]);
+    float sum = 0.0f;
+    for (int i = 0; i < n; ++i) {
+        probs[i] = isfinite(f[i]) ? expf(f[i] - mx) : 0.0f;
+        sum += probs[i];
+    }
+    if (!isfinite(sum) || sum == 0.0f) {
+        tok = last_argmax(logits, n);
+        goto done;
+    }
+    for (int i = 0; i < n; ++i) probs[i] = probs[i] / sum;
+    for (int i = 0; i < n; ++i) {
+        srt[i].v = probs[i];
+        srt[i].i = i;
+    }
+    qsort(srt, (size_t)n, sizeof(vi_t), cmp_desc);
+    {
+        float cum = 0.0f;
+        for (int j = 0; j < n; ++j) {
+            cum += srt[j].v;
+            keep[srt[j].i] = 1;
+            if (cum >= top_p) break;
+        }
+    }
+    float fsum = 0.0f;
+    for (int i = 0; i < n; ++i)
+        if (keep[i]) fsum += probs[i];
+    if (fsum > 0.0f)
+        for (int i = 0; i < n; ++i) probs[i] = keep[i] ? probs[i] / fsum : 0.0f;
+    {
+        const float r = orc_rng_next_f32(rng);
+        float cs = 0.0f;
+        tok = -1;
+        for (int i = 0; i < n; ++i) {
+            cs += probs[i];
+            if (r < cs) {
+                tok = i;
+                break;
+            }
+        }
+        if (tok < 0) {
+            tok = 0;
+            for (int i = n - 1; i >= 0; --i)
+                if (keep[i]) {
+                    tok = i;
+                    break;
+                }
+        }
+    }
+done:
+    free(f);
+    free(srt);
+    free(probs);
+    free(keep);
+    return tok;
+}
+
+/* ------------------------------------------------------------------------ */
 /* attention                                                                */
 /* ------------------------------------------------------------------------ */
 

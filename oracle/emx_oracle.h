@@ -85,6 +85,10 @@ void orc_silu(const uint16_t* x, size_t n, uint16_t* out);
 void orc_multiply(const uint16_t* a, const uint16_t* b, size_t n, uint16_t* out);
 void orc_add(const uint16_t* a, const uint16_t* b, size_t n, uint16_t* out);
 int orc_argmax(const uint16_t* x, int n); /* first index of the maximum */
+/* host sampler (crates/serve/src/sampler.rs:50-202) */
+uint64_t orc_rng_seed(uint64_t seed);
+float orc_rng_next_f32(uint64_t* state);
+int orc_sample_token(const float* logits, int n, float temperature, float top_p, int top_k, uint64_t* rng);
 
 /* ---- attention --------------------------------------------------------- */
 /* q[nq, Tq, D]; k,v[nkv, kv_stride, D] (first Tk rows used).

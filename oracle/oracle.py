@@ -37,6 +37,9 @@ _SIGS = {
     "orc_multiply": (None, [_P, _P, C.c_size_t, _P]),
     "orc_add": (None, [_P, _P, C.c_size_t, _P]),
     "orc_argmax": (C.c_int, [_P, C.c_int]),
+    "orc_rng_seed": (C.c_uint64, [C.c_uint64]),
+    "orc_rng_next_f32": (C.c_float, [_P]),
+    "orc_sample_token": (C.c_int, [_P, C.c_int, C.c_float, C.c_float, C.c_int, _P]),
     "orc_sdpa": (None, [_P, _P, _P] + [C.c_int] * 6 + [C.c_float, C.c_int, _P]),
     "orc_slice_update": (None, [_P, _P] + [C.c_int] * 5),
     "orc_softmax_bf16": (None, [_P, C.c_int, _P]),
@@ -176,6 +179,18 @@ def add(a, b):
 def argmax(x):
     x = _c(x, np.uint16)
     return lib().orc_argmax(_p(x), x.size)
+
+
+def rng_seed(seed: int) -> int:
+    return int(lib().orc_rng_seed(C.c_uint64(seed)))
+
+
+def sample_token(logits_f32, temperature, top_p, top_k, state: int):
+    """sampler.rs sample_token on f32 logits; returns (token, new rng state)."""
+    x = _c(logits_f32, np.float32)
+    st = C.c_uint64(state)
+    tok = lib().orc_sample_token(_p(x), x.size, temperature, top_p, int(top_k), C.cast(C.byref(st), C.c_void_p))
+    return tok, st.value
 
 
 def sdpa(q, k, v, nkv, Tk, kv_stride, scale, causal):

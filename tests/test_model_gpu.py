@@ -304,3 +304,25 @@ def test_full_config_greedy_parity_32_steps(ctx, name, prompt_len):
     ref = oracle_run(cfg, 2024, prompt, chain[:-1])
     noise = noise_floor(ref, oracle_run(cfg, 2024, prompt, chain[:-1], reverse=True))
     check_steps([(t, r[1]) for t, r in zip(chain, ref)], ref, noise, name)
+
+
+@pytest.mark.parametrize("cfg_name,prompt_len,chunk", [("dense_int4", 150, 64), ("mixed_int8", 150, 40),
+                                                       ("deep", 300, 128)])
+def test_chunked_prefill_matches_one_pass(ctx, cfg_name, prompt_len, chunk):
+    """emx_qwen3_prefill_chunked (crates/prefill/src/pipeline.rs:60-117): chunks
+    that attend the cache before them give the logits of one causal pass over
+    the whole prompt (the oracle's), also past max_prefill."""
+    cfg = DEEP_CFG if cfg_name == "deep" else TINY_CFGS[cfg_name]
+    rng = np.random.default_rng(prompt_len + chunk)
+    prompt = rng.integers(0, cfg.vocab, prompt_len).astype(np.int32)
+    forced = rng.integers(0, cfg.vocab, 4)
+    m = emx.Qwen3(ctx, cfg)
+    m.init_random(31)
+    gpu = [m.prefill_chunked(prompt, chunk, want_logits=True)]
+    assert m.offset == prompt_len
+    for t in forced:
+        gpu.append(m.decode_step(int(t), want_logits=True))
+    m.close()
+    ref = oracle_run(cfg, 31, prompt, forced)
+    noise = noise_floor(ref, oracle_run(cfg, 31, prompt, forced, reverse=True))
+    check_steps(gpu, ref, noise, f"chunked prefill {cfg_name}")
