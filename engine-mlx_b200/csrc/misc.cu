@@ -392,6 +392,29 @@ __global__ void moe_combine_kernel(const bf16* y, const float* w, const int* n, 
   }
 }
 
+// The expert-parallel combine through NVLink peer memory: this rank's
+// weighted sum of its expert slots (moe_combine_kernel's arithmetic) stored
+// into slot [rank] of every rank's region and published; the consumer's
+// AddNorm prologue sums the ranks' slots in rank order.
+struct BarAll {
+  static __device__ __forceinline__ void sync() { __syncthreads(); }
+};
+
+__global__ void moe_combine_peer_kernel(const bf16* y, const float* w, const int* n, int H, const PeerX* peer) {
+  pdl_trigger();
+  pdl_wait();
+  const PeerX& P = *peer;
+  const unsigned e = *P.epoch + 1u;
+  const int ns = *n;
+  for (int k = blockIdx.x * blockDim.x + threadIdx.x; k < H; k += gridDim.x * blockDim.x) {
+    float acc = 0.f;
+    for (int s = 0; s < ns; ++s) acc = __fadd_rn(acc, __fmul_rn(bf2f(y[(size_t)s * H + k]), w[s]));
+    for (int d = 0; d < P.world; ++d) peer_slot(P, d, e, P.rank)[k] = acc;
+  }
+  __shared__ unsigned last;
+  peer_publish<BarAll>(P, threadIdx.x, &last);
+}
+
 __global__ void add_f32_kernel(bf16* x, const float* add, size_t n, int round) {
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
     const float a = round ? bfround(add[i]) : add[i];
@@ -445,6 +468,12 @@ cudaError_t k_moe_residual(bf16* x, const bf16* y, const float* w, const int* n,
 cudaError_t k_moe_combine(const bf16* y, const float* w, const int* n, int H, float* out, cudaStream_t st, bool pdl) {
   void* args[] = {(void*)&y, (void*)&w, (void*)&n, (void*)&H, (void*)&out};
   return launch_pdl((const void*)moe_combine_kernel, dim3((H + 255) / 256), dim3(256), args, st, pdl);
+}
+
+cudaError_t k_moe_combine_peer(const bf16* y, const float* w, const int* n, int H, const PeerX* peer, cudaStream_t st,
+                               bool pdl) {
+  void* args[] = {(void*)&y, (void*)&w, (void*)&n, (void*)&H, (void*)&peer};
+  return launch_pdl((const void*)moe_combine_peer_kernel, dim3((H + 255) / 256), dim3(256), args, st, pdl);
 }
 
 cudaError_t k_dequantize(const uint32_t* w, const bf16* s, const bf16* b, bf16* out, int N, int K, int gs, int bits,

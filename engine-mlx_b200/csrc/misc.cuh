@@ -1,6 +1,7 @@
 // misc.cuh — standalone kernels behind the op-level C ABI and the prefill path.
 #pragma once
 #include "common.cuh"
+#include "peer.cuh"
 
 namespace emx {
 
@@ -69,6 +70,9 @@ cudaError_t k_moe_route(const bf16* logits, int E, int k, int normalize, int e_b
                         float* w, int* n, cudaStream_t st, bool pdl);
 // out[k] = sum_{s < *n} w[s] * y[s, k] in fp32, slot order (expert-parallel partial).
 cudaError_t k_moe_combine(const bf16* y, const float* w, const int* n, int H, float* out, cudaStream_t st, bool pdl);
+// The same sum stored into every rank's peer-memory slot and published.
+cudaError_t k_moe_combine_peer(const bf16* y, const float* w, const int* n, int H, const PeerX* peer, cudaStream_t st,
+                               bool pdl);
 
 // x[i] = bf16(x[i] + addend[i]) with addend = bf16(add[i]) when `round`, else
 // add[i] (rows x n, fp32 add) — the residual add after a tensor- / expert-

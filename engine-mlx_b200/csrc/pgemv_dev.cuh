@@ -141,27 +141,6 @@ __device__ __forceinline__ uint4 pack8exact(const float (&f)[8]) {
   return r;
 }
 
-__device__ __forceinline__ unsigned ld_acquire_sys_u32(const unsigned* p) {
-  unsigned v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
-__device__ __forceinline__ void st_release_sys_u32(unsigned* p, unsigned v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-// In rank `dst`'s region: the slot holding rank `src`'s partial of reduction e.
-__device__ __forceinline__ float* peer_slot(const PeerX& P, int dst, unsigned e, int src) {
-  return reinterpret_cast<float*>(P.base[dst] + kPeerHeader +
-                                  ((size_t)(e & 1u) * kPeerMaxRanks + src) * kPeerSlotFloats * 4);
-}
-
-// In rank `dst`'s region: rank `src`'s flag (the last reduction it stored there).
-__device__ __forceinline__ unsigned* peer_flag(const PeerX& P, int dst, int src) {
-  return reinterpret_cast<unsigned*>(P.base[dst]) + src;
-}
-
 // The pre-norm source values of elements [8c, 8c+8) (bf16 values as float).
 // `psrc` (kProAddNorm with a peer sum): the world ranks' fp32 partials.
 __device__ __forceinline__ void src8(const GemvArgs& a, int c, int tok, float (&v)[8],
@@ -196,8 +175,9 @@ __device__ __forceinline__ void src8(const GemvArgs& a, int c, int tok, float (&
         for (int e = 0; e < 8; ++e) add[e] = __fadd_rn(add[e], __fmul_rn(y[e], w));
       }
     } else if (psrc) {
-      // the ranks' partials summed in rank order (the same bits on every rank),
-      // then rounded like the unsharded projection's bf16 output
+      // the ranks' partials summed in rank order (the same bits on every
+      // rank); a TP sum is then rounded like the unsharded projection's bf16
+      // output (add_round), an EP expert sum is not
 #pragma unroll
       for (int e = 0; e < 8; ++e) add[e] = 0.f;
       for (int r = 0; r < pworld; ++r) {
@@ -206,8 +186,10 @@ __device__ __forceinline__ void src8(const GemvArgs& a, int c, int tok, float (&
         add[0] += p0.x, add[1] += p0.y, add[2] += p0.z, add[3] += p0.w;
         add[4] += p1.x, add[5] += p1.y, add[6] += p1.z, add[7] += p1.w;
       }
+      if (a.add_round) {
 #pragma unroll
-      for (int e = 0; e < 8; ++e) add[e] = bfround(add[e]);
+        for (int e = 0; e < 8; ++e) add[e] = bfround(add[e]);
+      }
     } else {
       const float4 p0 = *reinterpret_cast<const float4*>(a.add_f32 + k0);
       const float4 p1 = *reinterpret_cast<const float4*>(a.add_f32 + k0 + 4);
@@ -674,27 +656,10 @@ __device__ __forceinline__ void pg_epilogue(const GemvArgs& a, const PGeom& geo,
   }
 }
 
-// After a peer-sum producer's epilogue (every thread of every CTA): the CTA
-// barrier orders its threads' slot stores before thread 0's system-scope
-// fence (fences are cumulative), which precedes the CTA's ticket; the last
-// CTA through the ticket advances the epoch and sets this rank's flag in
-// every region.
+// After a peer-sum producer GEMV's epilogue (every thread of every CTA).
 template <class Sync>
 __device__ __forceinline__ void pg_peer_publish(const GemvArgs& a, int tid, unsigned* flag_last) {
-  Sync::sync();
-  if (tid == 0) {
-    const PeerX& P = *a.peer;
-    __threadfence_system();
-    *flag_last = (atomicAdd(P.ticket, 1u) == gridDim.x - 1) ? 1u : 0u;
-    if (*flag_last) {
-      __threadfence();
-      *P.ticket = 0u;
-      const unsigned e = *P.epoch + 1u;
-      *P.epoch = e;
-      __threadfence_system();
-      for (int d = 0; d < P.world; ++d) st_release_sys_u32(peer_flag(P, d, P.rank), e);
-    }
-  }
+  peer_publish<Sync>(*a.peer, tid, flag_last);
 }
 
 __device__ __forceinline__ void argmax_pair(float& bv, int& bi, float ov, int oi) {

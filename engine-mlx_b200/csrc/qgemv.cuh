@@ -8,6 +8,7 @@
 // launch.
 #pragma once
 #include "common.cuh"
+#include "peer.cuh"
 
 namespace emx {
 
@@ -31,25 +32,6 @@ enum GemvEpi : int {
   kEpiSwiglu = 2,  // rows [0,I) gate, [I,2I) up: y[n] = silu(g)*u with MLX's bf16 steps
   kEpiArgmax = 3,  // bf16 logits (optionally stored); greedy token over all rows
   kEpiF32 = 4,     // yf[n] = acc (fp32 partial, e.g. before a tensor-parallel sum)
-};
-
-// Decode tensor-parallel sum through NVLink peer memory (comm.cu sets it
-// up).  Each rank owns a region [flags (u32 per source rank) | pad to
-// kPeerHeader | two buffers of kPeerMaxRanks fp32 slots], mapped into every
-// rank.  The producing GEMV (kEpiF32 with `peer`) stores its partial into
-// slot [rank] of buffer (e+1) & 1 of every rank's region (peer stores over
-// NVLink, e = reductions so far), and its last CTA then sets flag [rank] = e+1
-// in every region; the consuming prologue (kProAddNorm with `peer`) waits on
-// its own region's flags and sums the local slots in rank order, so every
-// rank computes the same bits and the partials cross NVLink once.
-constexpr int kPeerMaxRanks = 8;
-constexpr int kPeerSlotFloats = 16384;
-constexpr int kPeerHeader = 256;
-struct PeerX {
-  unsigned char* base[kPeerMaxRanks];  // each rank's region in this process (base[rank] is local)
-  int world, rank;
-  unsigned* epoch;   // local: reductions produced so far
-  unsigned* ticket;  // local: CTAs through the producing GEMV
 };
 
 struct GemvArgs {

@@ -640,7 +640,7 @@ int enqueue_step(emx_qwen3* m) {
   // tensor parallel: the o / down partials are summed through NVLink peer
   // memory inside the GEMVs (producer epilogue, consumer prologue) when the
   // communicator could map every rank's exchange region; else NCCL
-  const PeerX* peer = m->tp && m->H <= kPeerSlotFloats ? comm_peer(m->comm) : nullptr;
+  const PeerX* peer = (m->tp || m->ep) && m->H <= kPeerSlotFloats ? comm_peer(m->comm) : nullptr;
   auto set_add = [&](GemvArgs& a) {
     // the residual add of the previous block's sharded / expert output, fused here
     a.pro = kProAddNorm;
@@ -652,6 +652,7 @@ int enqueue_step(emx_qwen3* m) {
       a.moe_n = m->moe_n;
     } else if (peer) {
       a.peer = peer;
+      a.add_round = m->tp ? 1 : 0;  // a TP sum is the unsharded projection's bf16 output
     } else {
       a.add_f32 = m->part;
       a.add_round = m->tp ? 1 : 0;
@@ -809,7 +810,11 @@ int enqueue_step(emx_qwen3* m) {
       da.n_slots = m->moe_n;
       da.slot_rows = m->H;
       if ((rc = launch_gemv(m, da, lw.p_edown, pdl))) return rc;
-      if (m->ep) {
+      if (m->ep && peer) {
+        e = k_moe_combine_peer(m->moe_y, m->moe_w, m->moe_n, m->H, peer, st, pdl);
+        if (e != cudaSuccess) return fail_cuda(e, "moe combine");
+        ++m->step_launches;
+      } else if (m->ep) {
         e = k_moe_combine(m->moe_y, m->moe_w, m->moe_n, m->H, m->part, st, pdl);
         if (e != cudaSuccess) return fail_cuda(e, "moe combine");
         ++m->step_launches;
