@@ -268,7 +268,7 @@ __global__ void pack_kernel(const uint32_t* __restrict__ w, const bf16* __restri
 void make_pgeom(int N, int K, int bits, int gs, int epi, const PgemvPlan& p, PGeom* g) {
   (void)N;
   pgeom_make(g, K, bits, gs, epi, p.lb_total, p.stage_tiles, p.nbuf, p.x_slots, p.lbs_max,
-             p.x_slots == 1 && K <= 8192);
+             p.norm && p.x_slots == 1 && K <= 8192);
   pgeom_layout(*g, gs);
 }
 
@@ -301,7 +301,7 @@ cudaError_t pgemv_pack(const uint32_t* w, const bf16* s, const bf16* b, int N, i
 }
 
 int pgemv_make_plan(int N, int K, int bits, int gs, int epi, int x_slots, int num_sms, int budget, PgemvPlan* plan,
-                    int ctas_per_sm) {
+                    int ctas_per_sm, int norm) {
   if (!(bits == 4 || bits == 8) || !(gs == 32 || gs == 64 || gs == 128)) return -1;
   if (K <= 0 || N <= 0 || K % gs != 0) return -1;
   const bool sw = epi == kEpiSwiglu;
@@ -311,6 +311,7 @@ int pgemv_make_plan(int N, int K, int bits, int gs, int epi, int x_slots, int nu
   if (lrows % 16 != 0) return -1;
   const int LB = lrows / 16;
   PgemvPlan p{};
+  p.norm = norm ? 1 : 0;
   p.halves = halves;
   p.lb_total = LB;
   p.x_slots = x_slots > 1 ? x_slots : 1;

@@ -53,14 +53,17 @@ struct PgemvPlan {
   int smem;        // dynamic shared memory bytes
   int x_slots;
   int lbs_max;     // logical blocks of the busiest CTA
+  int norm;        // room for the norm weights (the norm prologues need it)
 };
 
 // N = physical rows of one launch (2x logical rows for SwiGLU); `budget` is
 // the dynamic shared memory the plan may use; `ctas_per_sm` > 1 spreads a
 // streamed matrix over more CTAs (more warps hiding the dequant latency).
 // Returns 0 or -1 (unsupported).
+// `norm` = 0: the launches use no norm prologue, so no room is kept for
+// the norm weights (more for the stage ring).
 int pgemv_make_plan(int N, int K, int bits, int gs, int epi, int x_slots, int num_sms, int budget, PgemvPlan* plan,
-                    int ctas_per_sm = 1);
+                    int ctas_per_sm = 1, int norm = 1);
 
 // One GEMV; a.w must point at the packed matrix (a.s / a.b unused).
 cudaError_t pgemv_launch(const GemvArgs& a, const PgemvPlan& p, cudaStream_t st, bool pdl);

@@ -269,11 +269,29 @@ GemvArgs gemv_base(const emx_qwen3* m, const QW& q) {
 constexpr int kGemvSmem = 114 * 1024;
 constexpr int kGemvBudgetPair = 94 * 1024;
 
-int plan(emx_qwen3* m, const QW& q, int epi, int x_slots, int n_rows_override, PgemvPlan* p, int ctas_per_sm = 1) {
+// A GEMV between two GEMVs (gate|up, down) shares its SM with neither, so
+// when half an SM leaves its stages short of the 8 tiles that keep each of
+// the eight consumer warps on two units at a time (a large-K matrix whose x
+// and row slots fill the budget), it may take up to kGemvSmemWide.
+constexpr int kGemvSmemWide = 200 * 1024;
+constexpr int kFullStageTiles = 8;
+
+// norm: the launches use a norm prologue; widen: the GEMV may grow past
+// half an SM (see above).
+int plan(emx_qwen3* m, const QW& q, int epi, int x_slots, int n_rows_override, PgemvPlan* p, int ctas_per_sm = 1,
+         bool norm = true, bool widen = false) {
   const int N = n_rows_override > 0 ? n_rows_override : q.N;
   const int budget = ctas_per_sm > 1 ? kGemvBudgetPair : kGemvSmem;
-  if (pgemv_make_plan(N, q.K, q.bits, q.gs, epi, x_slots, m->ctx->num_sms, budget, p, ctas_per_sm))
+  if (pgemv_make_plan(N, q.K, q.bits, q.gs, epi, x_slots, m->ctx->num_sms, budget, p, ctas_per_sm, norm ? 1 : 0))
     return fail(EMX_ERR_INVALID, "no GEMV plan for N=%d K=%d bits=%d group=%d", N, q.K, q.bits, q.gs);
+  const int spans = (q.K / q.gs + 7) / 8;
+  const int cta_tiles = p->lbs_max * p->halves * spans;
+  PgemvPlan wide;
+  if (widen && ctas_per_sm == 1 && p->stage_tiles < std::min(kFullStageTiles, cta_tiles) &&
+      pgemv_make_plan(N, q.K, q.bits, q.gs, epi, x_slots, m->ctx->num_sms, kGemvSmemWide, &wide, 1, norm ? 1 : 0) ==
+          0 &&
+      wide.stage_tiles > p->stage_tiles)
+    *p = wide;
   if (ctas_per_sm == 1) p->smem = std::max(p->smem, kGemvSmem);
   return EMX_OK;
 }
@@ -521,14 +539,14 @@ int build(emx_qwen3* m) {
     }
     // launch plans
     if ((rc = plan(m, lw.qkv, kEpiStore, 1, 0, &lw.p_qkv))) return rc;
-    if ((rc = plan(m, lw.o, m->tp ? kEpiF32 : kEpiResid, 1, 0, &lw.p_o))) return rc;
+    if ((rc = plan(m, lw.o, m->tp ? kEpiF32 : kEpiResid, 1, 0, &lw.p_o, 1, false))) return rc;
     if (!m->moe) {
-      if ((rc = plan(m, lw.gate_up, kEpiSwiglu, 1, 0, &lw.p_gu))) return rc;
-      if ((rc = plan(m, lw.down, m->tp ? kEpiF32 : kEpiResid, 1, 0, &lw.p_down))) return rc;
+      if ((rc = plan(m, lw.gate_up, kEpiSwiglu, 1, 0, &lw.p_gu, 1, true, true))) return rc;
+      if ((rc = plan(m, lw.down, m->tp ? kEpiF32 : kEpiResid, 1, 0, &lw.p_down, 1, false, true))) return rc;
     } else {
       if ((rc = plan(m, lw.router, kEpiStore, 1, 0, &lw.p_router))) return rc;
       if ((rc = plan(m, lw.e_gu, kEpiSwiglu, 1, c.top_k * 2 * m->Im, &lw.p_egu))) return rc;
-      if ((rc = plan(m, lw.e_down, kEpiStore, c.top_k, c.top_k * H, &lw.p_edown))) return rc;
+      if ((rc = plan(m, lw.e_down, kEpiStore, c.top_k, c.top_k * H, &lw.p_edown, 1, false))) return rc;
     }
   }
   if ((rc = plan(m, c.tied ? m->embed : m->lm, kEpiArgmax, 1, 0, &m->p_lm, 2))) return rc;
