@@ -370,29 +370,40 @@ int st_open(const char* path, StFile* out) {
                          &out->tensors, path);
 }
 
-int st_index_files(const char* index_path, std::vector<std::string>* files) {
-  const int fd = open(index_path, O_RDONLY);
-  if (fd < 0) return fail(EMX_ERR_INVALID, "%s: cannot open (%s)", index_path, strerror(errno));
+namespace {
+
+// A whole JSON file (at most kMaxHeader bytes) that must hold one object.
+int read_json_file(const char* path, JVal* root) {
+  const int fd = open(path, O_RDONLY);
+  if (fd < 0) return fail(EMX_ERR_INVALID, "%s: cannot open (%s)", path, strerror(errno));
   std::string text;
   char buf[65536];
   while (true) {
     const ssize_t r = read(fd, buf, sizeof(buf));
     if (r < 0) {
       close(fd);
-      return fail(EMX_ERR_INVALID, "%s: read failed", index_path);
+      return fail(EMX_ERR_INVALID, "%s: read failed", path);
     }
     if (r == 0) break;
     text.append(buf, (size_t)r);
     if (text.size() > kMaxHeader) {
       close(fd);
-      return fail(EMX_ERR_INVALID, "%s: larger than %llu bytes", index_path, (unsigned long long)kMaxHeader);
+      return fail(EMX_ERR_INVALID, "%s: larger than %llu bytes", path, (unsigned long long)kMaxHeader);
     }
   }
   close(fd);
-  JVal root;
   JReader rd(text.data(), text.size());
-  if (!rd.document(&root) || root.kind != JVal::Obj)
-    return fail(EMX_ERR_INVALID, "%s: not a JSON object (%s)", index_path, rd.error().c_str());
+  if (!rd.document(root) || root->kind != JVal::Obj)
+    return fail(EMX_ERR_INVALID, "%s: not a JSON object (%s)", path, rd.error().c_str());
+  return EMX_OK;
+}
+
+}  // namespace
+
+int st_index_files(const char* index_path, std::vector<std::string>* files) {
+  JVal root;
+  const int rc = read_json_file(index_path, &root);
+  if (rc) return rc;
   const JVal* wm = root.get("weight_map");
   if (!wm || wm->kind != JVal::Obj) return fail(EMX_ERR_INVALID, "%s: no weight_map object", index_path);
   files->clear();
@@ -406,9 +417,151 @@ int st_index_files(const char* index_path, std::vector<std::string>* files) {
   return EMX_OK;
 }
 
+namespace {
+
+// config.json fields (Qwen3Config, crates/serve/src/config.rs:6-30, read by
+// Qwen3Config::from_dir, config.rs:73-86, with its serde defaults).
+struct CfgReader {
+  const JVal& root;
+  const char* path;
+  int rc = EMX_OK;
+  int need_int(const char* key) {
+    const JVal* v = root.get(key);
+    if (!v || v->kind != JVal::Int || v->i <= 0 || v->i > (1 << 30)) {
+      if (!rc) rc = fail(EMX_ERR_INVALID, "%s: '%s' missing or not a positive integer", path, key);
+      return 0;
+    }
+    return (int)v->i;
+  }
+  int opt_int(const char* key, int dflt) {
+    const JVal* v = root.get(key);
+    if (!v || v->kind == JVal::Null) return dflt;
+    if (v->kind != JVal::Int || v->i < 0 || v->i > (1 << 30)) {
+      if (!rc) rc = fail(EMX_ERR_INVALID, "%s: '%s' is not a non-negative integer", path, key);
+      return dflt;
+    }
+    return (int)v->i;
+  }
+  float opt_float(const char* key, float dflt) {
+    const JVal* v = root.get(key);
+    if (!v || v->kind == JVal::Null) return dflt;
+    if (v->kind == JVal::Int) return (float)v->i;
+    if (v->kind == JVal::Num) return (float)v->d;
+    if (!rc) rc = fail(EMX_ERR_INVALID, "%s: '%s' is not a number", path, key);
+    return dflt;
+  }
+  bool opt_bool(const char* key, bool dflt) {
+    const JVal* v = root.get(key);
+    if (!v || v->kind == JVal::Null) return dflt;
+    if (v->kind != JVal::Bool) {
+      if (!rc) rc = fail(EMX_ERR_INVALID, "%s: '%s' is not a boolean", path, key);
+      return dflt;
+    }
+    return v->b;
+  }
+};
+
+// One quantization setting ({"group_size": g, "bits": b}); false when the
+// entry is not such an object.
+bool quant_pair(const JVal& v, int* gs, int* bits) {
+  if (v.kind != JVal::Obj) return false;
+  const JVal* g = v.get("group_size");
+  const JVal* b = v.get("bits");
+  if (!g || !b || g->kind != JVal::Int || b->kind != JVal::Int) return false;
+  *gs = (int)g->i;
+  *bits = (int)b->i;
+  return true;
+}
+
+}  // namespace
+
 }  // namespace emx
 
 using namespace emx;
+
+extern "C" int emx_qwen3_config_from_dir(const char* model_dir, int kv_cap, int max_prefill, emx_qwen3_config* out) {
+  if (!model_dir || !out) return fail(EMX_ERR_INVALID, "emx_qwen3_config_from_dir: null argument");
+  if (kv_cap < 1 || max_prefill < 1 || max_prefill > kv_cap)
+    return fail(EMX_ERR_INVALID, "emx_qwen3_config_from_dir: kv_cap %d / max_prefill %d out of range", kv_cap,
+                max_prefill);
+  std::string path = model_dir;
+  struct stat st;
+  if (stat(path.c_str(), &st) == 0 && S_ISDIR(st.st_mode)) path += "/config.json";
+  JVal root;
+  int rc = read_json_file(path.c_str(), &root);
+  if (rc) return rc;
+  CfgReader r{root, path.c_str()};
+  emx_qwen3_config c;
+  std::memset(&c, 0, sizeof(c));
+  c.hidden = r.need_int("hidden_size");
+  c.layers = r.need_int("num_hidden_layers");
+  c.inter = r.need_int("intermediate_size");
+  c.n_q = r.need_int("num_attention_heads");
+  c.n_kv = r.need_int("num_key_value_heads");
+  c.vocab = r.need_int("vocab_size");
+  if (r.rc) return r.rc;
+  c.eps = r.opt_float("rms_norm_eps", 1e-6f);
+  c.rope_theta = r.opt_float("rope_theta", 1000000.0f);
+  c.head_dim = r.opt_int("head_dim", c.n_q ? c.hidden / c.n_q : 0);
+  c.norm_groups = r.opt_int("layernorm_num_groups", 1);
+  c.tied = r.opt_bool("tie_word_embeddings", true) ? 1 : 0;
+  // MoE (Qwen3-MoE config keys)
+  c.n_experts = r.opt_int("num_experts", 0);
+  c.top_k = r.opt_int("num_experts_per_tok", 0);
+  c.moe_inter = r.opt_int("moe_intermediate_size", 0);
+  c.norm_topk = r.opt_bool("norm_topk_prob", false) ? 1 : 0;
+  if (r.rc) return r.rc;
+  if (c.n_experts > 0 && (c.top_k < 1 || c.top_k > c.n_experts || c.moe_inter < 1))
+    return fail(EMX_ERR_INVALID, "%s: num_experts %d needs num_experts_per_tok in [1, %d] and moe_intermediate_size",
+                path.c_str(), c.n_experts, c.n_experts);
+  // quantization: the model-wide {group_size, bits}, then MLX's per-module
+  // entries keyed by module name (one setting per class of projection)
+  const JVal* q = root.get("quantization");
+  if (!q) q = root.get("quantization_config");
+  int gs = 0, bits = 0;
+  if (!q || !quant_pair(*q, &gs, &bits))
+    return fail(EMX_ERR_INVALID, "%s: no quantization {group_size, bits}: the engine takes affine-quantized "
+                "checkpoints only", path.c_str());
+  int cls_gs[6], cls_bits[6], cls_set[6] = {0, 0, 0, 0, 0, 0};  // attn, mlp, embed, lm, router, expert
+  for (int k = 0; k < 6; ++k) {
+    cls_gs[k] = gs;
+    cls_bits[k] = bits;
+  }
+  for (const auto& kv : q->obj) {
+    const std::string& key = kv.first;
+    if (key == "group_size" || key == "bits" || key == "mode") continue;
+    int cls = -1;
+    if (key.find(".switch_mlp.") != std::string::npos) cls = 5;
+    else if (key.size() >= 8 && key.compare(key.size() - 8, 8, "mlp.gate") == 0) cls = 4;
+    else if (key.find(".self_attn.") != std::string::npos) cls = 0;
+    else if (key.find(".mlp.") != std::string::npos) cls = 1;
+    else if (key == "model.embed_tokens") cls = 2;
+    else if (key == "lm_head") cls = 3;
+    else continue;  // a module off this path
+    int g2, b2;
+    if (!quant_pair(kv.second, &g2, &b2))
+      return fail(EMX_ERR_INVALID, "%s: module '%s' is not quantized ({group_size, bits}); the engine takes "
+                  "affine-quantized projections only", path.c_str(), key.c_str());
+    if (cls_set[cls] && (cls_gs[cls] != g2 || cls_bits[cls] != b2))
+      return fail(EMX_ERR_INVALID, "%s: module '%s' (%d bits, group %d) differs from others of its kind (%d, %d); "
+                  "the engine takes one setting per kind", path.c_str(), key.c_str(), b2, g2, cls_bits[cls],
+                  cls_gs[cls]);
+    cls_set[cls] = 1;
+    cls_gs[cls] = g2;
+    cls_bits[cls] = b2;
+  }
+  c.attn_bits = cls_bits[0], c.attn_group = cls_gs[0];
+  c.mlp_bits = cls_bits[1], c.mlp_group = cls_gs[1];
+  c.embed_bits = cls_bits[2], c.embed_group = cls_gs[2];
+  c.lm_bits = cls_bits[3], c.lm_group = cls_gs[3];
+  c.router_bits = cls_bits[4], c.router_group = cls_gs[4];
+  c.expert_bits = cls_bits[5], c.expert_group = cls_gs[5];
+  c.kv_cap = kv_cap;
+  c.max_prefill = max_prefill;
+  *out = c;
+  return EMX_OK;
+}
+
 
 extern "C" int emx_safetensors_index(const char* file, emx_st_tensor* out, int cap, int* n) {
   if (!file || !n || (cap > 0 && !out)) return fail(EMX_ERR_INVALID, "emx_safetensors_index: null argument");

@@ -96,6 +96,7 @@ _SIGS = {
     "emx_qwen3_tensor_shape": (C.c_int, [C.c_void_p, C.c_char_p, C.POINTER(C.c_int64), C.POINTER(C.c_int),
                                          C.POINTER(C.c_int)]),
     "emx_safetensors_index": (C.c_int, [C.c_char_p, C.c_void_p, C.c_int, C.POINTER(C.c_int)]),
+    "emx_qwen3_config_from_dir": (C.c_int, [C.c_char_p, C.c_int, C.c_int, C.POINTER(QwenConfig)]),
     "emx_qwen3_prefill_chunked": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.POINTER(C.c_int32),
                                             C.c_void_p]),
     "emx_qwen3_set_sampling": (C.c_int, [C.c_void_p, C.c_float, C.c_float, C.c_int, C.c_uint64]),
@@ -433,6 +434,17 @@ class Qwen3Config:
             v = getattr(self, f[0])
             setattr(c, f[0], float(v) if f[1] is C.c_float else int(v))
         return c
+
+    @staticmethod
+    def from_dir(model_dir: str, kv_cap: int = 4096, max_prefill: int = 512) -> "Qwen3Config":
+        """Qwen3Config::from_dir: the shape and quantization of an MLX model
+        directory's config.json (host only)."""
+        c = QwenConfig()
+        _check(lib().emx_qwen3_config_from_dir(model_dir.encode(), kv_cap, max_prefill, C.byref(c)))
+        kw = {f[0]: getattr(c, f[0]) for f in QwenConfig._fields_}
+        for b in ("tied", "norm_topk"):
+            kw[b] = bool(kw[b])
+        return Qwen3Config(**kw)
 
 
 # The BASELINE configurations (random-init shapes of the named models).

@@ -212,6 +212,18 @@ typedef struct {
 
 typedef struct emx_qwen3 emx_qwen3;
 
+/* Host only: Qwen3Config::from_dir (crates/serve/src/config.rs:73-86, fields
+ * and serde defaults at config.rs:6-30, head_dim default at config.rs:88-91)
+ * from `model_dir`/config.json (or a config.json path), plus the MoE keys
+ * (num_experts, num_experts_per_tok, moe_intermediate_size, norm_topk_prob)
+ * and tie_word_embeddings (default true).  Quantization: the model-wide
+ * {group_size, bits} of "quantization" and MLX's per-module entries keyed by
+ * module name, one setting per kind (attention, dense MLP, embedding,
+ * lm_head, router, experts); an unquantized module or two settings within a
+ * kind fail with EMX_ERR_INVALID.  kv_cap and max_prefill are the engine's
+ * own (MAX_CAP, crates/serve/src/engine.rs:202). */
+int emx_qwen3_config_from_dir(const char* model_dir, int kv_cap, int max_prefill, emx_qwen3_config* out);
+
 /* Qwen3Engine::from_init (crates/serve/src/engine.rs:62-227): allocates the
  * weights, the static bf16 KV cache [layers][n_kv][kv_cap][head_dim] and the
  * decode state.  comm == NULL: one GPU; otherwise the model is tensor-parallel
