@@ -369,7 +369,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int qt = gridDim.x - 1 - blockIdx.x;  // the longest rows first
   const int h = blockIdx.y;
   const int kvh = h / (a.nq / a.nkv);
-  const int nt = qt + 1;  // key tiles at or before the diagonal
+  // key tiles at or before the diagonal: the cached prefix (whole tiles)
+  // first, then the chunk's own rows
+  const int nt = qt + 1 + a.prefix / kTBN;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -506,7 +508,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       } else {
 #pragma unroll
         for (int c = 0; c < 64; ++c) {
-          const bool vis = valid_q && kv0 + c <= qrow;
+          const bool vis = valid_q && kv0 + c <= qrow + a.prefix;
           s[c] = vis ? s[c] * sl2 : -INFINITY;
           mx = fmaxf(mx, s[c]);
         }
@@ -637,15 +639,16 @@ cudaError_t attn_prefill_launch(const AttnPrefillArgs& a, cudaStream_t st, int* 
   if (a.prefix < 0 || a.prefix > a.offset) return cudaErrorInvalidValue;
   const bool aligned =
       ((reinterpret_cast<uintptr_t>(a.q) | reinterpret_cast<uintptr_t>(a.kc) | reinterpret_cast<uintptr_t>(a.vc)) & 15) == 0;
-  // the tcgen05 kernel covers a chunk attending itself; a chunk that also
-  // attends cached rows before it goes through the mma.sync kernel
-  if (a.prefix == 0 && aligned) {
+  // the tcgen05 kernel takes a chunk attending itself, or a cached prefix of
+  // whole 128-row tiles (then the diagonal tiles stay aligned); other
+  // prefixes go through the mma.sync kernel
+  if (a.prefix % kTBN == 0 && aligned) {
     CUtensorMap tq, tk, tv;
+    const size_t k0 = (size_t)(a.offset - a.prefix) * kD;
+    const uint64_t rows = (uint64_t)a.prefix + (uint64_t)a.T;
     cudaError_t e = encode_rows(&tq, a.q, (uint64_t)a.T, (uint64_t)a.nq, (uint64_t)a.T * kD * 2);
-    if (e == cudaSuccess)
-      e = encode_rows(&tk, a.kc + (size_t)a.offset * kD, (uint64_t)a.T, (uint64_t)a.nkv, (uint64_t)a.cap * kD * 2);
-    if (e == cudaSuccess)
-      e = encode_rows(&tv, a.vc + (size_t)a.offset * kD, (uint64_t)a.T, (uint64_t)a.nkv, (uint64_t)a.cap * kD * 2);
+    if (e == cudaSuccess) e = encode_rows(&tk, a.kc + k0, rows, (uint64_t)a.nkv, (uint64_t)a.cap * kD * 2);
+    if (e == cudaSuccess) e = encode_rows(&tv, a.vc + k0, rows, (uint64_t)a.nkv, (uint64_t)a.cap * kD * 2);
     if (e != cudaSuccess) return e;
     e = cudaFuncSetAttribute(attn_prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem);
     if (e != cudaSuccess) return e;
