@@ -572,6 +572,19 @@ class Qwen3:
         _check(lib().emx_qwen3_create(ctx.h, C.byref(self._c), comm.h if comm else None, C.byref(h)))
         self.h = h.value
 
+    @classmethod
+    def from_dir(cls, ctx: Ctx, model_dir: str, kv_cap: int = 4096, max_prefill: int = 512,
+                 comm: Optional[Comm] = None) -> "Qwen3":
+        """Qwen3Engine::load: config.json, then the checkpoint files of an MLX
+        model directory (this rank's shard under TP / EP)."""
+        m = cls(ctx, Qwen3Config.from_dir(model_dir, kv_cap, max_prefill), comm)
+        try:
+            m.load_safetensors(model_dir)
+        except Exception:
+            m.close()
+            raise
+        return m
+
     def close(self):
         if self.h:
             lib().emx_qwen3_destroy(self.h)

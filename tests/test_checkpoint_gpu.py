@@ -156,3 +156,20 @@ def test_loader_refusals(ctx, tmp_path):
     assert "model.safetensors not found" in ei.value.msg
     a.close()
     b.close()
+
+
+def test_model_from_a_directory_with_config_json(ctx, tmp_path):
+    """Qwen3.from_dir: config.json (emx_qwen3_config_from_dir) then the
+    checkpoint; the model equals the one that wrote them."""
+    cfg = emx.Qwen3Config(**DENSE)
+    a = emx.Qwen3(ctx, cfg)
+    a.init_random(14)
+    emx.write_safetensors(str(tmp_path / "model.safetensors"), dump(a))
+    conf = {"hidden_size": cfg.hidden, "num_hidden_layers": cfg.layers, "intermediate_size": cfg.inter,
+            "num_attention_heads": cfg.n_q, "num_key_value_heads": cfg.n_kv, "head_dim": cfg.head_dim,
+            "vocab_size": cfg.vocab, "tie_word_embeddings": True, "quantization": {"group_size": 64, "bits": 4}}
+    (tmp_path / "config.json").write_text(json.dumps(conf))
+    b = emx.Qwen3.from_dir(ctx, str(tmp_path), kv_cap=cfg.kv_cap, max_prefill=cfg.max_prefill)
+    same_model(a, b)
+    a.close()
+    b.close()
