@@ -13,7 +13,7 @@
 //     (tile, half-span) units round-robin, and arrives on the stage's
 //     "empty" mbarrier when done — there is no CTA-wide barrier in the loop.
 // A unit: per slice quad, one conflict-free 128-bit shared load per word set
-// gives four slices' A registers; a LOP3 per register turns codes into bf16
+// gives four slices' A registers; a LOP3 per register turns codes into fp16
 // (magic-number exponent, exact) and an m16n8k16 MMA per slice adds the
 // four group dot products of rows g, g+8 at once: column j < 4 of B holds x
 // masked to group j, so only the lanes with g == t load x (two adjacent
@@ -21,8 +21,9 @@
 // block; x groups sit 2*gs + 16 bytes apart, so the four loading lanes hit
 // four different bank groups.  Each warp runs two units at once, interleaved
 // quad by quad, so one unit's accumulator drain overlaps the other's math.
-// Then per row s*dot + (b - C*s)*sum(x_g) in fp32 — the MLX qmv
-// factorisation, C being the magic offset — reduced over the lane pair and
+// x is staged in fp16 after an exact power-of-two scaling (pgemv_dev.cuh).
+// Then per row s*(dot - 1024*sum x'') + b*sum x' in fp32 — the MLX qmv
+// factorisation, 1024 being the magic offset — reduced over the lane pair and
 // stored to a per-(row, span, half-span) slot.  After the last stage one
 // barrier, then the epilogue sums each row's slots in order and applies the
 // fused output step (store / residual / SwiGLU / argmax / fp32 partial).
@@ -48,6 +49,7 @@ __global__ void __launch_bounds__(kThreads, 2) pgemv_kernel(const GemvArgs a, co
   uint64_t* empty = full + kMaxBuf;
   float* scratch = reinterpret_cast<float*>(smem + 128);  // 32 floats
   float* inv = scratch + 32;                             // 8 floats
+  float* xsc = scratch + 40;                             // 2^e of the x staging
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + 320);
   uint64_t* nwbar = reinterpret_cast<uint64_t*>(smem + 336);
   const PgSmem sm = pg_smem(smem, geo);
@@ -152,7 +154,7 @@ __global__ void __launch_bounds__(kThreads, 2) pgemv_kernel(const GemvArgs a, co
   }
 
   pg_prologue<GS, SyncCta>(a, geo, sm, reinterpret_cast<const bf16*>(smem + geo.off_nw), norm_pre ? nwbar : nullptr,
-                           0u, scratch, inv, abort_flag, tok, tid, kThreads, blockIdx.x == 0);
+                           0u, scratch, inv, xsc, abort_flag, tok, tid, kThreads, blockIdx.x == 0);
   __syncthreads();
 
   float best_v = -INFINITY;
@@ -185,7 +187,7 @@ __global__ void __launch_bounds__(kThreads, 2) pgemv_kernel(const GemvArgs a, co
   }
   __syncthreads();
 
-  pg_epilogue(a, geo, sm.red, lb0, lb1, tid, kThreads, res_early, res_pre, best_v, best_i);
+  pg_epilogue(a, geo, sm.red, lb0, lb1, tid, kThreads, res_early, res_pre, best_v, best_i, *xsc);
   if (a.epi == kEpiF32 && a.peer) {
     __shared__ unsigned published;
     pg_peer_publish<SyncCta>(a, tid, &published);
@@ -236,9 +238,11 @@ __global__ void pack_kernel(const uint32_t* __restrict__ w, const bf16* __restri
     const int k = 4 * (4 * q + wi);  // first of the slice's four group offsets
     unsigned char* wp = tbase + ((hs * QH + q) * HW) * 512 + lane * 16 + wi * 4;
     if (BITS == 4) {
-      const uint32_t word = code(rA, G, k) | (code(rB, G, k) << 4) | (code(rA, G, k + 2) << 8) |
-                            (code(rB, G, k + 2) << 12) | (code(rA, G, k + 1) << 16) | (code(rB, G, k + 1) << 20) |
-                            (code(rA, G, k + 3) << 24) | (code(rB, G, k + 3) << 28);
+      // low nibbles of the two halves: A registers 0 / 1 (rows g, g+8 at k, k+1);
+      // high nibbles: registers 2 / 3 (rows g, g+8 at k+2, k+3)
+      const uint32_t word = code(rA, G, k) | (code(rA, G, k + 2) << 4) | (code(rB, G, k) << 8) |
+                            (code(rB, G, k + 2) << 12) | (code(rA, G, k + 1) << 16) | (code(rA, G, k + 3) << 20) |
+                            (code(rB, G, k + 1) << 24) | (code(rB, G, k + 3) << 28);
       *reinterpret_cast<uint32_t*>(wp) = word;
     } else {
       const uint32_t w0 = code(rA, G, k) | (code(rB, G, k) << 8) | (code(rA, G, k + 1) << 16) | (code(rB, G, k + 1) << 24);

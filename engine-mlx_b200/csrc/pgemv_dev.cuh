@@ -7,15 +7,20 @@
 // The packed layout these functions read is described in pgemv.cuh.  The
 // math per unit (16 rows x one half-span of 4 groups):
 //   one conflict-free 128-bit shared load per word set gives four slices' A
-//   registers; a LOP3 per register turns codes into bf16 (magic-number
-//   exponent, exact) and an m16n8k16 MMA per slice adds the four group dot
-//   products of rows g, g+8 at once: column j < 4 of B holds x masked to
-//   group j, so only the lanes with g == t load x and the other lanes read a
-//   zero block.  Then per row s*dot + (b - C*s)*sum(x_g) in fp32 (the MLX qmv
-//   factorisation, C being the magic offset), reduced over the lane pair and
-//   stored to a per-(row, span, half-span) slot; the epilogue sums a row's
-//   slots in a fixed order, so the result does not depend on which CTA or
-//   warp computed a unit.
+//   registers; a LOP3 per register places codes in the mantissa of an fp16
+//   1024 (magic-number exponent, exact: 1024 + q, or 1024 + 16 q for the
+//   upper nibble of an int4 byte) and an m16n8k16 f16 MMA per slice adds the
+//   four group dot products of rows g, g+8 at once: column j < 4 of B holds
+//   x masked to group j, so only the lanes with g == t load x and the other
+//   lanes read a zero block.  x is staged in fp16 after an exact
+//   power-of-two scaling x' = x * 2^-e that keeps the largest |x'| below 2^15
+//   (so every bf16 value above 2^-14 of the largest keeps all its bits); the
+//   x elements that meet an upper nibble are stored as x' / 16.  Then per row
+//   s*(dot - 1024*sum x'') + b*sum x' in fp32 (the MLX qmv factorisation; the
+//   1024 offsets cancel against the sum of the staged fp16 values x''),
+//   reduced over the lane pair and stored to a per-(row, span, half-span)
+//   slot; the epilogue sums a row's slots in a fixed order and multiplies by
+//   2^e, so the result does not depend on which CTA or warp computed a unit.
 #pragma once
 #include "attn_decode.cuh"
 #include "qgemv.cuh"
@@ -27,6 +32,7 @@ constexpr int kMaxBuf = 8;
 
 struct PGeom {
   int K, ng, S;
+  int bits;  // code width: int4 rows stage their upper-nibble x elements as x' / 16
   int tile_bytes, a_bytes;
   int halves;
   int lb_total;
@@ -45,13 +51,14 @@ struct PGeom {
 __host__ __device__ inline int ptile_bytes(int bits, int gs) { return 16 * 8 * gs * bits / 8 + 512; }
 
 // Shared-memory carve-up from byte `base` on: x slots, norm weights, the zero
-// block, group sums of x, the row-slot reduction area, then the stage ring.
+// block, the per-group sums of x (pairs of groups: 1024 * sum x'' of both,
+// then sum x' of both), the row-slot reduction area, then the stage ring.
 __host__ __device__ inline int pgeom_layout(PGeom& g, int gs, int base = 384) {
   g.off_x = base;
   g.off_nw = g.off_x + g.x_slots * g.xslot_bytes;
   g.off_zero = g.off_nw + g.nw_bytes;
   g.off_xs = g.off_zero + 2 * gs;
-  g.off_red = g.off_xs + ((g.x_slots * g.S * 8 * 4 + 15) & ~15);
+  g.off_red = g.off_xs + ((g.x_slots * g.S * 8 * 8 + 15) & ~15);
   g.off_buf = (g.off_red + g.red_rows * g.S * 2 * 4 + 127) & ~127;
   return g.off_buf + g.nbuf * g.stage_bytes;
 }
@@ -60,6 +67,7 @@ __host__ __device__ inline int pgeom_layout(PGeom& g, int gs, int base = 384) {
 inline void pgeom_make(PGeom* g, int K, int bits, int gs, int epi, int lb_total, int stage_tiles, int nbuf,
                        int x_slots, int lbs_max, bool norm_room) {
   g->K = K;
+  g->bits = bits;
   g->ng = K / gs;
   g->S = (g->ng + 7) / 8;
   g->tile_bytes = ptile_bytes(bits, gs);
@@ -230,22 +238,88 @@ __device__ __forceinline__ unsigned char* pg_xchunk(const PGeom& geo, const PgSm
   return sm.xsm + (size_t)slot * geo.xslot_bytes + (c / CPG) * geo.gstride + (c % CPG) * 16;
 }
 
-// Stores chunk c (bf16 bits `raw`, values `o`) of x slot `slot` and, from
-// the CPG lanes that hold one group (consecutive c in consecutive lanes; all
-// 32 lanes call), the group's sum of x.
+// Exponent e of the power-of-two staging scale for values of magnitude at
+// most `bound`: |v| * 2^-e < 2^15 (bound < 2^E from the float's own exponent
+// field, e = E - 15), clamped to [-111, 113] so that 2^e, 2^-e and
+// 2^-(e+4) are normal floats.  bound <= 0 or NaN: 0.
+__device__ __forceinline__ int pg_scale_exp(float bound) {
+  if (!(bound > 0.f)) return 0;
+  const int E = (int)((__float_as_uint(bound) >> 23) & 0xffu) - 126;
+  return min(max(E - 15, -111), 113);
+}
+
+// 2^e as a float, -126 <= e <= 127.
+__device__ __forceinline__ float pg_pow2(int e) { return __int_as_float((127 + e) << 23); }
+
+// Two floats to packed fp16 (round to nearest even).
+__device__ __forceinline__ uint32_t h2bits(float lo, float hi) {
+  const __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// Block-wide (sum, max, max) of three per-thread values over the threads
+// [0, nthr) that call it; every thread gets the result (warp totals summed
+// in warp order).  `scratch` holds >= 3 * warps floats.
+template <class Sync>
+__device__ __forceinline__ float3 part_reduce3(float s, float m1, float m2, float* scratch, int tid, int nthr) {
+  const int lane = tid & 31, warp = tid >> 5, nw = (nthr + 31) >> 5;
+  s = warp_sum(s);
+  m1 = warp_max(m1);
+  m2 = warp_max(m2);
+  Sync::sync();
+  if (lane == 0) {
+    scratch[warp] = s;
+    scratch[nw + warp] = m1;
+    scratch[2 * nw + warp] = m2;
+  }
+  Sync::sync();
+  float3 r = make_float3(0.f, 0.f, 0.f);
+  for (int w = 0; w < nw; ++w) {
+    r.x += scratch[w];
+    r.y = fmaxf(r.y, scratch[nw + w]);
+    r.z = fmaxf(r.z, scratch[2 * nw + w]);
+  }
+  return r;
+}
+
+// Stores chunk c (values `o`, bf16 values held as floats) of x slot `slot`
+// in fp16 scaled by sc = 2^-e (the elements k % 4 >= 2 of an int4 matrix by
+// sc / 16: they meet the upper nibble, whose magic-number code is 16x) and,
+// from the CPG lanes that hold one group (consecutive c in consecutive lanes;
+// all 32 lanes call), the group's 1024 * sum x'' and sum x'.
 template <int GS>
-__device__ __forceinline__ void pg_emit(const PGeom& geo, const PgSmem& sm, int slot, int c, bool valid, uint4 raw,
-                                        const float (&o)[8]) {
+__device__ __forceinline__ void pg_emit(const PGeom& geo, const PgSmem& sm, int slot, int c, bool valid,
+                                        const float (&o)[8], float sc) {
   constexpr int CPG = GS / 8;
-  float ps = 0.f;
+  const float sh = geo.bits == 4 ? sc * 0.0625f : sc;
+  float sx = 0.f, sxx = 0.f;
   if (valid) {
-    *reinterpret_cast<uint4*>(pg_xchunk<GS>(geo, sm, slot, c)) = raw;
+    float h[8];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) ps += o[e];
+    for (int e = 0; e < 8; ++e) {
+      const float xs = __fmul_rn(o[e], sc);
+      h[e] = __half2float(__float2half_rn((e & 2) ? __fmul_rn(o[e], sh) : xs));
+      sx += xs;
+      sxx += h[e];
+    }
+    uint4 pk;
+    pk.x = h2bits(h[0], h[1]);
+    pk.y = h2bits(h[2], h[3]);
+    pk.z = h2bits(h[4], h[5]);
+    pk.w = h2bits(h[6], h[7]);
+    *reinterpret_cast<uint4*>(pg_xchunk<GS>(geo, sm, slot, c)) = pk;
   }
 #pragma unroll
-  for (int off = 1; off < CPG; off <<= 1) ps += __shfl_xor_sync(0xffffffffu, ps, off);
-  if (valid && (c % CPG) == 0) sm.xs[slot * geo.S * 8 + c / CPG] = ps;
+  for (int off = 1; off < CPG; off <<= 1) {
+    sx += __shfl_xor_sync(0xffffffffu, sx, off);
+    sxx += __shfl_xor_sync(0xffffffffu, sxx, off);
+  }
+  if (valid && (c % CPG) == 0) {
+    const int G = c / CPG;
+    float* p = sm.xs + (size_t)slot * geo.S * 16 + (G >> 1) * 4 + (G & 1);
+    p[0] = 1024.0f * sxx;
+    p[2] = sx;
+  }
 }
 
 // Zero padding after x: x past K (whole chunks), the zero block, group sums
@@ -259,7 +333,40 @@ __device__ __forceinline__ void pg_pad(const PGeom& geo, const PgSmem& sm, int t
   for (int i = tid; i < GS / 2; i += nthr) reinterpret_cast<uint32_t*>(sm.zero)[i] = 0u;
   const int S = geo.S;
   const int gpad = S * 8 - geo.ng;
-  for (int i = tid; i < geo.x_slots * gpad; i += nthr) sm.xs[(i / gpad) * S * 8 + geo.ng + i % gpad] = 0.f;
+  for (int i = tid; i < geo.x_slots * gpad; i += nthr) {
+    const int G = geo.ng + i % gpad;
+    float* p = sm.xs + (size_t)(i / gpad) * S * 16 + (G >> 1) * 4 + (G & 1);
+    p[0] = 0.f;
+    p[2] = 0.f;
+  }
+}
+
+// The staged bf16 source of x slots [0, nslots) (chunk c of a slot staged
+// by thread c % nthr), max |x| per thread in `mx`: one reduction fixes the
+// scale, then each thread converts the chunks it staged to the fp16 layout.
+template <int GS, class Sync>
+__device__ __forceinline__ void pg_convert_staged(const PGeom& geo, const PgSmem& sm, int nslots, float mx,
+                                                  float* scratch, float* xsc, int tid, int nthr) {
+  const float3 r = part_reduce3<Sync>(0.f, mx, 0.f, scratch, tid, nthr);
+  const int e = pg_scale_exp(r.y);
+  const float sc = pg_pow2(-e);
+  if (tid == 0) *xsc = pg_pow2(e);
+  const int nch = geo.K / 8;
+  for (int slot = 0; slot < nslots; ++slot) {
+#pragma unroll 1
+    for (int it = 0; it * nthr < nch; ++it) {
+      const int c = it * nthr + tid;
+      const bool valid = c < nch;
+      float v[8];
+      if (valid) {
+        unpack8f(*reinterpret_cast<const uint4*>(pg_xchunk<GS>(geo, sm, slot, c)), v);
+      } else {
+#pragma unroll
+        for (int e2 = 0; e2 < 8; ++e2) v[e2] = 0.f;
+      }
+      pg_emit<GS>(geo, sm, slot, c, valid, v, sc);
+    }
+  }
 }
 
 // kProMerge: x = the decode attention output, merged from the splits'
@@ -267,109 +374,113 @@ __device__ __forceinline__ void pg_pad(const PGeom& geo, const PgSmem& sm, int t
 // kAttnDeferSplits), with the attention's own arithmetic (attn_decode.cu):
 // M = max m_s, w_s = exp(m_s - M), den = the butterfly sum of fma(w_s, l_s)
 // over the split lanes, out = bf16(sum_s fma(w_s / den, acc_s)) in split
-// order -- the bits the attention's merge would store.  Returns false when
-// the attention merged itself (x is then read from a.x).
+// order -- the bits the attention's merge would store.  The merged bf16
+// values are staged in x slot 0 (chunk c by thread c % nthr) and their max
+// |x| accumulated in `mx`.  Returns false when the attention merged itself
+// (x is then read from a.x).
 template <int GS>
 __device__ __forceinline__ bool pg_merge_attn(const GemvArgs& a, const PGeom& geo, const PgSmem& sm, int tid,
-                                              int nthr, bool lead) {
+                                              int nthr, bool lead, float& mx) {
   const int ns = attn_active_splits(*a.attn_pos + 1, a.attn_grid);
   if (ns < 1 || ns > kAttnDeferSplits) return false;
   constexpr int HD = 128, PS = HD + 2;
   const int hpg = a.attn_hpg;
   const size_t sstride = (size_t)hpg * PS;  // between the splits of one head
   const int nch = geo.K / 8;
-  for (int it = 0; it * nthr < nch; ++it) {
-    const int c = it * nthr + tid;
-    const bool valid = c < nch;
+  for (int c = tid; c < nch; c += nthr) {
     float o[8];
 #pragma unroll
     for (int e = 0; e < 8; ++e) o[e] = 0.f;
-    if (valid) {
-      const int q = c / (HD / 8), d0 = (c % (HD / 8)) * 8;
-      const float* pb = a.attn_part + ((size_t)(q / hpg) * ns * hpg + (q % hpg)) * PS;
-      float ms[kAttnDeferSplits], ls[kAttnDeferSplits];
-      float2 v[kAttnDeferSplits][4];
+    const int q = c / (HD / 8), d0 = (c % (HD / 8)) * 8;
+    const float* pb = a.attn_part + ((size_t)(q / hpg) * ns * hpg + (q % hpg)) * PS;
+    float ms[kAttnDeferSplits], ls[kAttnDeferSplits];
+    float2 v[kAttnDeferSplits][4];
 #pragma unroll
-      for (int s2 = 0; s2 < kAttnDeferSplits; ++s2) {
-        ms[s2] = -INFINITY;
-        ls[s2] = 0.f;
+    for (int s2 = 0; s2 < kAttnDeferSplits; ++s2) {
+      ms[s2] = -INFINITY;
+      ls[s2] = 0.f;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) v[s2][j] = make_float2(0.f, 0.f);
-        if (s2 < ns) {
-          const float* ps = pb + s2 * sstride;
-          ms[s2] = __ldcg(ps);
-          ls[s2] = __ldcg(ps + 1);
+      for (int j = 0; j < 4; ++j) v[s2][j] = make_float2(0.f, 0.f);
+      if (s2 < ns) {
+        const float* ps = pb + s2 * sstride;
+        ms[s2] = __ldcg(ps);
+        ls[s2] = __ldcg(ps + 1);
 #pragma unroll
-          for (int j = 0; j < 4; ++j) v[s2][j] = __ldcg(reinterpret_cast<const float2*>(ps + 2 + d0 + 2 * j));
-        }
+        for (int j = 0; j < 4; ++j) v[s2][j] = __ldcg(reinterpret_cast<const float2*>(ps + 2 + d0 + 2 * j));
       }
-      float M = -INFINITY;
-#pragma unroll
-      for (int s2 = 0; s2 < kAttnDeferSplits; ++s2) M = fmaxf(M, ms[s2]);
-      float w[kAttnDeferSplits], t[kAttnDeferSplits];
-#pragma unroll
-      for (int s2 = 0; s2 < kAttnDeferSplits; ++s2) {
-        w[s2] = ms[s2] == -INFINITY ? 0.f : expf(ms[s2] - M);
-        t[s2] = fmaf(w[s2], ls[s2], 0.f);
-      }
-      static_assert(kAttnDeferSplits == 4, "the butterfly below covers four split lanes");
-      const float den = (t[0] + t[2]) + (t[1] + t[3]);
-#pragma unroll
-      for (int s2 = 0; s2 < kAttnDeferSplits; ++s2) {
-        if (s2 < ns) {
-          const float sw = __fdiv_rn(w[s2], den);
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            o[2 * j] = fmaf(sw, v[s2][j].x, o[2 * j]);
-            o[2 * j + 1] = fmaf(sw, v[s2][j].y, o[2 * j + 1]);
-          }
-        }
-      }
-#pragma unroll
-      for (int e = 0; e < 8; ++e) o[e] = bfround(o[e]);
     }
-    const uint4 pk = valid ? pack8exact(o) : make_uint4(0u, 0u, 0u, 0u);
-    pg_emit<GS>(geo, sm, 0, c, valid, pk, o);
-    if (valid && lead && a.x_out) *reinterpret_cast<uint4*>(a.x_out + c * 8) = pk;
+    float M = -INFINITY;
+#pragma unroll
+    for (int s2 = 0; s2 < kAttnDeferSplits; ++s2) M = fmaxf(M, ms[s2]);
+    float w[kAttnDeferSplits], t[kAttnDeferSplits];
+#pragma unroll
+    for (int s2 = 0; s2 < kAttnDeferSplits; ++s2) {
+      w[s2] = ms[s2] == -INFINITY ? 0.f : expf(ms[s2] - M);
+      t[s2] = fmaf(w[s2], ls[s2], 0.f);
+    }
+    static_assert(kAttnDeferSplits == 4, "the butterfly below covers four split lanes");
+    const float den = (t[0] + t[2]) + (t[1] + t[3]);
+#pragma unroll
+    for (int s2 = 0; s2 < kAttnDeferSplits; ++s2) {
+      if (s2 < ns) {
+        const float sw = __fdiv_rn(w[s2], den);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          o[2 * j] = fmaf(sw, v[s2][j].x, o[2 * j]);
+          o[2 * j + 1] = fmaf(sw, v[s2][j].y, o[2 * j + 1]);
+        }
+      }
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      o[e] = bfround(o[e]);
+      mx = fmaxf(mx, fabsf(o[e]));
+    }
+    const uint4 pk = pack8exact(o);
+    *reinterpret_cast<uint4*>(pg_xchunk<GS>(geo, sm, 0, c)) = pk;
+    if (lead && a.x_out) *reinterpret_cast<uint4*>(a.x_out + c * 8) = pk;
   }
   return true;
 }
 
-// x prologue: x in padded groups (zero past K to whole spans) and the group
-// sums of x, built by threads [0, nthr).  The `lead` CTA also stores the new
-// residual of embedding / add prologues to a.x_out.  Norm prologues take the
-// weights from `nwsm`, which becomes valid when `nwbar` completes phase
-// `nw_parity` (nwbar == nullptr: already valid).  `scratch` holds >= 32
-// floats, `inv` 8.
+// x prologue: x in padded groups (zero past K to whole spans), fp16 after the
+// power-of-two scale (2^e to *xsc), and the group sums, built by threads
+// [0, nthr).  The `lead` CTA also stores the new residual of embedding / add
+// prologues to a.x_out.  Norm prologues take the weights from `nwsm`, which
+// becomes valid when `nwbar` completes phase `nw_parity` (nwbar == nullptr:
+// already valid); their scale comes from the bound max|v| * inv * max|w| of
+// the normalised values.  `scratch` holds >= 32 floats, `inv` 8.
 template <int GS, class Sync>
 __device__ __forceinline__ void pg_prologue(const GemvArgs& a, const PGeom& geo, const PgSmem& sm,
                                             const bf16* nwsm, uint64_t* nwbar, uint32_t nw_parity, float* scratch,
-                                            float* inv, volatile int* abort_flag, int tok, int tid, int nthr,
-                                            bool lead) {
+                                            float* inv, float* xsc, volatile int* abort_flag, int tok, int tid,
+                                            int nthr, bool lead) {
   const int K = geo.K;
   const int nch = K / 8;
-  // o holds bf16 values (the norm output is rounded per element)
-  auto emit = [&](int slot, int c, bool valid, const float (&o)[8]) {
-    pg_emit<GS>(geo, sm, slot, c, valid, valid ? pack8exact(o) : make_uint4(0u, 0u, 0u, 0u), o);
-  };
-  const bool merged = a.pro == kProMerge && pg_merge_attn<GS>(a, geo, sm, tid, nthr, lead);
-  if (merged) {
-  } else if (a.pro == kProX || a.pro == kProMerge) {
-    for (int slot = 0; slot < geo.x_slots; ++slot) {
+  const bool norm = a.pro == kProNorm || a.pro == kProEmbedNorm || a.pro == kProAddNorm;
+  if (!norm) {
+    // the source in bf16 (merged attention output, or x as given in every
+    // slot), then one scale for all of it
+    float mx = 0.f;
+    const bool merged = a.pro == kProMerge && pg_merge_attn<GS>(a, geo, sm, tid, nthr, lead, mx);
+    const int nslots = merged ? 1 : geo.x_slots;
+    if (!merged) {
+      for (int slot = 0; slot < nslots; ++slot) {
 #pragma unroll 1
-      for (int it = 0; it * nthr < nch; ++it) {
-        const int c = it * nthr + tid;
-        const bool valid = c < nch;
-        const uint4 raw =
-            valid ? *reinterpret_cast<const uint4*>(a.x + (size_t)slot * K + c * 8) : make_uint4(0u, 0u, 0u, 0u);
-        float v[8];
-        unpack8f(raw, v);
-        pg_emit<GS>(geo, sm, slot, c, valid, raw, v);
+        for (int c = tid; c < nch; c += nthr) {
+          const uint4 raw = *reinterpret_cast<const uint4*>(a.x + (size_t)slot * K + c * 8);
+          float v[8];
+          unpack8f(raw, v);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) mx = fmaxf(mx, fabsf(v[e]));
+          *reinterpret_cast<uint4*>(pg_xchunk<GS>(geo, sm, slot, c)) = raw;
+        }
       }
     }
+    pg_convert_staged<GS, Sync>(geo, sm, nslots, mx, scratch, xsc, tid, nthr);
   } else {
     // pass 1: pre-norm source staged in the x buffer, sums of squares per
-    // norm group
+    // norm group, max |v|
     const int groups = a.norm_groups > 0 ? a.norm_groups : 1;
     const int gd = K / groups;
     const bool store = (a.pro == kProEmbedNorm || a.pro == kProAddNorm) && lead && a.x_out;
@@ -401,13 +512,17 @@ __device__ __forceinline__ void pg_prologue(const GemvArgs& a, const PGeom& geo,
     float ssg[8];
 #pragma unroll
     for (int gi = 0; gi < 8; ++gi) ssg[gi] = 0.f;
+    float mv = 0.f;
 #pragma unroll 1
     for (int c = tid; c < nch; c += nthr) {
       float v[8];
       src8(a, c, tok, v, pworld ? psrc : nullptr, pworld);
       float ss = 0.f;
 #pragma unroll
-      for (int e = 0; e < 8; ++e) ss = fmaf(v[e], v[e], ss);
+      for (int e = 0; e < 8; ++e) {
+        ss = fmaf(v[e], v[e], ss);
+        mv = fmaxf(mv, fabsf(v[e]));
+      }
       const int grp = (c * 8) / gd;
 #pragma unroll
       for (int gi = 0; gi < 8; ++gi)
@@ -416,19 +531,38 @@ __device__ __forceinline__ void pg_prologue(const GemvArgs& a, const PGeom& geo,
       *reinterpret_cast<uint4*>(pg_xchunk<GS>(geo, sm, 0, c)) = pk;
       if (store) *reinterpret_cast<uint4*>(a.x_out + c * 8) = pk;
     }
+    // the norm weights (requested before the dependency wait) and their max
+    if (nwbar && !wait_or_abort(nwbar, nw_parity, abort_flag, a.status)) {
+      // no weights: the outputs are garbage and the status word says so
+    }
+    float mw = 0.f;
+#pragma unroll 1
+    for (int c = tid; c < nch; c += nthr) {
+      float w[8];
+      unpack8f(*reinterpret_cast<const uint4*>(nwsm + c * 8), w);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) mw = fmaxf(mw, fabsf(w[e]));
+    }
+    float iv1 = 0.f, ivmax = 0.f, vmax = 0.f, wmax = 0.f;
     for (int gi = 0; gi < groups; ++gi) {
       float sv = 0.f;
 #pragma unroll
       for (int q = 0; q < 8; ++q)
         if (q == gi) sv = ssg[q];
-      const float ss = part_sum<Sync>(sv, scratch, tid, nthr);
-      if (tid == 0) inv[gi] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)gd), a.eps)));
+      const float3 r = part_reduce3<Sync>(sv, mv, mw, scratch, tid, nthr);
+      const float iv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(r.x, (float)gd), a.eps)));
+      if (gi == 0) iv1 = iv;
+      if (groups > 1 && tid == 0) inv[gi] = iv;
+      ivmax = fmaxf(ivmax, iv);
+      vmax = r.y;
+      wmax = r.z;
     }
-    Sync::sync();
+    if (groups > 1) Sync::sync();
+    // |bf16(bf16(v * inv) * w)| <= max|v| * inv * max|w| * (1 + 2^-8)^2
+    const int e = pg_scale_exp(vmax * ivmax * wmax * 1.02f);
+    const float sc = pg_pow2(-e);
+    if (tid == 0) *xsc = pg_pow2(e);
     // pass 2: scale and weight in place (each thread rewrites its own chunks)
-    if (nwbar && !wait_or_abort(nwbar, nw_parity, abort_flag, a.status)) {
-      // no weights: the outputs are garbage and the status word says so
-    }
 #pragma unroll 1
     for (int it = 0; it * nthr < nch; ++it) {
       const int c = it * nthr + tid;
@@ -438,16 +572,16 @@ __device__ __forceinline__ void pg_prologue(const GemvArgs& a, const PGeom& geo,
         float v[8], w[8];
         unpack8f(*reinterpret_cast<const uint4*>(pg_xchunk<GS>(geo, sm, 0, c)), v);
         unpack8f(*reinterpret_cast<const uint4*>(nwsm + c * 8), w);
-        const float iv = inv[(c * 8) / gd];
+        const float iv = groups == 1 ? iv1 : inv[(c * 8) / gd];
 #pragma unroll
-        for (int e = 0; e < 8; ++e)
-          o[e] = groups == 1 ? bfround(__fmul_rn(bfround(__fmul_rn(v[e], iv)), w[e]))
-                             : bfround(__fmul_rn(__fmul_rn(v[e], iv), w[e]));
+        for (int e2 = 0; e2 < 8; ++e2)
+          o[e2] = groups == 1 ? bfround(__fmul_rn(bfround(__fmul_rn(v[e2], iv)), w[e2]))
+                              : bfround(__fmul_rn(__fmul_rn(v[e2], iv), w[e2]));
       } else {
 #pragma unroll
-        for (int e = 0; e < 8; ++e) o[e] = 0.f;
+        for (int e2 = 0; e2 < 8; ++e2) o[e2] = 0.f;
       }
-      emit(0, c, valid, o);
+      pg_emit<GS>(geo, sm, 0, c, valid, o, sc);
     }
   }
   pg_pad<GS>(geo, sm, tid, nthr);
@@ -470,10 +604,7 @@ __device__ __forceinline__ void pg_stage(const PGeom& geo, const PgSmem& sm, con
   const int lb_tiles = halves * S;
   const int g = lane >> 2, t = lane & 3, t1 = t & 1;
   const bool has_x = g == t;  // the lanes whose B column carries x
-  const uint32_t MASK = 0x000F000Fu;
-  const uint32_t MAGIC_LO = 0x43004300u;  // bf16 128 + nibble
-  const uint32_t MAGIC_HI = 0x45004500u;  // bf16 2048 + 16 * nibble
-  constexpr float C = BITS == 4 ? 128.0f : 2176.0f;
+  const uint32_t M16 = 0x64006400u;  // fp16 1024 in both halves: 1024 + code is exact
   // tile -> (logical block, half, span) by a 64-bit multiply, not a
   // division: floor(n / d) == (n * ceil(2^32 / d)) >> 32 for n < 2^32 / d
   // (the magic is 2^32 itself for d == 1, hence 64 bits; the host computes
@@ -483,7 +614,7 @@ __device__ __forceinline__ void pg_stage(const PGeom& geo, const PgSmem& sm, con
     const unsigned char* aw;   // this lane's code words
     const unsigned char* px;   // x of the unit's group for this lane (or the zero block)
     const unsigned char* sbp;  // this lane's scale/bias record
-    const float* xg;           // the group sums
+    const float* xg;           // the group sums {1024 sum x'' (2 groups), sum x' (2 groups)}
     int slot;                  // red index of row g (row g+8 is 8 rows on)
   };
   auto unit = [&](int u) -> Unit {
@@ -499,12 +630,15 @@ __device__ __forceinline__ void pg_stage(const PGeom& geo, const PgSmem& sm, con
     r.aw = tile + hs * (A_BYTES / 2) + lane * 16;
     r.px = has_x ? sm.xsm + (size_t)xsl * geo.xslot_bytes + (size_t)(sp * 8 + hs * 4 + t) * geo.gstride : sm.zero;
     r.sbp = tile + A_BYTES + hs * 256 + (g * 2 + t1) * 16;
-    r.xg = sm.xs + xsl * S * 8 + sp * 8 + hs * 4 + 2 * t1;
+    r.xg = sm.xs + (size_t)xsl * S * 16 + (sp * 4 + hs * 2 + t1) * 4;
     r.slot = (((lb - lb0) * halves + h) * 16 + g) * SKP + sp * 2 + hs;
     return r;
   };
-  // slice quad q of a unit: HW code loads, two x loads, four (int4) or
-  // eight (int8) MMAs into four independent accumulators
+  // slice quad q of a unit: HW code loads, two x loads, four MMAs into four
+  // independent accumulators.  int4 word: nibbles 0 / 4 (bits 0-3, 16-19) row
+  // g at k, k+1; nibbles 2 / 6 row g+8 at k, k+1; nibbles 1 / 5 row g at k+2,
+  // k+3 (x16: x staged / 16 there); nibbles 3 / 7 row g+8 at k+2, k+3.  int8
+  // words u (k, k+1) and v (k+2, k+3): bytes 0 / 2 row g, bytes 1 / 3 row g+8.
   auto quad = [&](const Unit& U, int q, float (&d)[4][4]) {
     uint4 wa[HW];
 #pragma unroll
@@ -517,18 +651,15 @@ __device__ __forceinline__ void pg_stage(const PGeom& geo, const PgSmem& sm, con
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       if (BITS == 4) {
-        const uint32_t w = w0v[j];
-        mma_bf16_16816(d[j], lop3_and_or(w, MASK, MAGIC_LO), lop3_and_or(w >> 4, MASK, MAGIC_LO),
-                       lop3_and_or(w >> 8, MASK, MAGIC_LO), lop3_and_or(w >> 12, MASK, MAGIC_LO), bx[2 * j],
-                       bx[2 * j + 1]);
+        const uint32_t w = w0v[j], w8 = w >> 8;
+        mma_f16_16816(d[j], lop3_and_or(w, 0x000F000Fu, M16), lop3_and_or(w8, 0x000F000Fu, M16),
+                      lop3_and_or(w, 0x00F000F0u, M16), lop3_and_or(w8, 0x00F000F0u, M16), bx[2 * j],
+                      bx[2 * j + 1]);
       } else {
         const uint32_t u0 = w0v[j], u1 = w1v[j];
-        mma_bf16_16816(d[(j & 1) * 2], lop3_and_or(u0, MASK, MAGIC_LO), lop3_and_or(u0 >> 8, MASK, MAGIC_LO),
-                       lop3_and_or(u1, MASK, MAGIC_LO), lop3_and_or(u1 >> 8, MASK, MAGIC_LO), bx[2 * j],
-                       bx[2 * j + 1]);
-        mma_bf16_16816(d[(j & 1) * 2 + 1], lop3_and_or(u0 >> 4, MASK, MAGIC_HI),
-                       lop3_and_or(u0 >> 12, MASK, MAGIC_HI), lop3_and_or(u1 >> 4, MASK, MAGIC_HI),
-                       lop3_and_or(u1 >> 12, MASK, MAGIC_HI), bx[2 * j], bx[2 * j + 1]);
+        mma_f16_16816(d[j], lop3_and_or(u0, 0x00FF00FFu, M16), lop3_and_or(u0 >> 8, 0x00FF00FFu, M16),
+                      lop3_and_or(u1, 0x00FF00FFu, M16), lop3_and_or(u1 >> 8, 0x00FF00FFu, M16), bx[2 * j],
+                      bx[2 * j + 1]);
       }
     }
   };
@@ -539,18 +670,15 @@ __device__ __forceinline__ void pg_stage(const PGeom& geo, const PgSmem& sm, con
 #pragma unroll
     for (int e = 0; e < 4; ++e) dv[e] = (d[0][e] + d[1][e]) + (d[2][e] + d[3][e]);
     const uint4 sb = *reinterpret_cast<const uint4*>(U.sbp);
-    const float2 xg = *reinterpret_cast<const float2*>(U.xg);
+    const float4 xg = *reinterpret_cast<const float4*>(U.xg);
     const float s0 = __uint_as_float(sb.x << 16), s1 = __uint_as_float(sb.x & 0xffff0000u);
     const float s2 = __uint_as_float(sb.y << 16), s3 = __uint_as_float(sb.y & 0xffff0000u);
     const float b0 = __uint_as_float(sb.z << 16), b1 = __uint_as_float(sb.z & 0xffff0000u);
     const float b2 = __uint_as_float(sb.w << 16), b3 = __uint_as_float(sb.w & 0xffff0000u);
-    float pa = fmaf(s0, dv[0], 0.f), pb = fmaf(s2, dv[2], 0.f);
-    pa = fmaf(fmaf(-C, s0, b0), xg.x, pa);
-    pa = fmaf(s1, dv[1], pa);
-    pa = fmaf(fmaf(-C, s1, b1), xg.y, pa);
-    pb = fmaf(fmaf(-C, s2, b2), xg.x, pb);
-    pb = fmaf(s3, dv[3], pb);
-    pb = fmaf(fmaf(-C, s3, b3), xg.y, pb);
+    float pa = fmaf(s0, dv[0] - xg.x, b0 * xg.z);
+    pa = fmaf(s1, dv[1] - xg.y, fmaf(b1, xg.w, pa));
+    float pb = fmaf(s2, dv[2] - xg.x, b2 * xg.z);
+    pb = fmaf(s3, dv[3] - xg.y, fmaf(b3, xg.w, pb));
     pa += __shfl_xor_sync(0xffffffffu, pa, 1);
     pb += __shfl_xor_sync(0xffffffffu, pb, 1);
     if (t == 0) {
@@ -602,11 +730,12 @@ __device__ __forceinline__ bool pg_res_early(const GemvArgs& a, int lb0, int lb1
   return early;
 }
 
-// Epilogue: each logical row of [lb0, lb1) sums its slots in order and the
-// fused output step runs (argmax: this thread's best in best_v / best_i).
+// Epilogue: each logical row of [lb0, lb1) sums its slots in order, scales
+// the sum by xscale (2^e of the x staging) and the fused output step runs
+// (argmax: this thread's best in best_v / best_i).
 __device__ __forceinline__ void pg_epilogue(const GemvArgs& a, const PGeom& geo, const float* red, int lb0, int lb1,
                                             int tid, int nthr, bool res_early, const float (&res_pre)[2],
-                                            float& best_v, int& best_i) {
+                                            float& best_v, int& best_i, float xscale) {
   const int halves = geo.halves, SKP = geo.S * 2;
   const int nlog = (lb1 - lb0) * 16;
   for (int i = tid; i < nlog; i += nthr) {
@@ -615,6 +744,7 @@ __device__ __forceinline__ void pg_epilogue(const GemvArgs& a, const PGeom& geo,
     const int prow = lbl * halves * 16 + r;
     float acc = 0.f;
     for (int j = 0; j < SKP; ++j) acc += red[prow * SKP + j];
+    acc *= xscale;  // x was staged as x * 2^-e
     switch (a.epi) {
       case kEpiStore:
         a.y[n] = f2bf(acc);
@@ -627,6 +757,7 @@ __device__ __forceinline__ void pg_epilogue(const GemvArgs& a, const PGeom& geo,
       case kEpiSwiglu: {
         float accu = 0.f;
         for (int j = 0; j < SKP; ++j) accu += red[(prow + 16) * SKP + j];
+        accu *= xscale;
         const float gv = bfround(acc), uv = bfround(accu);
         const float sg = bfround(sigmoid_f(gv));
         const float sv = bfround(__fmul_rn(gv, sg));

@@ -69,6 +69,7 @@ struct StepHdr {
   int wi[kCons];
   float scratch[32];
   float inv[8];
+  float xsc;  // 2^e of the current phase's x staging
   float2 rcs[kHD / 2];  // (cos, sin) of this step's RoPE angles
   float swt[kMaxMergeW];  // attention merge weights [q head][split]
 };
@@ -167,6 +168,7 @@ __device__ __noinline__ void merge_prologue(const StepArgs& A, StepHdr& H, const
   const int hpg = A.nq / A.nkv;
   const size_t sstride = (size_t)hpg * kPartStride;  // between the splits of one head
   const int nch = geo.K / 8;                         // 16 chunks per head
+  float mx = 0.f;
   if (ns > kMergeRegs) {
     for (int q = warp; q < A.nq; q += kCons) {
       const float* pb = A.attn_part + ((size_t)(q / hpg) * ns * hpg + (q % hpg)) * kPartStride;
@@ -240,10 +242,14 @@ __device__ __noinline__ void merge_prologue(const StepArgs& A, StepHdr& H, const
         }
       }
 #pragma unroll
-      for (int e = 0; e < 8; ++e) o[e] = bfround(o[e]);
+      for (int e = 0; e < 8; ++e) {
+        o[e] = bfround(o[e]);
+        mx = fmaxf(mx, fabsf(o[e]));
+      }
+      *reinterpret_cast<uint4*>(pg_xchunk<64>(geo, sm, 0, c)) = pack8exact(o);
     }
-    pg_emit<64>(geo, sm, 0, c, valid, valid ? pack8exact(o) : make_uint4(0u, 0u, 0u, 0u), o);
   }
+  pg_convert_staged<64, CSync>(geo, sm, 1, mx, H.scratch, &H.xsc, tid, kNT);
   pg_pad<64>(geo, sm, tid, kNT);
 }
 
@@ -264,7 +270,7 @@ __device__ __noinline__ void gemv_phase(const StepArgs& A, StepHdr& H, unsigned 
     if (merge_ns > 0)
       merge_prologue(A, H, geo, sm, merge_ns, tid);
     else
-      pg_prologue<64, CSync>(ga, geo, sm, nwsm, nwbar, nwpar, H.scratch, H.inv, &H.abort_flag, tok, tid, kNT,
+      pg_prologue<64, CSync>(ga, geo, sm, nwsm, nwbar, nwpar, H.scratch, H.inv, &H.xsc, &H.abort_flag, tok, tid, kNT,
                              lb0 == 0);
   }
   CSync::sync();
@@ -284,7 +290,7 @@ __device__ __noinline__ void gemv_phase(const StepArgs& A, StepHdr& H, unsigned 
     if (lane == 0) mbar_arrive(&H.empty[slot]);
   }
   CSync::sync();
-  pg_epilogue(ga, geo, sm.red, lb0, lb1, tid, kNT, res_early, res_pre, best_v, best_i);
+  pg_epilogue(ga, geo, sm.red, lb0, lb1, tid, kNT, res_early, res_pre, best_v, best_i, H.xsc);
 }
 
 template <int BITS>
