@@ -3,7 +3,7 @@
 // the prefill q/k/v post-processing and static-cache writes.
 //
 // Each restates one mlx-c op the reference calls through MlxCtx
-// (crates/mlx-ffi/src/ops/real/*): dequantize_weight (transform.rs:95-109),
+// (crates/mlx-ffi/src/ops/real/*): dequantize_weight (transform.rs:45-60),
 // rms_norm (blas.rs:5-9), grouped_rms_norm (grouped_norm.rs:50-135),
 // rope_dynamic (blas.rs:75-80), silu (blas.rs:33-37), multiply/add
 // (blas.rs:17-31), argmax (array.rs:6-10), softmax_axis (elementwise.rs:68-72),

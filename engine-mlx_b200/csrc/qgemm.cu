@@ -1,6 +1,6 @@
 // qgemm.cu — quantized matmul for M > 1 rows (prefill), MLX qmm semantics:
 // y = x . bf16(dequant(W))^T with fp32 accumulation
-// (mlx_quantized_matmul, crates/mlx-ffi/src/ops/real/transform.rs:127-138, as
+// (mlx_quantized_matmul, crates/mlx-ffi/src/ops/real/transform.rs:77-89, as
 // forward_qwen3.rs:66-162 calls it over the whole prompt).
 //
 // Short prompts with group size 64 (every BASELINE config): the tcgen05 GEMM

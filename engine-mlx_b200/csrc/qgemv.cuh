@@ -1,7 +1,7 @@
 // qgemv.cuh — batch-1 quantized matrix-vector product (MLX affine layout).
 //
 // Replaces mlx_quantized_matmul(x, w, scales, biases, transpose=true, gs, bits,
-// "affine") for M == 1 (crates/mlx-ffi/src/ops/real/transform.rs:127-138) as
+// "affine") for M == 1 (crates/mlx-ffi/src/ops/real/transform.rs:77-89) as
 // the served decode step calls it for qkv, o, gate_up, down and lm_head
 // (crates/serve/src/compiled.rs:133-198), and the per-expert quantized
 // matmuls of moe_forward (crates/ops/src/moe.rs:140-163) as one gathered

@@ -141,6 +141,10 @@ struct emx_qwen3 {
   bool step_coop = true;   // launch it cooperatively
   StepPlan sp{};
   StepArgs sa{};
+  uint64_t* step_words = nullptr;  // the persistent step's flag-word exchange buffers
+  unsigned* step_ctl = nullptr;    // epoch, abort word, attention tickets
+  size_t step_nwords = 0, step_nctl = 0;
+  unsigned long long step_epochs = 0;  // persistent steps since the words were cleared
 };
 
 namespace {
@@ -371,12 +375,23 @@ int shard_rule(const emx_qwen3_config& c, int world, int rank, const std::string
 // Shared memory of the persistent step's CTA (one per SM).
 constexpr int kStepBudget1 = 227 * 1024;
 
+// Zeroes the persistent step's exchange words and control block (epoch 0:
+// no stale word can carry a flag of the steps to come).
+int clear_step_words(emx_qwen3* m) {
+  if (!m->step_words) return EMX_OK;
+  EMX_CHECK_CUDA(cudaMemsetAsync(m->step_words, 0, m->step_nwords * sizeof(uint64_t), m->ctx->stream), "step words");
+  EMX_CHECK_CUDA(cudaMemsetAsync(m->step_ctl, 0, m->step_nctl * sizeof(unsigned), m->ctx->stream), "step control");
+  m->step_epochs = 0;
+  return EMX_OK;
+}
+
 // Plans the persistent decode step when the model qualifies (dense, one GPU,
-// group size 64 everywhere, head_dim 128, 1/2/4 q heads per KV head) and
-// sets up its argument block; otherwise the per-kernel chain stays in use.
+// group size 64 everywhere, head_dim 128, 1/2/4 q heads per KV head, one
+// norm group) and sets up its argument block and exchange words; it is then
+// the default decode path (sampling still runs the per-kernel chain).
 int setup_step(emx_qwen3* m) {
   const emx_qwen3_config& c = m->c;
-  if (m->moe || m->world > 1) return EMX_OK;
+  if (m->moe || m->world > 1 || c.norm_groups != 1) return EMX_OK;
   const QW& lmw = c.tied ? m->embed : m->lm;
   const LayerW& l0 = m->L[0];
   if (l0.qkv.gs != 64 || l0.o.gs != 64 || l0.gate_up.gs != 64 || l0.down.gs != 64 || lmw.gs != 64) return EMX_OK;
@@ -394,17 +409,25 @@ int setup_step(emx_qwen3* m) {
   for (int i = 0; i < 5; ++i) sh.bits[i] = bits[i];
   StepPlan p{};
   const int nsm = m->ctx->num_sms;
-  if (step_make_plan(sh, nsm, 1, kStepBudget1, &p) || step_occupancy(p) < 1) {
+  if (step_make_plan(sh, nsm, kStepBudget1, &p) || step_occupancy(p) < 1) {
     cudaGetLastError();
     return EMX_OK;
   }
   int rc;
   StepLayer* d_layers = nullptr;
-  unsigned* sync = nullptr;
   float* part = nullptr;
-  if ((rc = alloc_t(m, (size_t)c.layers, &d_layers)) || (rc = alloc_t(m, step_sync_words(nsm), &sync)) ||
+  size_t words[5];
+  step_exchange_words(sh, words);
+  size_t nw = 0;
+  for (size_t w : words) nw += w;
+  // exchange words, then epoch, abort word and the attention tickets
+  const size_t ctl = 2 + (size_t)m->nkv;
+  if ((rc = alloc_t(m, (size_t)c.layers, &d_layers)) || (rc = alloc_t(m, nw, &m->step_words)) ||
+      (rc = alloc_t(m, ctl, &m->step_ctl)) ||
       (rc = alloc_t(m, (size_t)m->nkv * p.tmpl.max_splits * p.hpg * (m->hd + 4), &part)))
     return rc;
+  m->step_nwords = nw;
+  m->step_nctl = ctl;
   std::vector<StepLayer> hl(c.layers);
   for (int l = 0; l < c.layers; ++l) {
     const LayerW& lw = m->L[l];
@@ -423,8 +446,6 @@ int setup_step(emx_qwen3* m) {
   EMX_CHECK_CUDA(cudaMemcpyAsync(d_layers, hl.data(), sizeof(StepLayer) * hl.size(), cudaMemcpyHostToDevice,
                                  m->ctx->stream),
                  "step layer table");
-  EMX_CHECK_CUDA(cudaMemsetAsync(sync, 0, step_sync_words(nsm) * sizeof(unsigned), m->ctx->stream), "step sync");
-  EMX_CHECK_CUDA(cudaStreamSynchronize(m->ctx->stream), "step setup");
   StepArgs a = p.tmpl;
   a.layers = d_layers;
   a.lm_w = lmw.pk;
@@ -436,10 +457,15 @@ int setup_step(emx_qwen3* m) {
   a.emb_gs = m->embed.gs;
   a.token = m->token;
   a.eps = c.eps;
-  a.h = m->xa;
-  a.qkvb = m->qkvb;
-  a.attnb = m->attnb;
-  a.act = m->hb;
+  uint64_t* w = m->step_words;
+  a.xw = w;
+  a.qkvw = a.xw + words[0];
+  a.attw = a.qkvw + words[1];
+  a.xmw = a.attw + words[2];
+  a.hw = a.xmw + words[3];
+  a.epoch = m->step_ctl;
+  a.abort_word = m->step_ctl + 1;
+  a.attn_tick = m->step_ctl + 2;
   a.logits = m->logits;
   a.rope_cs = m->rope_cs;
   a.attn_part = part;
@@ -450,13 +476,13 @@ int setup_step(emx_qwen3* m) {
   a.am_val = m->am_val;
   a.am_idx = m->am_idx;
   a.am_ticket = m->am_ticket;
-  a.sync = sync;
   a.status = m->ctx->status;
-  step_finish_args(&a);
   m->sp = p;
   m->sa = a;
+  if ((rc = clear_step_words(m))) return rc;
+  EMX_CHECK_CUDA(cudaStreamSynchronize(m->ctx->stream), "step setup");
   m->step_ok = true;
-  m->fused = false;  // measured slower than the programmatically chained kernels; opt in with set_fused
+  m->fused = true;
   return EMX_OK;
 }
 
@@ -895,6 +921,13 @@ int ensure_graph(emx_qwen3* m) {
 int run_steps(emx_qwen3* m, int n) {
   int rc = ensure_packed(m);
   if (rc) return rc;
+  if (m->fused && !m->sampling) {
+    // the step's flags are epoch * (layers + 1) + layer + 1 in 32 bits:
+    // clear the words before the epoch could make a flag wrap
+    const unsigned long long lim = 0xffffffffull / (unsigned long long)(m->c.layers + 1) - 2;
+    if (m->step_epochs + (unsigned long long)n >= lim && (rc = clear_step_words(m))) return rc;
+    m->step_epochs += (unsigned long long)n;
+  }
   if (!m->compiled) {  // eager: the same kernels, launched one by one
     for (int i = 0; i < n; ++i)
       if ((rc = enqueue_step(m))) return rc;
@@ -1405,6 +1438,8 @@ int emx_qwen3_reset(emx_qwen3* m) {
   Q_REQUIRE(m, "emx_qwen3_reset: null model");
   m->offset = 0;
   EMX_CHECK_CUDA(cudaMemsetAsync(m->state, 0, sizeof(int) * 64, m->ctx->stream), "reset");
+  const int rc = clear_step_words(m);  // also ends a persistent step that gave up on a wait
+  if (rc) return rc;
   return ctx_sync_check(m->ctx, "emx_qwen3_reset");
 }
 

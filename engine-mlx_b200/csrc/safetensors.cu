@@ -419,8 +419,8 @@ int st_index_files(const char* index_path, std::vector<std::string>* files) {
 
 namespace {
 
-// config.json fields (Qwen3Config, crates/serve/src/config.rs:6-30, read by
-// Qwen3Config::from_dir, config.rs:73-86, with its serde defaults).
+// config.json fields (Qwen3Config, crates/serve/src/config.rs:8-30, read by
+// Qwen3Config::from_dir, config.rs:77-90, with its serde defaults).
 struct CfgReader {
   const JVal& root;
   const char* path;

@@ -1,4 +1,4 @@
-// sample.cu — sample_token (crates/serve/src/sampler.rs:98-202) on the device.
+// sample.cu — sample_token (crates/serve/src/sampler.rs:101-202) on the device.
 //
 // One CTA of 1024 threads per draw; the logits (bf16, in L2 right after the
 // lm_head) are read a few times and the probabilities kept in a scratch

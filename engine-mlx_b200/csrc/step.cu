@@ -1,37 +1,39 @@
 // step.cu — persistent decode-step kernel for dense single-GPU models.
 //
-// Grid: cps CTAs on each of the nsm SMs (cooperative launch, all resident).
-// Each CTA has nine warps:
+// Grid: one CTA per SM (cooperative launch, all resident).  Each CTA has
+// nine warps:
 //   * warp 8, lane 0 is the producer.  It walks the step's stage sequence —
 //     for every layer: its norm vectors (a double-buffered "aux" area), the
 //     qkv GEMV tiles of this CTA, the K/V rows of this CTA's attention split,
 //     the o, gate|up and down tiles; then the final norm and the lm_head
 //     tiles — and bulk-copies each stage into a ring of `nslots` shared-memory
 //     slots (full/empty mbarriers), never waiting for a phase to begin.
-//   * warps 0-7 consume, phase by phase, and meet the other CTAs at a grid
-//     barrier between phases (the phase's outputs are the next phase's
-//     inputs).  GEMV phases use the packed-GEMV pieces of pgemv_dev.cuh
-//     unchanged, so a row's result is bit-identical to the one-matrix kernel.
-//     The attention phase is split-KV flash-decode: CTA v < n_kv * splits
-//     owns (KV head, split); q/k RMSNorm + RoPE of the new token, the KV
-//     cache write of row `pos`, online softmax over 32-row tiles, and the
-//     merge of the splits by the last CTA of each head (ticket).
-//
-// Placement: at the start every CTA takes a per-SM arrival number k with an
-// atomic and is indexed v = k * nsm + smid, so that a matrix's logical row
-// blocks are divided among SMs first and then between the CTAs of an SM —
-// no SM does two CTAs' shares while another idles.  Should an SM id or
-// arrival number fall outside the expected range, every CTA uses its
-// blockIdx instead (still a partition, only not SM-aware).
-//
-// Barriers: a monotonically increasing arrival counter; barrier b waits for
-// b * grid arrivals (release add, acquire poll).  Every wait is bounded
-// (kWaitLimitNs); a CTA that gives up raises a global abort word that the
-// others see within one poll, and all of them leave.  The CTA that merges
-// the argmax last resets the counters for the next step.
+//   * warps 0-7 consume, phase by phase.  A phase's input vector arrives in
+//     flag words (step.cuh): the consumers poll the words of the whole vector
+//     (up to four chunks' loads in flight before any is checked) until each
+//     carries the flag of this step and layer, so a phase starts as soon as
+//     the last of its inputs has landed, with no grid barrier.  GEMV phases
+//     stage x and run the packed-GEMV pieces of pgemv_dev.cuh; their rows go
+//     out as flag words.  The residual stream is kept per CTA in shared
+//     memory (`res`): the x of the qkv phase, then the x of the gate|up
+//     phase, so the o and down epilogues add their residual without another
+//     read.
+//   * The attention phase is split-KV flash-decode: CTA v < n_kv * splits
+//     owns (KV head, split): q/k RMSNorm + RoPE of the new token, the KV cache
+//     write of row `pos` (by the split that owns it), and an online softmax
+//     kept by each warp over its rows of the 32-row tiles (no barrier per
+//     tile), merged across warps once.  One split per head writes its
+//     normalised output; with
+//     more, each stores its partial and the last to finish (ticket) merges
+//     the head.
+// The last CTA through the lm_head's argmax ticket writes the token, moves
+// the position and adds one to the epoch, so the next step's flags differ.
+// Every wait is bounded (kWaitLimitNs); a CTA that gives up raises a global
+// abort word that the others see within a poll, and all of them leave.
 #include "step.cuh"
 
 #include <algorithm>
+#include <cstring>
 
 namespace emx {
 
@@ -39,71 +41,54 @@ namespace {
 
 using namespace pg;
 
-constexpr int kCons = 8;             // consumer warps
-constexpr int kNT = kCons * 32;      // consumer threads
-constexpr int kThreads = kNT + 32;   // + the producer warp
+constexpr int kCons = 8;              // consumer warps
+constexpr int kNT = kCons * 32;       // consumer threads
+constexpr int kThreads = kNT + 32;    // + the producer warp
 constexpr int kHD = 128;
-constexpr int kAT = 32;              // attention rows per tile (stage)
-constexpr int kMinRows = 64;         // fewest KV rows an attention split is given
-constexpr int kMergeRegs = 4;        // splits merged from registers (one round of loads)
-constexpr int kVOff = kAT * kHD * 2; // V rows' offset inside a slot
+constexpr int kAT = 64;               // attention rows per tile (stage)
+constexpr int kRowsPerSplit = 256;    // cache rows per attention split before another is added
+constexpr int kMaxSplitsMerge = 32;   // splits one head's merge takes (one per lane)
+constexpr int kVOff = kAT * kHD * 2;  // V rows' offset inside a slot
 constexpr int kMaxSlots = 8;
 constexpr int kPartStride = kHD + 4;  // floats per (split, head) partial: m, l, pad, pad, output[128]
-constexpr int kMaxMergeW = 1024;      // q heads x splits whose merge weights fit the header
-// ring slot: 8 int4 tiles or 4 int8 tiles (16 or 8 MMA units), or 32 K + 32 V
-// rows; half of that when two CTAs share an SM
+// ring slot: 8 int4 tiles or 4 int8 tiles (16 MMA units), or 64 K + 64 V rows
 constexpr int kSlotBytes = 36864;
 using CSync = SyncNamed<kNT>;
 
 struct StepHdr {
-  StepArgs args;  // copy of the kernel arguments (shared-memory reads in the phase functions)
   uint64_t full[kMaxSlots];
   uint64_t empty[kMaxSlots];
   uint64_t auxfull[2];
   uint64_t auxempty[2];
   int abort_flag;
-  int v;         // placement index
-  int p;         // position of the new token
+  int p;           // position of the new token
+  int tok;         // this step's token
+  unsigned ebase;  // the flag of layer l is ebase + l + 1
   unsigned flag;
+  float xsc;  // 2^e of the current phase's x staging
   float wv[kCons];
   int wi[kCons];
   float scratch[32];
-  float inv[8];
-  float xsc;  // 2^e of the current phase's x staging
   float2 rcs[kHD / 2];  // (cos, sin) of this step's RoPE angles
-  float swt[kMaxMergeW];  // attention merge weights [q head][split]
 };
 
 template <int HPG>
 struct AttnSm {
-  float qs[HPG][kHD];      // q * scale
+  float qs[HPG][kHD];      // q * scale * log2 e
   float qn[HPG + 1][kHD];  // normed q heads (+ k) before RoPE
-  float sc[HPG][kAT];      // scores -> probabilities of one tile
-  float stat_m[HPG], stat_l[HPG], stat_a[HPG];
-  float4 sacc[kCons][HPG][32];  // per-warp partial outputs, lane l = dims 4l..4l+3
+  float wm[kCons][HPG], wl[kCons][HPG];  // per-warp running max and sum
+  float4 sacc[kCons][HPG][32];           // per-warp partial outputs, lane l = dims 4l..4l+3
+  float swt[HPG][kMaxSplitsMerge];  // merge weights of a head's splits
   bf16 knew[kHD];
   bf16 vnew[kHD];
 };
 
 __host__ __device__ inline int round128(int v) { return (v + 127) & ~127; }
 
-__device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p) {
-  unsigned v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
-__device__ __forceinline__ void red_release_add(unsigned* p, unsigned v) {
-  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-// Rows [b0, b1) of W work items for placement index v: SM (v % nsm) takes
-// its contiguous share of W, CTA (v / nsm) of the SM its part of that.
-__device__ __forceinline__ void sm_range(int W, int v, int nsm, int cps, int& b0, int& b1) {
-  const int s = v % nsm, k = v / nsm;
-  const int A0 = (int)((long long)s * W / nsm), A1 = (int)((long long)(s + 1) * W / nsm);
-  b0 = A0 + (A1 - A0) * k / cps;
-  b1 = A0 + (A1 - A0) * (k + 1) / cps;
+// Logical blocks [b0, b1) of W for CTA v of G.
+__device__ __forceinline__ void cta_range(int W, int v, int G, int& b0, int& b1) {
+  b0 = (int)((long long)v * W / G);
+  b1 = (int)((long long)(v + 1) * W / G);
 }
 
 __device__ __forceinline__ void split_range(int L, int splits, int split, int& p0, int& p1) {
@@ -111,209 +96,295 @@ __device__ __forceinline__ void split_range(int L, int splits, int split, int& p
   p1 = (int)((long long)(split + 1) * L / splits);
 }
 
+// Attention splits per KV head for the new row p (rows 0..p attend).
 __device__ __forceinline__ int attn_splits(const StepArgs& A, int p) {
-  if (p < 0 || p >= A.cap) return 0;
-  const int s = (p + 1 + kMinRows - 1) / kMinRows;
+  const int s = (p + kRowsPerSplit) / kRowsPerSplit;
   return s < A.max_splits ? s : A.max_splits;
 }
 
-// Grid barrier: thread 0 of the group arrives (release) and polls (acquire)
-// until `target` arrivals; bounded, and it gives up at once when any CTA has
-// raised the abort word.  Returns false (all threads) after an abort.
-template <class Sync>
-__device__ __forceinline__ bool grid_barrier(const StepArgs& A, unsigned target, int tid, StepHdr& H) {
-  Sync::sync();
-  // a CTA that gave up on one of its own waits tells the others
-  if (tid == 0 && H.abort_flag) *reinterpret_cast<volatile unsigned*>(A.sync + 2) = 1u;
-  if (tid == 0 && !H.abort_flag) {
-    // the release add, after the group barrier, publishes every thread's
-    // writes of the phase (release cumulativity)
-    red_release_add(A.sync, 1u);
-    volatile unsigned* gabort = A.sync + 2;
-    uint64_t t0 = 0;
-    for (uint32_t i = 0;; ++i) {
-      if (ld_acquire_u32(A.sync) >= target) break;
-      if (*gabort) {
-        H.abort_flag = 1;
-        break;
-      }
-      if (i == 0) {
-        t0 = globaltimer_ns();
-      } else if ((i & 31u) == 0u && globaltimer_ns() - t0 > kWaitLimitNs) {
-        report_status(A.status, kDevTimeoutPeer);
-        *gabort = 1u;
-        H.abort_flag = 1;
-        break;
-      }
-    }
-  }
-  Sync::sync();
-  return !*reinterpret_cast<volatile int*>(&H.abort_flag);
+// ------------------------------------------------------------ flag words
+__device__ __forceinline__ void fw_store(uint64_t* p, uint32_t d, unsigned flag) {
+  const uint64_t v = ((uint64_t)flag << 32) | d;
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
-struct Cons {
-  int seq;  // stages consumed so far
-  int rot;  // first warp of the next stage's units
-};
+__device__ __forceinline__ void fw_load2(const uint64_t* p, uint64_t& a, uint64_t& b) {
+  asm volatile("ld.relaxed.gpu.global.v2.u64 {%0,%1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
 
-// The o projection's x: the attention output, merged from the splits'
-// partials (m, l, output) of every head — weights exp(m_s - M) / sum_s
-// exp(m_s - M) l_s, the splits summed in order — rounded to bf16.  Up to
-// kMergeRegs splits every thread loads its head's (m, l) and its 8 output
-// dims of all splits in one round; more splits take a second round (the
-// weights first, through shared memory).
-__device__ __noinline__ void merge_prologue(const StepArgs& A, StepHdr& H, const PGeom& geo, const PgSmem& sm,
-                                               int ns, int tid) {
-  const int warp = tid >> 5, lane = tid & 31;
-  const int hpg = A.nq / A.nkv;
-  const size_t sstride = (size_t)hpg * kPartStride;  // between the splits of one head
-  const int nch = geo.K / 8;                         // 16 chunks per head
-  float mx = 0.f;
-  if (ns > kMergeRegs) {
-    for (int q = warp; q < A.nq; q += kCons) {
-      const float* pb = A.attn_part + ((size_t)(q / hpg) * ns * hpg + (q % hpg)) * kPartStride;
-      float ms = -INFINITY, ls = 0.f, ms2 = -INFINITY, ls2 = 0.f;
-      if (lane < ns) {
-        ms = __ldcg(pb + lane * sstride);
-        ls = __ldcg(pb + lane * sstride + 1);
+__device__ __forceinline__ bool fw_ok(uint64_t a, uint64_t b, unsigned flag) {
+  return (unsigned)(a >> 32) == flag && (unsigned)(b >> 32) == flag;
+}
+
+// 2^x in one instruction (approximate, ~2 ulp; 0 for large negative x).
+__device__ __forceinline__ float ex2f(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ bool aborted(StepHdr& H) { return *reinterpret_cast<volatile int*>(&H.abort_flag) != 0; }
+
+// Polls the two words at p (16-byte aligned) until both carry `flag`.  False
+// after kWaitLimitNs (status recorded, the global abort word raised) or once
+// another CTA or warp has aborted.
+__device__ __noinline__ bool fw_wait2(const uint64_t* p, unsigned flag, uint64_t& a, uint64_t& b,
+                                      const StepArgs& A, StepHdr& H) {
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 0;; ++i) {
+    fw_load2(p, a, b);
+    if (fw_ok(a, b, flag)) return true;
+    if ((i & 31u) == 31u) {
+      if (aborted(H) || *reinterpret_cast<volatile unsigned*>(A.abort_word)) {
+        *reinterpret_cast<volatile int*>(&H.abort_flag) = 1;
+        return false;
       }
-      if (lane + 32 < ns) {
-        ms2 = __ldcg(pb + (lane + 32) * sstride);
-        ls2 = __ldcg(pb + (lane + 32) * sstride + 1);
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        report_status(A.status, kDevTimeoutPeer);
+        atomicExch(A.abort_word, 1u);
+        *reinterpret_cast<volatile int*>(&H.abort_flag) = 1;
+        return false;
       }
-      const float M = warp_max(fmaxf(ms, ms2));
-      const float w1 = ms == -INFINITY ? 0.f : expf(ms - M), w2 = ms2 == -INFINITY ? 0.f : expf(ms2 - M);
-      const float den = warp_sum(fmaf(w1, ls, w2 * ls2));
-      if (lane < ns) H.swt[q * ns + lane] = __fdiv_rn(w1, den);
-      if (lane + 32 < ns) H.swt[q * ns + lane + 32] = __fdiv_rn(w2, den);
     }
-    CSync::sync();
   }
+}
+
+// Reads the 8-element chunks [0, nch) of a bf16 vector held in flag words
+// (chunk c = words 4c..4c+3) carrying `flag` into shared memory: chunk c goes
+// to dst + (c / cpg) * gstride + (c % cpg) * 16 (the x-slot layout of a GEMV,
+// or a plain vector with cpg = nch).  Thread tid takes chunks tid, tid + kNT,
+// ...; up to four chunks are polled together: each round issues the loads of
+// every chunk not yet seen, then checks them.  On abort the thread stops (the
+// caller's next barrier and abort check end the phase).
+__device__ __noinline__ void fw_read_vec(const uint64_t* src, int nch, unsigned flag, unsigned char* dst, int cpg,
+                                         int gstride, const StepArgs& A, StepHdr& H, int tid) {
+  constexpr int kPass = 4;  // chunks whose loads are in flight together
+  for (int c0 = tid; c0 < nch; c0 += kPass * kNT) {
+    uint64_t w[kPass][4];
+    unsigned pend = 0u;  // chunks of this pass not yet seen with the flag
+#pragma unroll
+    for (int j = 0; j < kPass; ++j)
+      if (c0 + j * kNT < nch) pend |= 1u << j;
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t it = 0; pend; ++it) {
+#pragma unroll
+      for (int j = 0; j < kPass; ++j) {
+        if (pend & (1u << j)) {
+          const uint64_t* q = src + 4 * (size_t)(c0 + j * kNT);
+          fw_load2(q, w[j][0], w[j][1]);
+          fw_load2(q + 2, w[j][2], w[j][3]);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < kPass; ++j) {
+        if ((pend & (1u << j)) && fw_ok(w[j][0], w[j][1], flag) && fw_ok(w[j][2], w[j][3], flag)) {
+          pend &= ~(1u << j);
+          const int c = c0 + j * kNT;
+          *reinterpret_cast<uint4*>(dst + (size_t)(c / cpg) * gstride + (c % cpg) * 16) =
+              make_uint4((uint32_t)w[j][0], (uint32_t)w[j][1], (uint32_t)w[j][2], (uint32_t)w[j][3]);
+        }
+      }
+      if (pend && (it & 31u) == 31u) {
+        if (aborted(H) || *reinterpret_cast<volatile unsigned*>(A.abort_word)) {
+          *reinterpret_cast<volatile int*>(&H.abort_flag) = 1;
+          return;
+        }
+        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+          report_status(A.status, kDevTimeoutPeer);
+          atomicExch(A.abort_word, 1u);
+          *reinterpret_cast<volatile int*>(&H.abort_flag) = 1;
+          return;
+        }
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------- prologues
+// The token's embedding row (dequantised, bf16) into res — the layer-0 input.
+__device__ void load_res_embed(const StepArgs& A, int tok, bf16* res, int tid) {
+  const int per = 32 / A.emb_bits;
+  const int ngk = A.H / A.emb_gs;
+  const uint32_t* row = A.emb_w + (size_t)tok * (A.H / per);
+  for (int c = tid; c < A.H / 8; c += kNT) {
+    const int k0 = c * 8;
+    const bf16 sv = A.emb_s[(size_t)tok * ngk + k0 / A.emb_gs];
+    const bf16 bv = A.emb_b[(size_t)tok * ngk + k0 / A.emb_gs];
+    float v[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int k = k0 + e;
+      const uint32_t q = (row[k / per] >> (A.emb_bits * (k % per))) & ((1u << A.emb_bits) - 1u);
+      v[e] = bf2f(dequant1(q, sv, bv));
+    }
+    *reinterpret_cast<uint4*>(res + k0) = pack8exact(v);
+  }
+}
+
+// x = rms_norm(res, nw) staged for a GEMV phase (fp16, power-of-two scale to
+// H.xsc), with MLX's rounding points: bf16(bf16(x * inv) * w).
+__device__ void stage_norm(const PGeom& geo, const PgSmem& sm, const bf16* res, const bf16* nw, float eps,
+                           StepHdr& H, int tid) {
+  const int K = geo.K, nch = K / 8;
+  float ss = 0.f, mv = 0.f, mw = 0.f;
+  for (int c = tid; c < nch; c += kNT) {
+    float v[8], w[8];
+    unpack8f(*reinterpret_cast<const uint4*>(res + c * 8), v);
+    unpack8f(*reinterpret_cast<const uint4*>(nw + c * 8), w);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      ss = fmaf(v[e], v[e], ss);
+      mv = fmaxf(mv, fabsf(v[e]));
+      mw = fmaxf(mw, fabsf(w[e]));
+    }
+  }
+  const float3 r = part_reduce3<CSync>(ss, mv, mw, H.scratch, tid, kNT);
+  const float iv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(r.x, (float)K), eps)));
+  const int e = pg_scale_exp(r.y * iv * r.z * 1.02f);
+  const float sc = pg_pow2(-e);
+  if (tid == 0) H.xsc = pg_pow2(e);
+#pragma unroll 1
   for (int it = 0; it * kNT < nch; ++it) {
     const int c = it * kNT + tid;
     const bool valid = c < nch;
     float o[8];
-#pragma unroll
-    for (int e = 0; e < 8; ++e) o[e] = 0.f;
     if (valid) {
-      const int q = c / (kHD / 8), d0 = (c % (kHD / 8)) * 8;
-      const float* pb = A.attn_part + ((size_t)(q / hpg) * ns * hpg + (q % hpg)) * kPartStride;
-      auto add = [&](float w, const float4& v0, const float4& v1) {
-        o[0] = fmaf(w, v0.x, o[0]);
-        o[1] = fmaf(w, v0.y, o[1]);
-        o[2] = fmaf(w, v0.z, o[2]);
-        o[3] = fmaf(w, v0.w, o[3]);
-        o[4] = fmaf(w, v1.x, o[4]);
-        o[5] = fmaf(w, v1.y, o[5]);
-        o[6] = fmaf(w, v1.z, o[6]);
-        o[7] = fmaf(w, v1.w, o[7]);
-      };
-      if (ns <= kMergeRegs) {
-        float ms[kMergeRegs], ls[kMergeRegs];
-        float4 v0[kMergeRegs], v1[kMergeRegs];
+      float v[8], w[8];
+      unpack8f(*reinterpret_cast<const uint4*>(res + c * 8), v);
+      unpack8f(*reinterpret_cast<const uint4*>(nw + c * 8), w);
 #pragma unroll
-        for (int s2 = 0; s2 < kMergeRegs; ++s2) {
-          if (s2 < ns) {
-            const float* ps = pb + s2 * sstride;
-            ms[s2] = __ldcg(ps);
-            ls[s2] = __ldcg(ps + 1);
-            v0[s2] = __ldcg(reinterpret_cast<const float4*>(ps + 4 + d0));
-            v1[s2] = __ldcg(reinterpret_cast<const float4*>(ps + 8 + d0));
-          }
-        }
-        float M = -INFINITY;
+      for (int e2 = 0; e2 < 8; ++e2) o[e2] = bfround(__fmul_rn(bfround(__fmul_rn(v[e2], iv)), w[e2]));
+    } else {
 #pragma unroll
-        for (int s2 = 0; s2 < kMergeRegs; ++s2)
-          if (s2 < ns) M = fmaxf(M, ms[s2]);
-        float w[kMergeRegs], den = 0.f;
-#pragma unroll
-        for (int s2 = 0; s2 < kMergeRegs; ++s2) {
-          w[s2] = (s2 < ns && ms[s2] != -INFINITY) ? expf(ms[s2] - M) : 0.f;
-          if (s2 < ns) den = fmaf(w[s2], ls[s2], den);
-        }
-#pragma unroll
-        for (int s2 = 0; s2 < kMergeRegs; ++s2)
-          if (s2 < ns) add(__fdiv_rn(w[s2], den), v0[s2], v1[s2]);
-      } else {
-        for (int s2 = 0; s2 < ns; ++s2) {
-          const float* ps = pb + s2 * sstride;
-          add(H.swt[q * ns + s2], __ldcg(reinterpret_cast<const float4*>(ps + 4 + d0)),
-              __ldcg(reinterpret_cast<const float4*>(ps + 8 + d0)));
-        }
-      }
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        o[e] = bfround(o[e]);
-        mx = fmaxf(mx, fabsf(o[e]));
-      }
-      *reinterpret_cast<uint4*>(pg_xchunk<64>(geo, sm, 0, c)) = pack8exact(o);
+      for (int e2 = 0; e2 < 8; ++e2) o[e2] = 0.f;
     }
+    pg_emit<64>(geo, sm, 0, c, valid, o, sc);
+  }
+  pg_pad<64>(geo, sm, tid, kNT);
+}
+
+// x read from flag words as given (attention output, SwiGLU output) and
+// staged for a GEMV phase.
+__device__ void stage_raw_fw(const PGeom& geo, const PgSmem& sm, const uint64_t* src, unsigned flag,
+                             const StepArgs& A, StepHdr& H, int tid) {
+  const int nch = geo.K / 8;
+  fw_read_vec(src, nch, flag, sm.xsm, 8, geo.gstride, A, H, tid);
+  float mx = 0.f;  // max |x| over the chunks this thread staged
+  for (int c = tid; c < nch; c += kNT) {
+    float v[8];
+    unpack8f(*reinterpret_cast<const uint4*>(pg_xchunk<64>(geo, sm, 0, c)), v);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) mx = fmaxf(mx, fabsf(v[e]));
   }
   pg_convert_staged<64, CSync>(geo, sm, 1, mx, H.scratch, &H.xsc, tid, kNT);
   pg_pad<64>(geo, sm, tid, kNT);
 }
 
-// One GEMV phase on rows [lb0, lb1) of this CTA (consumer threads only).
-// merge_ns > 0: x is the attention merge of merge_ns splits.
+// The residual vector from flag words into res.
+__device__ void load_res_fw(const uint64_t* src, int H_, unsigned flag, bf16* res, const StepArgs& A, StepHdr& H,
+                            int tid) {
+  fw_read_vec(src, H_ / 8, flag, reinterpret_cast<unsigned char*>(res), H_ / 8, 0, A, H, tid);
+}
+
+// ------------------------------------------------------------- GEMV phases
+// The stages of logical blocks [lb0, lb1) from the ring (consumer threads);
+// ends with a consumer barrier.
 template <int BITS>
-__device__ __noinline__ void gemv_phase(const StepArgs& A, StepHdr& H, unsigned char* smem, const PGeom& geo,
-                                        const GemvArgs& ga, int lb0, int lb1, const bf16* nwsm, uint64_t* nwbar,
-                                        uint32_t nwpar, int tok, Cons& cs, int tid, float& best_v, int& best_i,
-                                        int release_aux, int merge_ns) {
+__device__ __noinline__ void gemv_run(const StepArgs& A, StepHdr& H, unsigned char* smem, const PGeom& geo,
+                                      int lb0, int lb1, int& seq, int& rot, int tid) {
   const int warp = tid >> 5, lane = tid & 31;
   const PgSmem sm = pg_smem(smem, geo);
-  const bool active = lb1 > lb0;
-  float res_pre[2] = {0.f, 0.f};
-  bool res_early = false;
-  if (active) {
-    res_early = pg_res_early(ga, lb0, lb1, tid, kNT, res_pre);
-    if (merge_ns > 0)
-      merge_prologue(A, H, geo, sm, merge_ns, tid);
-    else
-      pg_prologue<64, CSync>(ga, geo, sm, nwsm, nwbar, nwpar, H.scratch, H.inv, &H.xsc, &H.abort_flag, tok, tid, kNT,
-                             lb0 == 0);
-  }
-  CSync::sync();
-  if (release_aux >= 0 && tid == 0) mbar_arrive(&H.auxempty[release_aux]);
-  if (!active) return;
   const int lbt = geo.halves * geo.S;
   const int T1 = lb1 * lbt;
   unsigned char* ring = smem + A.off_ring;
   for (int a0 = lb0 * lbt; a0 < T1; a0 += geo.stage_tiles) {
     const int a1 = min(T1, a0 + geo.stage_tiles);
-    const int s = cs.seq++;
+    const int s = seq++;
     const int slot = s % A.nslots;
     if (wait_or_abort(&H.full[slot], (uint32_t)((s / A.nslots) & 1), &H.abort_flag, A.status))
-      pg_stage<BITS, 64>(geo, sm, ring + (size_t)slot * A.slot_bytes, a0, a1, lb0, warp, lane, kCons, cs.rot);
-    cs.rot = (cs.rot + (a1 - a0) * 2) % kCons;
+      pg_stage<BITS, 64>(geo, sm, ring + (size_t)slot * A.slot_bytes, a0, a1, lb0, warp, lane, kCons, rot);
+    rot = (rot + (a1 - a0) * 2) % kCons;
     __syncwarp();
     if (lane == 0) mbar_arrive(&H.empty[slot]);
   }
   CSync::sync();
-  pg_epilogue(ga, geo, sm.red, lb0, lb1, tid, kNT, res_early, res_pre, best_v, best_i, H.xsc);
 }
 
-template <int BITS>
-__device__ __forceinline__ void gemv_phase_any(int bits, const StepArgs& A, StepHdr& H, unsigned char* smem,
-                                               const PGeom& geo, const GemvArgs& ga, int lb0, int lb1,
-                                               const bf16* nwsm, uint64_t* nwbar, uint32_t nwpar, int tok, Cons& cs,
-                                               int tid, float& best_v, int& best_i, int release_aux, int merge_ns,
-                                               int v) {
-  (void)v;
+__device__ __forceinline__ void gemv_any(int bits, const StepArgs& A, StepHdr& H, unsigned char* smem,
+                                         const PGeom& geo, int lb0, int lb1, int& seq, int& rot, int tid) {
   if (bits == 8)
-    gemv_phase<8>(A, H, smem, geo, ga, lb0, lb1, nwsm, nwbar, nwpar, tok, cs, tid, best_v, best_i, release_aux,
-                  merge_ns);
+    gemv_run<8>(A, H, smem, geo, lb0, lb1, seq, rot, tid);
   else
-    gemv_phase<4>(A, H, smem, geo, ga, lb0, lb1, nwsm, nwbar, nwpar, tok, cs, tid, best_v, best_i, release_aux,
-                  merge_ns);
+    gemv_run<4>(A, H, smem, geo, lb0, lb1, seq, rot, tid);
 }
 
+enum OutKind : int { kOutStore = 0, kOutResid = 1, kOutSwiglu = 2 };
+
+// A row's value: xscale * the sum of its SKP slots in order (SKP even; vector
+// loads, so the slots arrive together).
+__device__ __forceinline__ float row_value(const float* red, int prow, int SKP, float xscale) {
+  const float* r = red + (size_t)prow * SKP;
+  float acc = 0.f;
+  if ((SKP & 3) == 0) {
+#pragma unroll 6
+    for (int j = 0; j < SKP; j += 4) {
+      const float4 q = *reinterpret_cast<const float4*>(r + j);
+      acc += q.x;
+      acc += q.y;
+      acc += q.z;
+      acc += q.w;
+    }
+  } else {
+#pragma unroll 4
+    for (int j = 0; j < SKP; j += 2) {
+      const float2 q = *reinterpret_cast<const float2*>(r + j);
+      acc += q.x;
+      acc += q.y;
+    }
+  }
+  return acc * xscale;
+}
+
+// The phase's rows [lb0*16, lb1*16) out as flag words, one row per thread
+// (lane pairs join their rows into a word): bf16(acc) (store),
+// bf16(res + bf16(acc)) (residual), or MLX's SwiGLU steps.
+template <int OUT>
+__device__ void epilogue_fw(const PGeom& geo, const PgSmem& sm, int lb0, int lb1, const bf16* res, uint64_t* dst,
+                            unsigned flag, float xscale, int tid) {
+  const int halves = geo.halves, SKP = geo.S * 2;
+  const int nrow = (lb1 - lb0) * 16;
+  for (int i0 = 0; i0 < nrow; i0 += kNT) {
+    const int li = i0 + tid;
+    float y = 0.f;
+    if (li < nrow) {
+      const int lbl = li >> 4, r = li & 15;
+      const int prow = lbl * halves * 16 + r;
+      const float acc = row_value(sm.red, prow, SKP, xscale);
+      if (OUT == kOutStore) {
+        y = bfround(acc);
+      } else if (OUT == kOutResid) {
+        y = bfround(__fadd_rn(bf2f(res[lb0 * 16 + li]), bfround(acc)));
+      } else {
+        const float accu = row_value(sm.red, prow + 16, SKP, xscale);
+        const float gv = bfround(acc), uv = bfround(accu);
+        const float sg = bfround(sigmoid_f(gv));
+        const float sv = bfround(__fmul_rn(gv, sg));
+        y = bfround(__fmul_rn(sv, uv));
+      }
+    }
+    const uint32_t bits = f2bits(y);
+    const uint32_t hi = __shfl_down_sync(0xffffffffu, bits, 1);
+    if (li < nrow && (li & 1) == 0) fw_store(dst + (size_t)(lb0 * 16 + li) / 2, bits | (hi << 16), flag);
+  }
+}
+
+// ----------------------------------------------------------- attention
 // The attention phase of one layer for this CTA's (KV head, split), if any.
 // `aux` holds the layer's q_norm at [2H] and k_norm at [2H + 128] (bf16).
 template <int HPG>
 __device__ __noinline__ void attn_phase(const StepArgs& A, StepHdr& H, unsigned char* smem, const StepLayer& LW,
                                         const bf16* aux, uint64_t* auxbar, uint32_t auxpar, int item, int ns, int p,
-                                        Cons& cs, int tid) {
+                                        unsigned flag, int& seq, int tid) {
   if (item < 0) return;
   AttnSm<HPG>& S = *reinterpret_cast<AttnSm<HPG>*>(smem + A.off_u);
   const int warp = tid >> 5, lane = tid & 31;
@@ -329,18 +400,22 @@ __device__ __noinline__ void attn_phase(const StepArgs& A, StepHdr& H, unsigned 
   if (LW.q_norm || LW.k_norm) wait_or_abort(auxbar, auxpar, &H.abort_flag, A.status);
 
   // ---- q heads (and k/v of the new row when owned): rms_norm + rope -------
+  // (rows of the qkv projection, read from its flag words: lane l takes
+  // elements 4l..4l+3 = words 2l, 2l+1)
   const int nprep = HPG + (owns_new ? 1 : 0);
   for (int hh = warp; hh < nprep; hh += kCons) {
     const bool is_k = hh == HPG;
-    const bf16* src = is_k ? A.qkvb + (size_t)A.nq * kHD + (size_t)kvh * kHD : A.qkvb + (size_t)(kvh * HPG + hh) * kHD;
+    const int e0 = is_k ? (A.nq + kvh) * kHD : (kvh * HPG + hh) * kHD;
     const bf16* nw = is_k ? nwk : nwq;
     const bool has_norm = is_k ? LW.k_norm != nullptr : LW.q_norm != nullptr;
+    uint64_t w0 = 0, w1 = 0;
+    fw_load2(A.qkvw + e0 / 2 + lane * 2, w0, w1);
+    if (!fw_ok(w0, w1, flag)) fw_wait2(A.qkvw + e0 / 2 + lane * 2, flag, w0, w1, A, H);
     float v[4];
-    const uint2 raw = *reinterpret_cast<const uint2*>(src + lane * 4);
-    v[0] = __uint_as_float(raw.x << 16);
-    v[1] = __uint_as_float(raw.x & 0xffff0000u);
-    v[2] = __uint_as_float(raw.y << 16);
-    v[3] = __uint_as_float(raw.y & 0xffff0000u);
+    v[0] = __uint_as_float((uint32_t)w0 << 16);
+    v[1] = __uint_as_float((uint32_t)w0 & 0xffff0000u);
+    v[2] = __uint_as_float((uint32_t)w1 << 16);
+    v[3] = __uint_as_float((uint32_t)w1 & 0xffff0000u);
     float ss = 0.f;
 #pragma unroll
     for (int e = 0; e < 4; ++e) ss = fmaf(v[e], v[e], ss);
@@ -367,165 +442,233 @@ __device__ __noinline__ void attn_phase(const StepArgs& A, StepHdr& H, unsigned 
         kc[(size_t)p * kHD + d] = f2bf(o);
         S.knew[d] = f2bf(o);
       } else {
-        S.qs[hh][d] = __fmul_rn(o, A.scale);
+        S.qs[hh][d] = __fmul_rn(o, A.scale_log2e);
       }
     }
     if (is_k) {
-      const bf16* vsrc = A.qkvb + (size_t)(A.nq + A.nkv) * kHD + (size_t)kvh * kHD;
-      const uint2 vr = *reinterpret_cast<const uint2*>(vsrc + lane * 4);
+      const int ev = (A.nq + A.nkv + kvh) * kHD;
+      uint64_t u0 = 0, u1 = 0;
+      fw_load2(A.qkvw + ev / 2 + lane * 2, u0, u1);
+      if (!fw_ok(u0, u1, flag)) fw_wait2(A.qkvw + ev / 2 + lane * 2, flag, u0, u1, A, H);
+      const uint2 vr = make_uint2((uint32_t)u0, (uint32_t)u1);
       *reinterpret_cast<uint2*>(vc + (size_t)p * kHD + lane * 4) = vr;
       *reinterpret_cast<uint2*>(S.vnew + lane * 4) = vr;
     }
   }
-  if (tid < HPG) {
-    S.stat_m[tid] = -INFINITY;
-    S.stat_l[tid] = 0.f;
-  }
   CSync::sync();
 
-  float qreg[HPG][4], acc[HPG][4];
+  float qreg[HPG][4], acc[HPG][4], wm[HPG], wl[HPG];
 #pragma unroll
-  for (int h = 0; h < HPG; ++h)
+  for (int h = 0; h < HPG; ++h) {
+    wm[h] = -INFINITY;
+    wl[h] = 0.f;
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       qreg[h][e] = S.qs[h][lane * 4 + e];
       acc[h][e] = 0.f;
     }
+  }
 
+  // Each warp keeps its own online softmax over the rows it takes (rows
+  // [8w, 8w + 8) of every tile), so the tiles need no CTA barrier; the warps
+  // merge once at the end.  Scores are in the base-2 domain (q carries
+  // scale * log2 e), so every exponential is one ex2.
   unsigned char* ring = smem + A.off_ring;
-  const int r0 = warp * 4;  // this warp's rows of a tile
+  const int r0 = warp * 8;  // this warp's rows of a tile
   for (int t = 0; t < ntile; ++t) {
     const int t0 = p0 + t * kAT;
     const int tn = min(kAT, p1 - t0);
-    const int s = cs.seq++;
+    const int s = seq++;
     const int slot = s % A.nslots;
-    bf16* kt = reinterpret_cast<bf16*>(ring + (size_t)slot * A.slot_bytes);
-    bf16* vt = reinterpret_cast<bf16*>(ring + (size_t)slot * A.slot_bytes + kVOff);
+    const bf16* kt = reinterpret_cast<const bf16*>(ring + (size_t)slot * A.slot_bytes);
+    const bf16* vt = reinterpret_cast<const bf16*>(ring + (size_t)slot * A.slot_bytes + kVOff);
     const bool ok = wait_or_abort(&H.full[slot], (uint32_t)((s / A.nslots) & 1), &H.abort_flag, A.status);
-    // the new row is never copied: the owner puts it in place
-    if (owns_new && p >= t0 && p < t0 + tn) {
-      const int r = p - t0;
-      if (tid < kHD / 8) {
-        reinterpret_cast<uint4*>(kt + (size_t)r * kHD)[tid] = reinterpret_cast<const uint4*>(S.knew)[tid];
-        reinterpret_cast<uint4*>(vt + (size_t)r * kHD)[tid] = reinterpret_cast<const uint4*>(S.vnew)[tid];
-      }
-      CSync::sync();
-    }
-    // QK^T: warp w scores rows [4w, 4w + 4).  Each lane forms its 4-dim
-    // partial of the four rows, then a transpose-reduction (xor 16, 8: halve
-    // the rows a lane keeps; xor 4, 2, 1: plain sums) leaves row
-    // 2*bit4(lane) + bit3(lane) in the lanes of that row's octet.
     if (ok && r0 < tn) {
-      float kf[4][4];
-#pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        const uint2 kv = r0 + r < tn ? *reinterpret_cast<const uint2*>(kt + (size_t)(r0 + r) * kHD + lane * 4)
-                                     : make_uint2(0u, 0u);
-        kf[r][0] = __uint_as_float(kv.x << 16);
-        kf[r][1] = __uint_as_float(kv.x & 0xffff0000u);
-        kf[r][2] = __uint_as_float(kv.y << 16);
-        kf[r][3] = __uint_as_float(kv.y & 0xffff0000u);
-      }
-#pragma unroll
-      for (int h = 0; h < HPG; ++h) {
-        float v[4];
+#pragma unroll 1
+      for (int g2 = 0; g2 < 2; ++g2) {
+        const int rb = r0 + 4 * g2;                  // first row of this group of four
+        const int nr = min(4, tn - rb);             // rows of the group in the tile
+        if (nr <= 0) break;
+        // the new row is never copied into the ring: it is read from S.knew / S.vnew
+        float kf[4][4], vf[4][4];
 #pragma unroll
         for (int r = 0; r < 4; ++r) {
-          float s2 = 0.f;
-#pragma unroll
-          for (int e = 0; e < 4; ++e) s2 = fmaf(qreg[h][e], kf[r][e], s2);
-          v[r] = s2;
+          const int rr = rb + r;
+          const bool isnew = owns_new && t0 + rr == p;
+          const bf16* kr = isnew ? S.knew : kt + (size_t)rr * kHD;
+          const bf16* vr = isnew ? S.vnew : vt + (size_t)rr * kHD;
+          const uint2 kv = r < nr ? *reinterpret_cast<const uint2*>(kr + lane * 4) : make_uint2(0u, 0u);
+          const uint2 vv = r < nr ? *reinterpret_cast<const uint2*>(vr + lane * 4) : make_uint2(0u, 0u);
+          kf[r][0] = __uint_as_float(kv.x << 16);
+          kf[r][1] = __uint_as_float(kv.x & 0xffff0000u);
+          kf[r][2] = __uint_as_float(kv.y << 16);
+          kf[r][3] = __uint_as_float(kv.y & 0xffff0000u);
+          vf[r][0] = __uint_as_float(vv.x << 16);
+          vf[r][1] = __uint_as_float(vv.x & 0xffff0000u);
+          vf[r][2] = __uint_as_float(vv.y << 16);
+          vf[r][3] = __uint_as_float(vv.y & 0xffff0000u);
         }
-        const bool up16 = (lane & 16) != 0;
 #pragma unroll
-        for (int r = 0; r < 2; ++r) {
-          const float send = up16 ? v[r] : v[r + 2];
-          const float keep = up16 ? v[r + 2] : v[r];
-          v[r] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+        for (int h = 0; h < HPG; ++h) {
+          // QK^T: each lane's 4-dim partials of the four rows, then a
+          // transpose-reduction (xor 16, 8: halve the rows a lane keeps; xor
+          // 4, 2, 1: plain sums) leaves row k in lane 8k (and its octet)
+          float v[4];
+#pragma unroll
+          for (int r = 0; r < 4; ++r) {
+            float s2 = 0.f;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) s2 = fmaf(qreg[h][e], kf[r][e], s2);
+            v[r] = s2;
+          }
+          const bool up16 = (lane & 16) != 0;
+#pragma unroll
+          for (int r = 0; r < 2; ++r) {
+            const float send = up16 ? v[r] : v[r + 2];
+            const float keep = up16 ? v[r + 2] : v[r];
+            v[r] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+          }
+          const bool up8 = (lane & 8) != 0;
+          {
+            const float send = up8 ? v[0] : v[1];
+            const float keep = up8 ? v[1] : v[0];
+            v[0] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+          }
+          v[0] += __shfl_xor_sync(0xffffffffu, v[0], 4);
+          v[0] += __shfl_xor_sync(0xffffffffu, v[0], 2);
+          v[0] += __shfl_xor_sync(0xffffffffu, v[0], 1);
+          float sk[4];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) sk[k] = __shfl_sync(0xffffffffu, v[0], k * 8);
+          // online softmax over the warp's rows so far
+          float mt = sk[0];
+#pragma unroll
+          for (int k = 1; k < 4; ++k)
+            if (k < nr) mt = fmaxf(mt, sk[k]);
+          const float mn = fmaxf(wm[h], mt);
+          const float alpha = wm[h] == -INFINITY ? 0.f : ex2f(wm[h] - mn);
+          float pk[4], ls = 0.f;
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            pk[k] = k < nr ? ex2f(sk[k] - mn) : 0.f;
+            ls += pk[k];
+          }
+          wl[h] = fmaf(wl[h], alpha, ls);
+          wm[h] = mn;
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            float a2 = acc[h][e] * alpha;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) a2 = fmaf(pk[k], vf[k][e], a2);
+            acc[h][e] = a2;
+          }
         }
-        const bool up8 = (lane & 8) != 0;
-        {
-          const float send = up8 ? v[0] : v[1];
-          const float keep = up8 ? v[1] : v[0];
-          v[0] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
-        }
-        v[0] += __shfl_xor_sync(0xffffffffu, v[0], 4);
-        v[0] += __shfl_xor_sync(0xffffffffu, v[0], 2);
-        v[0] += __shfl_xor_sync(0xffffffffu, v[0], 1);
-        const int k = ((lane >> 4) & 1) * 2 + ((lane >> 3) & 1);
-        if ((lane & 7) == 0 && r0 + k < tn) S.sc[h][r0 + k] = v[0];
-      }
-    }
-    CSync::sync();
-    // online softmax update at tile granularity (one warp per head)
-    for (int h = warp; h < HPG; h += kCons) {
-      const float sv = lane < tn ? S.sc[h][lane] : -INFINITY;
-      const float m = warp_max(sv);
-      const float mo = S.stat_m[h];
-      const float mn = fmaxf(mo, m);
-      const float e = lane < tn ? expf(sv - mn) : 0.f;
-      if (lane < tn) S.sc[h][lane] = e;
-      const float l = warp_sum(e);
-      if (lane == 0) {
-        const float alpha = (mo == -INFINITY) ? 0.f : expf(mo - mn);
-        S.stat_a[h] = alpha;
-        S.stat_l[h] = S.stat_l[h] * alpha + l;
-        S.stat_m[h] = mn;
-      }
-    }
-    CSync::sync();
-    // P.V: warp w accumulates rows [4w, 4w + 4) into its 4 dims per lane
-#pragma unroll
-    for (int h = 0; h < HPG; ++h) {
-      const float al = S.stat_a[h];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) acc[h][e] *= al;
-    }
-    const int rend = min(tn, r0 + 4);
-    for (int jj = r0; jj < rend; ++jj) {
-      const uint2 vv = *reinterpret_cast<const uint2*>(vt + (size_t)jj * kHD + lane * 4);
-      const float vf[4] = {__uint_as_float(vv.x << 16), __uint_as_float(vv.x & 0xffff0000u),
-                           __uint_as_float(vv.y << 16), __uint_as_float(vv.y & 0xffff0000u)};
-#pragma unroll
-      for (int h = 0; h < HPG; ++h) {
-        const float pr = S.sc[h][jj];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) acc[h][e] = fmaf(pr, vf[e], acc[h][e]);
       }
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&H.empty[slot]);
-    CSync::sync();  // sc is rewritten by the next tile
   }
 
-  // ---- the warps' partial outputs, then this split's result --------------
+  // ---- merge the warps: M = max_w m_w, L = sum_w 2^(m_w - M) l_w,
+  // num = sum_w 2^(m_w - M) acc_w (warps in order) -------------------------
 #pragma unroll
-  for (int h = 0; h < HPG; ++h) S.sacc[warp][h][lane] = make_float4(acc[h][0], acc[h][1], acc[h][2], acc[h][3]);
-  CSync::sync();
-  // this split's partial: (m, l) and the unnormalised output of each head,
-  // merged by the next phase's prologue
-  float* part = A.attn_part + ((size_t)kvh * ns + split) * HPG * kPartStride;
-  for (int i = tid; i < HPG * kHD; i += kNT) {
-    const int h = i / kHD, d = i % kHD;
-    float num = 0.f;
-#pragma unroll
-    for (int w = 0; w < kCons; ++w) num += reinterpret_cast<const float*>(&S.sacc[w][h][0])[d];
-    part[h * kPartStride + 4 + d] = num;
+  for (int h = 0; h < HPG; ++h) {
+    S.sacc[warp][h][lane] = make_float4(acc[h][0], acc[h][1], acc[h][2], acc[h][3]);
+    if (lane == 0) {
+      S.wm[warp][h] = wm[h];
+      S.wl[warp][h] = wl[h];
+    }
   }
-  if (tid < HPG) {
-    part[tid * kPartStride + 0] = S.stat_m[tid];
-    part[tid * kPartStride + 1] = S.stat_l[tid];
+  CSync::sync();
+  // (M, L) of head h and num of dims d, d + 1
+  auto merged = [&](int h, int d, float& M, float& Lh, float& n0, float& n1) {
+    M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kCons; ++w) M = fmaxf(M, S.wm[w][h]);
+    Lh = 0.f;
+    n0 = 0.f;
+    n1 = 0.f;
+#pragma unroll
+    for (int w = 0; w < kCons; ++w) {
+      const float mw = S.wm[w][h];
+      const float ew = mw == -INFINITY ? 0.f : ex2f(mw - M);
+      Lh = fmaf(ew, S.wl[w][h], Lh);
+      const float* aw = reinterpret_cast<const float*>(&S.sacc[w][h][0]);
+      n0 = fmaf(ew, aw[d], n0);
+      n1 = fmaf(ew, aw[d + 1], n1);
+    }
+  };
+  uint64_t* out = A.attw + (size_t)kvh * HPG * kHD / 2;  // this KV head's q heads, two dims per word
+  if (ns == 1) {
+    // the normalised output, with the merge's arithmetic for one split:
+    // bf16(fma(1 / L, num, 0))
+    for (int i = tid; i < HPG * kHD / 2; i += kNT) {
+      const int h = (2 * i) / kHD, d = (2 * i) % kHD;
+      float M, Lh, n0, n1;
+      merged(h, d, M, Lh, n0, n1);
+      const float sw = __fdiv_rn(1.0f, Lh);
+      const float o0 = bfround(fmaf(sw, n0, 0.f));
+      const float o1 = bfround(fmaf(sw, n1, 0.f));
+      fw_store(out + i, (uint32_t)f2bits(o0) | ((uint32_t)f2bits(o1) << 16), flag);
+    }
+    return;
+  }
+  // several splits: this split's partial (m, l, unnormalised output); the
+  // last split of the head to finish merges them all
+  float* part = A.attn_part + ((size_t)kvh * A.max_splits + split) * HPG * kPartStride;
+  for (int i = tid; i < HPG * kHD / 2; i += kNT) {
+    const int h = (2 * i) / kHD, d = (2 * i) % kHD;
+    float M, Lh, n0, n1;
+    merged(h, d, M, Lh, n0, n1);
+    *reinterpret_cast<float2*>(part + h * kPartStride + 4 + d) = make_float2(n0, n1);
+    if (d == 0) {
+      part[h * kPartStride + 0] = M;
+      part[h * kPartStride + 1] = Lh;
+    }
+  }
+  __threadfence();
+  CSync::sync();
+  if (tid == 0) H.flag = (atomicAdd(&A.attn_tick[kvh], 1u) == (unsigned)ns - 1) ? 1u : 0u;
+  CSync::sync();
+  if (!H.flag) return;
+  __threadfence();
+  const float* hb = A.attn_part + (size_t)kvh * A.max_splits * HPG * kPartStride;
+  // weights 2^(m_s - M) / sum_s 2^(m_s - M) l_s, one warp per q head
+  for (int h = warp; h < HPG; h += kCons) {
+    const float* pm = hb + (size_t)lane * HPG * kPartStride + h * kPartStride;
+    const float ms = lane < ns ? __ldcg(pm) : -INFINITY;
+    const float ls = lane < ns ? __ldcg(pm + 1) : 0.f;
+    const float M = warp_max(ms);
+    const float w = ms == -INFINITY ? 0.f : ex2f(ms - M);
+    const float den = warp_sum(fmaf(w, ls, 0.f));
+    if (lane < ns) S.swt[h][lane] = __fdiv_rn(w, den);
+  }
+  if (tid == 0) A.attn_tick[kvh] = 0u;
+  __threadfence();
+  CSync::sync();
+  for (int i = tid; i < HPG * kHD / 2; i += kNT) {
+    const int h = (2 * i) / kHD, d = (2 * i) % kHD;
+    float o0 = 0.f, o1 = 0.f;
+#pragma unroll 4
+    for (int s2 = 0; s2 < ns; ++s2) {
+      const float2 v = __ldcg(reinterpret_cast<const float2*>(hb + ((size_t)s2 * HPG + h) * kPartStride + 4 + d));
+      const float sw = S.swt[h][s2];
+      o0 = fmaf(sw, v.x, o0);
+      o1 = fmaf(sw, v.y, o1);
+    }
+    fw_store(out + i, (uint32_t)f2bits(bfround(o0)) | ((uint32_t)f2bits(bfround(o1)) << 16), flag);
   }
 }
 
-// The producer thread: every stage of the step for this CTA, in the order the
-// consumers take them.
-__device__ __noinline__ void producer(const StepArgs& A, StepHdr& H, unsigned char* smem, int v, int p) {
+// ------------------------------------------------------------ producer
+// Every stage of the step for this CTA, in the order the consumers take them.
+__device__ __noinline__ void producer(const StepArgs& A, StepHdr& H, unsigned char* smem, int v, int G, int p,
+                                      int ns) {
   const int NS = A.nslots, SB = A.slot_bytes;
   unsigned char* ring = smem + A.off_ring;
   const uint64_t pol = l2_evict_first_policy();
-  int s = 0;      // stages issued
-  int naux = 0;   // aux loads issued
+  int s = 0;     // stages issued
+  int naux = 0;  // aux loads issued
   auto acquire = [&]() -> int {
     const int slot = s % NS;
     if (s >= NS && !wait_or_abort(&H.empty[slot], (uint32_t)(((s / NS) - 1) & 1), &H.abort_flag, A.status))
@@ -536,7 +679,7 @@ __device__ __noinline__ void producer(const StepArgs& A, StepHdr& H, unsigned ch
   auto gemv = [&](int mat, const unsigned char* w) -> bool {
     const PGeom& geo = A.geo[mat];
     int b0, b1;
-    sm_range(geo.lb_total, v, A.nsm, A.cps, b0, b1);
+    cta_range(geo.lb_total, v, G, b0, b1);
     const int lbt = geo.halves * geo.S;
     for (int a0 = b0 * lbt; a0 < b1 * lbt; a0 += geo.stage_tiles) {
       const int a1 = min(b1 * lbt, a0 + geo.stage_tiles);
@@ -570,7 +713,6 @@ __device__ __noinline__ void producer(const StepArgs& A, StepHdr& H, unsigned ch
     ++naux;
     return true;
   };
-  const int ns = attn_splits(A, p);
   const int item = v < A.nkv * ns ? v : -1;
   auto attn = [&](const StepLayer& LW) -> bool {
     if (item < 0) return true;
@@ -615,26 +757,28 @@ __device__ __noinline__ void producer(const StepArgs& A, StepHdr& H, unsigned ch
   }
   if (ok) ok = aux(A.n_layers) && gemv(kMatLm, A.lm_w);
   // never leave with copies in flight into this CTA's shared memory
-  if (!ok || H.abort_flag) {
+  if (!ok || aborted(H)) {
     for (int t = max(0, s - NS); t < s; ++t) mbar_wait_bounded(&H.full[t % NS], (uint32_t)((t / NS) & 1), A.status);
-    for (int l = max(0, naux - 2); l < naux; ++l) mbar_wait_bounded(&H.auxfull[l & 1], (uint32_t)((l >> 1) & 1), A.status);
+    for (int l = max(0, naux - 2); l < naux; ++l)
+      mbar_wait_bounded(&H.auxfull[l & 1], (uint32_t)((l >> 1) & 1), A.status);
   }
 }
 
+__device__ __forceinline__ void argmax_pair(float& bv, int& bi, float ov, int oi) {
+  if (ov > bv || (ov == bv && oi < bi)) {
+    bv = ov;
+    bi = oi;
+  }
+}
+
+// ---------------------------------------------------------------- kernel
 template <int HPG>
-__global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant__ StepArgs P) {
+__global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant__ StepArgs A) {
   extern __shared__ __align__(128) unsigned char smem[];
   StepHdr& H = *reinterpret_cast<StepHdr*>(smem);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const unsigned G = gridDim.x;
-  {
-    static_assert(sizeof(StepArgs) % 4 == 0, "argument block copied by words");
-    const int* src = reinterpret_cast<const int*>(&P);
-    int* dst = reinterpret_cast<int*>(&H.args);
-    for (int i = tid; i < (int)(sizeof(StepArgs) / 4); i += kThreads) dst[i] = src[i];
-  }
-  __syncthreads();
-  const StepArgs& A = H.args;
+  const int G = (int)gridDim.x, v = (int)blockIdx.x;
+  const int L = A.n_layers;
 
   if (tid == 0) {
     for (int i = 0; i < A.nslots; ++i) {
@@ -645,83 +789,185 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
       mbar_init(&H.auxfull[b], 1);
       mbar_init(&H.auxempty[b], 1);
     }
-    H.abort_flag = 0;
+    H.abort_flag = *reinterpret_cast<volatile unsigned*>(A.abort_word) ? 1 : 0;
     fence_mbar_init();
-    unsigned smid;
-    asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
-    unsigned k = 0xffffffffu;
-    if (smid < (unsigned)A.nsm) k = atomicAdd(&A.sync[4 + smid], 1u);
-    if (smid >= (unsigned)A.nsm || k >= (unsigned)A.cps) atomicOr(&A.sync[1], 1u);
-    H.v = (int)(k * (unsigned)A.nsm + smid);
-  }
-  // barrier 1: every CTA has its placement number
-  const bool ok0 = grid_barrier<SyncCta>(A, G, tid, H);
-  if (tid == 0) {
-    if (ld_acquire_u32(A.sync + 1)) H.v = blockIdx.x;
     H.p = *reinterpret_cast<volatile int*>(A.pos);
+    H.ebase = *reinterpret_cast<volatile unsigned*>(A.epoch) * (unsigned)(L + 1);
+    int tok = *A.token;
+    if (tok < 0 || tok >= A.vocab) {
+      if (v == 0) report_status(A.status, kDevBadToken);
+      tok = 0;
+    }
+    H.tok = tok;
   }
   __syncthreads();
-  const int v = H.v, p = H.p;
-  const bool pos_ok = p >= 0 && p < A.cap;
-  if (tid < kHD / 2 && pos_ok) H.rcs[tid] = A.rope_cs[(size_t)p * (kHD / 2) + tid];
+  const int p = H.p;
+  if (p < 0 || p >= A.cap) {
+    if (tid == 0 && v == 0) report_status(A.status, kDevKvOverflow);
+    return;
+  }
+  if (H.abort_flag) return;  // an earlier step gave up: the words are stale until the host clears them
+  if (tid < kHD / 2) H.rcs[tid] = A.rope_cs[(size_t)p * (kHD / 2) + tid];
   __syncthreads();
-  if (!ok0) return;
+  const int ns = attn_splits(A, p);
   if (warp == kCons) {
-    if (lane == 0) producer(A, H, smem, v, p);
+    if (lane == 0) producer(A, H, smem, v, G, p, ns);
     return;
   }
 
   // ---- consumers --------------------------------------------------------
-  if (!pos_ok && v == 0 && tid == 0) report_status(A.status, kDevKvOverflow);
-  int tok = *A.token;
-  if (tok < 0 || tok >= A.vocab) {
-    if (tid == 0 && v == 0) report_status(A.status, kDevBadToken);
-    tok = 0;
-  }
-  const int ns = attn_splits(A, p);
   const int item = v < A.nkv * ns ? v : -1;
-  Cons cs{0, 0};
-  unsigned bar_n = 2;
-  float best_v = -INFINITY;
-  int best_i = 0x7fffffff;
-  auto range = [&](int mat, int& b0, int& b1) { sm_range(A.geo[mat].lb_total, v, A.nsm, A.cps, b0, b1); };
-  int b0, b1;
-  for (int l = 0; l < A.n_layers; ++l) {
+  bf16* res = reinterpret_cast<bf16*>(smem + A.off_res);
+  int seq = 0, rot = 0;
+  int q0, q1, o0, o1, g0, g1, d0, d1;
+  cta_range(A.geo[kMatQkv].lb_total, v, G, q0, q1);
+  cta_range(A.geo[kMatO].lb_total, v, G, o0, o1);
+  cta_range(A.geo[kMatGu].lb_total, v, G, g0, g1);
+  cta_range(A.geo[kMatDown].lb_total, v, G, d0, d1);
+  for (int l = 0; l < L; ++l) {
     const StepLayer& LW = A.layers[l];
+    const unsigned flag = H.ebase + (unsigned)l + 1u;
     const int ab = l & 1;
     const uint32_t apar = (uint32_t)((l >> 1) & 1);
     const bf16* aux = reinterpret_cast<const bf16*>(smem + A.off_aux + ab * A.aux_stride);
-    range(kMatQkv, b0, b1);
-    gemv_phase_any<4>(A.bits[kMatQkv], A, H, smem, A.geo[kMatQkv], A.ga[l == 0 ? 0 : 1], b0, b1, aux,
-                      &H.auxfull[ab], apar, tok, cs, tid, best_v, best_i, -1, 0, v);
-    if (!grid_barrier<CSync>(A, bar_n++ * G, tid, H)) return;
-    attn_phase<HPG>(A, H, smem, LW, aux, &H.auxfull[ab], apar, item, ns, p, cs, tid);
-    if (!grid_barrier<CSync>(A, bar_n++ * G, tid, H)) return;
-    range(kMatO, b0, b1);
-    gemv_phase_any<4>(A.bits[kMatO], A, H, smem, A.geo[kMatO], A.ga[2], b0, b1, nullptr, nullptr, 0u, tok, cs, tid,
-                      best_v, best_i, -1, ns, v);
-    if (!grid_barrier<CSync>(A, bar_n++ * G, tid, H)) return;
-    // post-attention norm + gate|up + SwiGLU (the aux buffer is free after its prologue)
-    range(kMatGu, b0, b1);
-    gemv_phase_any<4>(A.bits[kMatGu], A, H, smem, A.geo[kMatGu], A.ga[3], b0, b1, aux + A.H, &H.auxfull[ab], apar,
-                      tok, cs, tid, best_v, best_i, ab, 0, v);
-    if (!grid_barrier<CSync>(A, bar_n++ * G, tid, H)) return;
-    range(kMatDown, b0, b1);
-    gemv_phase_any<4>(A.bits[kMatDown], A, H, smem, A.geo[kMatDown], A.ga[4], b0, b1, nullptr, nullptr, 0u, tok, cs,
-                      tid, best_v, best_i, -1, 0, v);
-    if (!grid_barrier<CSync>(A, bar_n++ * G, tid, H)) return;
+    // ---- input norm + qkv: x of this layer into res (the o residual too)
+    if (q1 > q0 || o1 > o0) {
+      if (l == 0)
+        load_res_embed(A, H.tok, res, tid);
+      else
+        load_res_fw(A.xw, A.H, flag - 1u, res, A, H, tid);
+    }
+    CSync::sync();
+    if (aborted(H)) return;
+    if (q1 > q0) {
+      const PGeom& geo = A.geo[kMatQkv];
+      wait_or_abort(&H.auxfull[ab], apar, &H.abort_flag, A.status);
+      stage_norm(geo, pg_smem(smem, geo), res, aux, A.eps, H, tid);
+      CSync::sync();
+      gemv_any(A.bits[kMatQkv], A, H, smem, geo, q0, q1, seq, rot, tid);
+      epilogue_fw<kOutStore>(geo, pg_smem(smem, geo), q0, q1, res, A.qkvw, flag, H.xsc, tid);
+    }
+    // ---- attention (its shared memory overlaps the GEMV phases' slots)
+    CSync::sync();
+    attn_phase<HPG>(A, H, smem, LW, aux, &H.auxfull[ab], apar, item, ns, p, flag, seq, tid);
+    CSync::sync();
+    if (aborted(H)) return;
+    // ---- o projection + residual
+    if (o1 > o0) {
+      const PGeom& geo = A.geo[kMatO];
+      stage_raw_fw(geo, pg_smem(smem, geo), A.attw, flag, A, H, tid);
+      CSync::sync();
+      if (aborted(H)) return;
+      gemv_any(A.bits[kMatO], A, H, smem, geo, o0, o1, seq, rot, tid);
+      epilogue_fw<kOutResid>(geo, pg_smem(smem, geo), o0, o1, res, A.xmw, flag, H.xsc, tid);
+    }
+    // ---- post-attention norm + gate|up + SwiGLU: x of the MLP into res
+    // (the down residual too)
+    CSync::sync();
+    if (g1 > g0 || d1 > d0) load_res_fw(A.xmw, A.H, flag, res, A, H, tid);
+    CSync::sync();
+    if (aborted(H)) return;
+    if (g1 > g0) {
+      const PGeom& geo = A.geo[kMatGu];
+      wait_or_abort(&H.auxfull[ab], apar, &H.abort_flag, A.status);
+      stage_norm(geo, pg_smem(smem, geo), res, aux + A.H, A.eps, H, tid);
+      CSync::sync();
+      gemv_any(A.bits[kMatGu], A, H, smem, geo, g0, g1, seq, rot, tid);
+      epilogue_fw<kOutSwiglu>(geo, pg_smem(smem, geo), g0, g1, res, A.hw, flag, H.xsc, tid);
+    }
+    // the aux buffer of this layer is read for the last time above
+    CSync::sync();
+    if (tid == 0) mbar_arrive(&H.auxempty[ab]);
+    // ---- down projection + residual
+    if (d1 > d0) {
+      const PGeom& geo = A.geo[kMatDown];
+      stage_raw_fw(geo, pg_smem(smem, geo), A.hw, flag, A, H, tid);
+      CSync::sync();
+      if (aborted(H)) return;
+      gemv_any(A.bits[kMatDown], A, H, smem, geo, d0, d1, seq, rot, tid);
+      epilogue_fw<kOutResid>(geo, pg_smem(smem, geo), d0, d1, res, A.xw, flag, H.xsc, tid);
+    }
+    CSync::sync();  // res and the slots are rewritten by the next layer
   }
   // ---- final norm + lm_head + greedy argmax -----------------------------
-  const int lb = A.n_layers & 1;
-  range(kMatLm, b0, b1);
-  gemv_phase_any<4>(A.bits[kMatLm], A, H, smem, A.geo[kMatLm], A.ga[5], b0, b1,
-                    reinterpret_cast<const bf16*>(smem + A.off_aux + lb * A.aux_stride), &H.auxfull[lb],
-                    (uint32_t)((A.n_layers >> 1) & 1), tok, cs, tid, best_v, best_i, -1, 0, v);
-  if (H.abort_flag) return;
-  if (pg_argmax_merge<CSync>(A.ga[5], best_v, best_i, blockIdx.x, G, tid, kCons, H.wv, H.wi, &H.flag)) {
-    // every CTA has passed every barrier: reset the step's counters
-    for (int i = tid; i < 4 + A.nsm; i += kNT)
-      if (i != 2) A.sync[i] = 0u;
+  float best_v = -INFINITY;
+  int best_i = 0x7fffffff;
+  {
+    const PGeom& geo = A.geo[kMatLm];
+    int m0, m1;
+    cta_range(geo.lb_total, v, G, m0, m1);
+    if (m1 > m0) {
+      load_res_fw(A.xw, A.H, H.ebase + (unsigned)L, res, A, H, tid);
+      CSync::sync();
+      if (aborted(H)) return;
+      const int lb = L & 1;
+      const bf16* fnorm = reinterpret_cast<const bf16*>(smem + A.off_aux + lb * A.aux_stride);
+      wait_or_abort(&H.auxfull[lb], (uint32_t)((L >> 1) & 1), &H.abort_flag, A.status);
+      const PgSmem sm = pg_smem(smem, geo);
+      stage_norm(geo, sm, res, fnorm, A.eps, H, tid);
+      CSync::sync();
+      gemv_any(A.bits[kMatLm], A, H, smem, geo, m0, m1, seq, rot, tid);
+      const int SKP = geo.S * 2;
+      const float xs = H.xsc;
+      for (int i = tid; i < (m1 - m0) * 16; i += kNT) {
+        const int n = m0 * 16 + i;
+        const float val = bfround(row_value(sm.red, i, SKP, xs));
+        if (A.logits) A.logits[n] = f2bf(val);
+        if (val == val && (val > best_v || (val == best_v && n < best_i))) {
+          best_v = val;
+          best_i = n;
+        }
+      }
+    }
+  }
+  if (aborted(H)) return;
+  // ---- greedy token over all CTAs: (max, first index); the last CTA to
+  // arrive (ticket) writes the token and moves the step on
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best_v, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, best_i, o);
+    argmax_pair(best_v, best_i, ov, oi);
+  }
+  if (lane == 0) {
+    H.wv[warp] = best_v;
+    H.wi[warp] = best_i;
+  }
+  CSync::sync();
+  if (tid == 0) {
+    float bv = H.wv[0];
+    int bi = H.wi[0];
+    for (int w = 1; w < kCons; ++w) argmax_pair(bv, bi, H.wv[w], H.wi[w]);
+    A.am_val[v] = bv;
+    A.am_idx[v] = bi;
+    __threadfence();
+    H.flag = (atomicAdd(A.am_ticket, 1u) == (unsigned)G - 1) ? 1u : 0u;
+  }
+  CSync::sync();
+  if (!H.flag) return;
+  __threadfence();
+  if (warp == 0) {
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int c = lane; c < G; c += 32) argmax_pair(bv, bi, __ldcg(A.am_val + c), __ldcg(A.am_idx + c));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      argmax_pair(bv, bi, ov, oi);
+    }
+    if (lane == 0) {
+      if (bi == 0x7fffffff) bi = 0;
+      *A.token = bi;
+      if (A.hist && A.hist_n) {
+        const int hn = *A.hist_n;
+        A.hist[hn % A.hist_cap] = bi;
+        *A.hist_n = hn + 1;
+      }
+      *A.pos = p + 1;
+      *A.am_ticket = 0u;
+      *A.epoch = *reinterpret_cast<volatile unsigned*>(A.epoch) + 1u;
+    }
   }
 }
 
@@ -730,30 +976,42 @@ int attn_bytes() {
   return (int)sizeof(AttnSm<HPG>);
 }
 
+const void* kernel_for(int hpg) {
+  switch (hpg) {
+    case 1: return reinterpret_cast<const void*>(step_kernel<1>);
+    case 2: return reinterpret_cast<const void*>(step_kernel<2>);
+    case 4: return reinterpret_cast<const void*>(step_kernel<4>);
+    default: return nullptr;
+  }
+}
+
 }  // namespace
 
-size_t step_sync_words(int num_sms) { return (size_t)(4 + num_sms + 28); }
+void step_exchange_words(const StepShape& sh, size_t words[5]) {
+  words[0] = (size_t)sh.H / 2;
+  words[1] = (size_t)(sh.nq + 2 * sh.nkv) * kHD / 2;
+  words[2] = (size_t)sh.nq * kHD / 2;
+  words[3] = (size_t)sh.H / 2;
+  words[4] = (size_t)sh.I / 2;
+}
 
-int step_make_plan(const StepShape& sh, int num_sms, int cps, int budget, StepPlan* plan) {
+int step_make_plan(const StepShape& sh, int num_sms, int budget, StepPlan* plan) {
   static_assert(sizeof(StepArgs) <= 4096, "step arguments exceed the kernel parameter space");
-  if (sh.gs != 64 || sh.hd != kHD || sh.nkv <= 0 || sh.nq % sh.nkv != 0 || num_sms <= 0 || cps < 1 || cps > 2)
-    return -1;
+  if (sh.gs != 64 || sh.hd != kHD || sh.nkv <= 0 || sh.nq % sh.nkv != 0 || num_sms <= 0) return -1;
   const int hpg = sh.nq / sh.nkv;
   if (hpg != 1 && hpg != 2 && hpg != 4) return -1;
   if (sh.H % 64 != 0 || sh.I % 64 != 0) return -1;
   StepPlan P{};
   StepArgs& A = P.tmpl;
   memset(&A, 0, sizeof(A));
-  P.cps = cps;
-  P.grid = num_sms * cps;
+  P.grid = num_sms;
   P.hpg = hpg;
   A.nsm = num_sms;
-  A.cps = cps;
-  const int slot_bytes = cps == 1 ? kSlotBytes : kSlotBytes / 2;
-  A.slot_bytes = slot_bytes;
+  A.slot_bytes = kSlotBytes;
   A.off_aux = round128((int)sizeof(StepHdr));
   A.aux_stride = round128(4 * sh.H + 512);
-  A.off_u = A.off_aux + 2 * A.aux_stride;
+  A.off_res = A.off_aux + 2 * A.aux_stride;
+  A.off_u = A.off_res + round128(2 * sh.H);
   const int N[5] = {(sh.nq + 2 * sh.nkv) * kHD, sh.H, 2 * sh.I, sh.H, sh.vocab};
   const int K[5] = {sh.H, sh.nq * kHD, sh.H, sh.I, sh.H};
   const int epi[5] = {kEpiStore, kEpiResid, kEpiSwiglu, kEpiResid, kEpiArgmax};
@@ -765,10 +1023,9 @@ int step_make_plan(const StepShape& sh, int num_sms, int cps, int budget, StepPl
     const int halves = epi[m] == kEpiSwiglu ? 2 : 1;
     if ((N[m] / halves) % 16 != 0) return -1;
     const int W = N[m] / halves / 16;
-    const int per_sm = (W + num_sms - 1) / num_sms;
-    const int lbs_max = (per_sm + cps - 1) / cps;
+    const int lbs_max = (W + num_sms - 1) / num_sms;
     const int tb = ptile_bytes(bits, 64);
-    const int st = slot_bytes / tb;
+    const int st = kSlotBytes / tb;
     if (st < 1) return -1;
     pgeom_make(&A.geo[m], K[m], bits, 64, epi[m], W, st, 0, 1, lbs_max, false);
     end = std::max(end, pgeom_layout(A.geo[m], 64, A.off_u));
@@ -777,93 +1034,23 @@ int step_make_plan(const StepShape& sh, int num_sms, int cps, int budget, StepPl
   const int ab = hpg == 1 ? attn_bytes<1>() : hpg == 2 ? attn_bytes<2>() : attn_bytes<4>();
   end = std::max(end, A.off_u + ab);
   A.off_ring = round128(end);
-  const int nslots = std::min(kMaxSlots, (budget - A.off_ring) / slot_bytes);
+  const int nslots = std::min(kMaxSlots, (budget - A.off_ring) / kSlotBytes);
   if (nslots < 2) return -1;
   A.nslots = nslots;
-  P.smem = A.off_ring + nslots * slot_bytes;
-  A.max_splits = std::min(std::min(64, P.grid / sh.nkv), kMaxMergeW / sh.nq);
+  P.smem = A.off_ring + nslots * kSlotBytes;
+  A.max_splits = std::min(kMaxSplitsMerge, num_sms / sh.nkv);
   if (A.max_splits < 1) return -1;
   A.n_layers = sh.layers;
   A.H = sh.H;
+  A.I = sh.I;
   A.nq = sh.nq;
   A.nkv = sh.nkv;
   A.cap = sh.cap;
   A.vocab = sh.vocab;
   A.scale = 1.0f / sqrtf((float)kHD);
+  A.scale_log2e = A.scale * 1.4426950408889634f;
   *plan = P;
   return 0;
-}
-
-void step_finish_args(StepArgs* a) {
-  auto base = [&](int K) {
-    GemvArgs g;
-    memset(&g, 0, sizeof(g));
-    g.K = K;
-    g.eps = a->eps;
-    g.norm_groups = 1;
-    g.x_slots = 1;
-    g.status = a->status;
-    return g;
-  };
-  GemvArgs q = base(a->H);  // input norm + qkv
-  q.pro = kProNorm;
-  q.x = a->h;
-  q.epi = kEpiStore;
-  q.y = a->qkvb;
-  a->ga[1] = q;
-  q.pro = kProEmbedNorm;  // layer 0: the token's embedding row, stored as the residual
-  q.emb_w = a->emb_w;
-  q.emb_s = a->emb_s;
-  q.emb_b = a->emb_b;
-  q.emb_bits = a->emb_bits;
-  q.emb_gs = a->emb_gs;
-  q.vocab = a->vocab;
-  q.x_out = a->h;
-  a->ga[0] = q;
-  GemvArgs o = base(a->nq * kHD);  // o projection + residual
-  o.pro = kProX;
-  o.x = a->attnb;
-  o.epi = kEpiResid;
-  o.res = a->h;
-  o.y = a->h;
-  a->ga[2] = o;
-  GemvArgs gu = base(a->H);  // post-attention norm + gate|up + SwiGLU
-  gu.pro = kProNorm;
-  gu.x = a->h;
-  gu.epi = kEpiSwiglu;
-  gu.y = a->act;
-  a->ga[3] = gu;
-  GemvArgs d = base(a->geo[kMatDown].K);  // down projection + residual
-  d.pro = kProX;
-  d.x = a->act;
-  d.epi = kEpiResid;
-  d.res = a->h;
-  d.y = a->h;
-  a->ga[4] = d;
-  GemvArgs lm = base(a->H);  // final norm + lm_head + greedy argmax
-  lm.pro = kProNorm;
-  lm.x = a->h;
-  lm.epi = kEpiArgmax;
-  lm.y = a->logits;
-  lm.am_val = a->am_val;
-  lm.am_idx = a->am_idx;
-  lm.am_ticket = a->am_ticket;
-  lm.tok_out = a->token;
-  lm.hist = a->hist;
-  lm.hist_n = a->hist_n;
-  lm.hist_cap = a->hist_cap;
-  lm.pos = a->pos;
-  lm.pos_inc = 1;
-  a->ga[5] = lm;
-}
-
-static const void* kernel_for(int hpg) {
-  switch (hpg) {
-    case 1: return reinterpret_cast<const void*>(step_kernel<1>);
-    case 2: return reinterpret_cast<const void*>(step_kernel<2>);
-    case 4: return reinterpret_cast<const void*>(step_kernel<4>);
-    default: return nullptr;
-  }
 }
 
 int step_occupancy(const StepPlan& p) {

@@ -4,14 +4,20 @@
 // Replaces, for a dense single-GPU model, the per-layer kernel chain of the
 // decode step (qkv GEMV -> attention -> o GEMV -> gate|up GEMV -> down GEMV,
 // then the lm_head with argmax; the traced step of
-// crates/serve/src/compiled.rs:127-201).  Every CTA stays resident for the
-// whole step; phases are separated by a grid-wide barrier on a device
-// counter instead of a kernel boundary, and each CTA's producer warp streams
-// the packed weights (and the KV rows its attention split reads) of phase
-// after phase into a shared-memory ring without waiting for the phases to
-// start: weights do not depend on activations, so HBM keeps streaming
-// across the barriers.  Work is assigned per SM (two CTAs per SM share an SM's
-// slice), so no SM holds more than its share.
+// crates/serve/src/compiled.rs:127-201).  One CTA per SM stays resident for
+// the whole step.  Each CTA's producer warp streams the packed weights (and
+// the KV rows its attention split reads) of phase after phase into a
+// shared-memory ring without waiting for the phases to start: weights do not
+// depend on activations, so HBM keeps streaming while the consumers wait for
+// their inputs.
+//
+// Phases hand their outputs on through flag words: 64-bit words whose low
+// half holds 4 bytes of data (two bf16) and whose high half holds the flag of
+// the (step, layer) that wrote them.  A word is written by one 64-bit store
+// and read by 64-bit loads, so its data and flag travel together: a consumer
+// polls the words of its input vector until every flag is the expected one,
+// and needs neither a grid barrier nor a separate flag.  Flags grow by one
+// per layer; the host clears the words before the 32-bit flag could wrap.
 #pragma once
 #include "pgemv_dev.cuh"
 
@@ -34,9 +40,6 @@ struct StepArgs {
   int n_layers;
   pg::PGeom geo[5];  // per matrix kind, offsets in this kernel's layout
   int bits[5];
-  // prologue / epilogue arguments of the GEMV phases: qkv of layer 0
-  // (embedding + norm), qkv, o, gate|up, down, lm_head (+ argmax)
-  GemvArgs ga[6];
   const unsigned char* lm_w;  // packed lm_head (the embedding when tied)
   const bf16* final_norm;
   const uint32_t* emb_w;  // quantized embedding table
@@ -44,17 +47,23 @@ struct StepArgs {
   const bf16* emb_b;
   int emb_bits, emb_gs, vocab;
   int* token;  // in: this step's token; out: the next one
-  int H;
+  int H, I;
   float eps;
-  bf16* h;       // residual stream [H]
-  bf16* qkvb;    // [(nq + 2 nkv) * 128]
-  bf16* attnb;   // [nq * 128]
-  bf16* act;     // SwiGLU output [I]
-  bf16* logits;  // [vocab]
+  // flag-word exchange buffers (two bf16 per word)
+  uint64_t* xw;    // residual stream after a layer [H / 2]
+  uint64_t* qkvw;  // fused q|k|v projection [(nq + 2 nkv) * 64]
+  uint64_t* attw;  // attention output [nq * 64]
+  uint64_t* xmw;   // residual after the attention block [H / 2]
+  uint64_t* hw;    // SwiGLU output [I / 2]
+  unsigned* epoch;  // steps since the words were cleared (the last CTA adds one)
+  unsigned* abort_word;  // nonzero: a CTA gave up on a wait; every CTA leaves
+  bf16* logits;          // [vocab]
   const float2* rope_cs;  // (cos, sin) [cap][64]
   int cap, nq, nkv;
-  float scale;
-  float* attn_part;  // [n_kv][max_splits][hpg][132]: m, l, pad, pad, unnormalised output
+  float scale;        // 1 / sqrt(head_dim)
+  float scale_log2e;  // scale * log2 e: scores in the base-2 domain
+  float* attn_part;     // [n_kv][max_splits][hpg][132]: m, l, pad, pad, unnormalised output
+  unsigned* attn_tick;  // [n_kv], zero between uses
   int max_splits;
   int* pos;  // device offset; += 1 at the end of the step
   int* hist;
@@ -63,12 +72,9 @@ struct StepArgs {
   float* am_val;  // [grid]
   int* am_idx;
   unsigned* am_ticket;
-  // [0] barrier arrivals, [1] placement fallback, [2] abort, [4, 4 + nsm)
-  // per-SM arrivals; all zero between steps (the last CTA resets them)
-  unsigned* sync;
-  int nsm, cps;  // SMs, CTAs per SM (grid = nsm * cps)
+  int nsm;  // grid = one CTA per SM
   int slot_bytes, nslots;
-  int off_aux, aux_stride, off_u, off_ring;
+  int off_aux, aux_stride, off_res, off_u, off_ring;
   int* status;
 };
 
@@ -78,22 +84,18 @@ struct StepShape {
 };
 
 struct StepPlan {
-  int grid, cps, smem, hpg;
+  int grid, smem, hpg;
   StepArgs tmpl;  // geometry and layout (pointers unset)
 };
 
-// Words of the `sync` block for `num_sms` SMs.
-size_t step_sync_words(int num_sms);
-// Plans the step for `cps` CTAs per SM within `budget` bytes of shared
-// memory per CTA.  Returns 0, or -1 when the shape is not supported (the
-// caller keeps the per-kernel chain).
-int step_make_plan(const StepShape& sh, int num_sms, int cps, int budget, StepPlan* plan);
-// Fills a.ga from the other fields (after the pointers are set).
-void step_finish_args(StepArgs* a);
-// CTAs of the step kernel that fit on one SM with the plan's shared memory.
+// Flag-word counts of the exchange buffers (xw, qkvw, attw, xmw, hw in order).
+void step_exchange_words(const StepShape& sh, size_t words[5]);
+// Plans the step within `budget` bytes of shared memory per CTA; 0 on success.
+int step_make_plan(const StepShape& sh, int num_sms, int budget, StepPlan* plan);
+// CTAs of the step kernel that fit on one SM (0: the plan cannot launch).
 int step_occupancy(const StepPlan& p);
-// One decode step.  `coop` asks for a cooperative launch (co-residency
-// checked by the driver).
+// Launches one decode step (cooperative: all CTAs resident, which the
+// flag-word waits require).
 cudaError_t step_launch(const StepArgs& a, const StepPlan& p, cudaStream_t st, bool coop);
 
 }  // namespace emx

@@ -86,7 +86,7 @@ int emx_set_memory_limit(emx_ctx* ctx, size_t limit, size_t* previous);
  * One entry per MlxCtx method on the Qwen3 path; all pointers are device
  * pointers, all work is enqueued on ctx's stream. */
 
-/* MlxCtx::quantized_matmul (crates/mlx-ffi/src/ops/real/transform.rs:127-138):
+/* MlxCtx::quantized_matmul (crates/mlx-ffi/src/ops/real/transform.rs:77-89):
  * y[M,N] = x[M,K] . dequant(w)^T; transpose must be 1; bits 4|8; group 32|64|128.
  * M == 1 runs the batch-1 GEMV, M > 1 the prefill GEMM. */
 int emx_quantized_matmul(emx_ctx* ctx, const void* x, const void* w, const void* scales, const void* biases, void* y,
@@ -99,11 +99,11 @@ int emx_quantized_matmul(emx_ctx* ctx, const void* x, const void* w, const void*
 int emx_qpack_bytes(int N, int K, int group_size, int bits, size_t* bytes);
 int emx_qpack(emx_ctx* ctx, const void* w, const void* scales, const void* biases, void* out, int N, int K,
               int group_size, int bits);
-/* MlxCtx::quantized_matmul at M == 1 (transform.rs:127-138) over a packed
+/* MlxCtx::quantized_matmul at M == 1 (transform.rs:77-89) over a packed
  * tensor: y[N] = x[K] . dequant(w)^T, the decode GEMV the engine runs. */
 int emx_quantized_matvec_packed(emx_ctx* ctx, const void* x, const void* packed, void* y, int N, int K,
                                 int group_size, int bits);
-/* MlxCtx::dequantize_weight (transform.rs:95-109): out bf16[N,K]. */
+/* MlxCtx::dequantize_weight (transform.rs:45-60): out bf16[N,K]. */
 int emx_dequantize(emx_ctx* ctx, const void* w, const void* scales, const void* biases, void* out, int N, int K,
                    int group_size, int bits);
 /* MlxCtx::quantize_kv_native / mlx_quantize affine (crates/mlx-ffi/src/ops/real/quant.rs:8-38):
@@ -147,7 +147,7 @@ int emx_add(emx_ctx* ctx, const void* a, const void* b, void* out, size_t n);
 /* MlxCtx::argmax (crates/mlx-ffi/src/ops/real/array.rs:6-10): first index of
  * the maximum of each row; out int32[rows] (device). */
 int emx_argmax(emx_ctx* ctx, const void* x, int rows, int n, int32_t* out);
-/* sample_token (crates/serve/src/sampler.rs:98-202) on the device, for
+/* sample_token (crates/serve/src/sampler.rs:101-202) on the device, for
  * temperature >= 1e-6: temperature scaling, top-k (0 = off), softmax, top-p
  * (stable descending order, ties by index), renormalisation, one draw of
  * SimpleRng (xorshift64*; *rng_state is a device uint64 advanced in place)
@@ -212,8 +212,8 @@ typedef struct {
 
 typedef struct emx_qwen3 emx_qwen3;
 
-/* Host only: Qwen3Config::from_dir (crates/serve/src/config.rs:73-86, fields
- * and serde defaults at config.rs:6-30, head_dim default at config.rs:88-91)
+/* Host only: Qwen3Config::from_dir (crates/serve/src/config.rs:77-90, fields
+ * and serde defaults at config.rs:8-30, head_dim default at config.rs:92-96)
  * from `model_dir`/config.json (or a config.json path), plus the MoE keys
  * (num_experts, num_experts_per_tok, moe_intermediate_size, norm_topk_prob)
  * and tie_word_embeddings (default true).  Quantization: the model-wide

@@ -172,7 +172,7 @@ void orc_quantize(const float* w, int N, int K, int gs, int bits, uint32_t* wq, 
     }
 }
 
-/* mlx_dequantize affine -> bf16 (crates/mlx-ffi/src/ops/real/transform.rs:95-109):
+/* mlx_dequantize affine -> bf16 (crates/mlx-ffi/src/ops/real/transform.rs:45-60):
  * each element is the bf16 nearest to the exact s*q + b.  (An fp32 evaluation
  * followed by a cast gives the same bits whenever fp32 holds the sum exactly,
  * which is every group whose min and range are within 2^16 of each other.) */
@@ -189,7 +189,7 @@ void orc_dequantize(const uint32_t* wq, const uint16_t* scales, const uint16_t* 
     }
 }
 
-/* mlx_quantized_matmul (crates/mlx-ffi/src/ops/real/transform.rs:127-138),
+/* mlx_quantized_matmul (crates/mlx-ffi/src/ops/real/transform.rs:77-89),
  * called as qmatmul (crates/ops/src/quant.rs:57-76) for every Qwen3 linear. */
 /* Summation order of orc_qmatmul's fp32 reductions: 0 ascending k (the
  * reference's order), 1 descending.  Both are valid fp32 evaluations of the
@@ -451,7 +451,7 @@ static int last_argmax(const float* x, int n) {
     return best;
 }
 
-/* sample_token (sampler.rs:98-202), step for step in f32: temperature
+/* sample_token (sampler.rs:101-202), step for step in f32: temperature
  * scaling; top-k keeps values >= the k-th largest; softmax over the finite
  * values with a sequential sum; top-p keeps the largest probabilities (stable
  * descending order) until their running f32 sum reaches top_p; renormalise

@@ -26,7 +26,7 @@ def py_rng(seed):
 
 
 def py_sample(logits, temperature, top_p, top_k, r):
-    """sample_token (sampler.rs:98-202) in float32, sequential sums, stable sorts."""
+    """sample_token (sampler.rs:101-202) in float32, sequential sums, stable sorts."""
     x = np.asarray(logits, dtype=F32)
     n = x.size
     if temperature < 1e-6:

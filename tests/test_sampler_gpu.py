@@ -1,5 +1,5 @@
 """Device sampling (emx_sample_token, emx_qwen3_set_sampling) against the CPU
-oracle's restatement of the host sampler (crates/serve/src/sampler.rs:98-202).
+oracle's restatement of the host sampler (crates/serve/src/sampler.rs:101-202).
 
 The generator stream is bit-exact, so both sides draw the same r.  The host
 sums sequentially in fp32 and the device per slice; a token may differ only
