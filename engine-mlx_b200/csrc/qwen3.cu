@@ -91,6 +91,9 @@ struct Spec {
 
 using namespace emx;
 
+// Decode steps emx_qwen3_decode_stream keeps in flight ahead of its callback.
+constexpr int kStreamDepth = 8;
+
 struct emx_qwen3 {
   emx_ctx* ctx = nullptr;
   emx_qwen3_config c{};
@@ -128,7 +131,9 @@ struct emx_qwen3 {
   int offset = 0;
   cudaGraphExec_t gexec = nullptr;
   int step_launches = 0;
-  int32_t* pinned = nullptr;  // pinned host staging [kv_cap + 4]
+  int32_t* pinned = nullptr;  // pinned host staging [kv_cap + 8]
+  cudaEvent_t stream_ev[kStreamDepth] = {};  // decode_stream: one per step in flight
+  int32_t* stream_st = nullptr;               // decode_stream: device status after each step in flight (pinned)
   // persistent decode step (dense model on one GPU)
   bool step_ok = false;    // the shape has a plan and it fits
   bool fused = false;      // decode through the persistent step kernel
@@ -1188,6 +1193,9 @@ int emx_qwen3_destroy(emx_qwen3* m) {
   if (m->gexec) cudaGraphExecDestroy(m->gexec);
   for (void* p : m->allocs) ctx_free(m->ctx, p);
   if (m->pinned) cudaFreeHost(m->pinned);
+  for (cudaEvent_t e : m->stream_ev)
+    if (e) cudaEventDestroy(e);
+  if (m->stream_st) cudaFreeHost(m->stream_st);
   delete m;
   return EMX_OK;
 }
@@ -1545,6 +1553,82 @@ int emx_qwen3_decode(emx_qwen3* m, int32_t token, int n, int32_t* tokens_out) {
   rc = ctx_sync_check(m->ctx, "emx_qwen3_decode");
   if (rc) return rc;
   memcpy(tokens_out, m->pinned, sizeof(int32_t) * n);
+  return EMX_OK;
+}
+
+int emx_qwen3_decode_stream(emx_qwen3* m, int32_t token, int n, emx_token_cb cb, void* user, int* n_done) {
+  Q_REQUIRE(m && cb, "emx_qwen3_decode_stream: null argument");
+  Q_REQUIRE(n >= 1, "emx_qwen3_decode_stream: n=%d", n);
+  Q_REQUIRE(token >= 0 && token < m->c.vocab, "emx_qwen3_decode_stream: token %d outside [0, %d)", token,
+            m->c.vocab);
+  if (n_done) *n_done = 0;
+  if (m->offset + n > m->c.kv_cap)
+    return fail(EMX_ERR_STATE, "static KV overflow offset=%d + n=%d > cap=%d", m->offset, n, m->c.kv_cap);
+  cudaStream_t st = m->ctx->stream;
+  // steps in flight ahead of the callback: greedy decoding runs ahead (the
+  // steps past a stop are rolled back below); sampling runs one step at a
+  // time so the generator state never holds a discarded draw
+  const int depth = m->sampling ? 1 : kStreamDepth;
+  if (!m->stream_ev[0]) {
+    for (int i = 0; i < kStreamDepth; ++i)
+      EMX_CHECK_CUDA(cudaEventCreateWithFlags(&m->stream_ev[i], cudaEventDisableTiming), "stream events");
+    if (cudaMallocHost(reinterpret_cast<void**>(&m->stream_st), sizeof(int32_t) * kStreamDepth) != cudaSuccess)
+      return fail(EMX_ERR_OOM, "stream status buffer");
+  }
+  const int offset0 = m->offset;
+  m->pinned[0] = token;
+  m->pinned[1] = 0;
+  EMX_CHECK_CUDA(cudaMemcpyAsync(m->token, m->pinned, sizeof(int32_t), cudaMemcpyHostToDevice, st), "stream token");
+  EMX_CHECK_CUDA(cudaMemcpyAsync(m->hist_n, m->pinned + 1, sizeof(int32_t), cudaMemcpyHostToDevice, st),
+                 "stream history");
+  int32_t* out = m->pinned + 4;  // token of step i at out[i] (pinned holds kv_cap + 8 ints)
+  int issued = 0, done = 0, rc = EMX_OK;
+  bool stop = false;
+  while (done < n && !stop) {
+    // keep `depth` steps in flight: each one's token and the device status
+    // are copied to pinned memory behind an event
+    while (issued < n && issued - done < depth) {
+      if ((rc = run_steps(m, 1))) break;
+      cudaError_t e = cudaMemcpyAsync(out + issued, m->token, sizeof(int32_t), cudaMemcpyDeviceToHost, st);
+      if (e == cudaSuccess)
+        e = cudaMemcpyAsync(m->stream_st + issued % kStreamDepth, m->ctx->status, sizeof(int32_t),
+                            cudaMemcpyDeviceToHost, st);
+      if (e == cudaSuccess) e = cudaEventRecord(m->stream_ev[issued % kStreamDepth], st);
+      if (e != cudaSuccess) {
+        rc = fail_cuda(e, "stream step");
+        break;
+      }
+      ++issued;
+    }
+    if (rc) break;
+    const cudaError_t e = cudaEventSynchronize(m->stream_ev[done % kStreamDepth]);
+    if (e != cudaSuccess) {
+      rc = fail_cuda(e, "stream wait");
+      break;
+    }
+    if (m->stream_st[done % kStreamDepth] != 0) {  // a device error: report it with the stream drained
+      rc = ctx_sync_check(m->ctx, "emx_qwen3_decode_stream");
+      if (!rc) rc = fail(EMX_ERR_DEVICE, "emx_qwen3_decode_stream: device status %d", m->stream_st[done % kStreamDepth]);
+      break;
+    }
+    const int32_t t = out[done];
+    ++done;
+    if (n_done) *n_done = done;
+    if (cb(t, done - 1, user) != 0) stop = true;
+  }
+  if (rc) return rc;
+  if (issued > done) {
+    // the callback stopped early: the steps run past it are discarded
+    // (their K/V rows lie beyond the offset and are overwritten later)
+    EMX_CHECK_CUDA(cudaStreamSynchronize(st), "stream drain");
+    m->offset = offset0 + done;
+    m->pinned[0] = out[done - 1];
+    m->pinned[1] = offset0 + done;
+    m->pinned[2] = done;
+    EMX_CHECK_CUDA(cudaMemcpyAsync(m->state, m->pinned, 3 * sizeof(int32_t), cudaMemcpyHostToDevice, st),
+                   "stream rollback");
+    return ctx_sync_check(m->ctx, "emx_qwen3_decode_stream");
+  }
   return EMX_OK;
 }
 

@@ -116,10 +116,15 @@ _SIGS = {
     "emx_qwen3_decode": (C.c_int, [C.c_void_p, C.c_int32, C.c_int, C.c_void_p]),
     "emx_qwen3_prefill_device": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int]),
     "emx_qwen3_decode_device": (C.c_int, [C.c_void_p, C.c_int]),
+    "emx_qwen3_decode_stream": (C.c_int, [C.c_void_p, C.c_int32, C.c_int, C.c_void_p, C.c_void_p,
+                                          C.POINTER(C.c_int)]),
     "emx_qwen3_step_launches": (C.c_int, [C.c_void_p, C.POINTER(C.c_int)]),
 }
 
 _lib: Optional[C.CDLL] = None
+
+# emx_token_cb: int (*)(int32_t token, int index, void* user)
+TOKEN_CB = C.CFUNCTYPE(C.c_int, C.c_int32, C.c_int, C.c_void_p)
 
 
 def lib() -> C.CDLL:
@@ -695,6 +700,27 @@ class Qwen3:
         out = np.empty(n, dtype=np.int32)
         _check(lib().emx_qwen3_decode(self.h, int(token), n, out.ctypes.data))
         return out
+
+    def decode_stream(self, token: int, n: int, on_token) -> int:
+        """Per-token streaming (emx_qwen3_decode_stream): on_token(token, index)
+        is called as each token is produced; a true return value stops after
+        that token.  Returns the number of tokens delivered."""
+        err = []
+
+        def cb(tok, idx, _user):
+            try:
+                return 1 if on_token(int(tok), int(idx)) else 0
+            except BaseException as e:  # an exception stops the stream and is raised after it
+                err.append(e)
+                return 1
+
+        fn = TOKEN_CB(cb)
+        done = C.c_int()
+        rc = lib().emx_qwen3_decode_stream(self.h, int(token), n, C.cast(fn, C.c_void_p), None, C.byref(done))
+        if err:
+            raise err[0]
+        _check(rc)
+        return done.value
 
     def prefill_device(self, ids: Buffer, T: int):
         _check(lib().emx_qwen3_prefill_device(self.h, ids.ptr, T))

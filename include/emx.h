@@ -311,6 +311,20 @@ int emx_qwen3_decode_step(emx_qwen3* m, int32_t token, int32_t* next_token, void
 /* n greedy steps starting from `token`, one host synchronisation in total;
  * tokens_out receives the n generated ids. */
 int emx_qwen3_decode(emx_qwen3* m, int32_t token, int n, int32_t* tokens_out);
+/* Called by emx_qwen3_decode_stream with each generated token as it is
+ * produced (index = 0, 1, ... within the call); return 0 to go on, nonzero to
+ * stop after this token. */
+typedef int (*emx_token_cb)(int32_t token, int index, void* user);
+/* Per-token streaming for the server's SSE path (crates/serve/src/server.rs:
+ * 131-181 generates the whole reply, then splits it into words): up to n
+ * steps from `token`, each token handed to cb as soon as its step has run,
+ * while greedy decoding keeps up to 8 further steps in flight on the device.
+ * When cb returns nonzero the steps run past that token are discarded (the
+ * offset, device token and history return to just after it), so a stop at
+ * an end-of-sequence token leaves the engine as if decoding had stopped
+ * there.  With sampling on, steps run one at a time (no discarded draws).
+ * n_done (optional) receives the tokens delivered. */
+int emx_qwen3_decode_stream(emx_qwen3* m, int32_t token, int n, emx_token_cb cb, void* user, int* n_done);
 /* Device-resident variants for throughput measurement: no host copies.
  * prefill reads ids already on the device; decode runs n graph replays from
  * the device-held token. */

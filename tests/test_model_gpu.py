@@ -73,8 +73,10 @@ def noise_floor(ref, rev):
     return [(rel_l2(a[1], b[1]), float(np.abs(f32(a[1]) - f32(b[1])).max())) for a, b in zip(ref, rev)]
 
 
-def check_steps(gpu, ref, noise, what):
-    """gpu, ref: [(token, logits)]; noise: noise_floor(...) of the same steps."""
+def check_steps(gpu, ref, noise, what, max_tolerated=2):
+    """gpu, ref: [(token, logits)]; noise: noise_floor(...) of the same steps.
+    Returns (and prints) how many GPU tokens differed from the oracle's as
+    tolerated near-ties; more than max_tolerated fails."""
     tolerated = 0
     for i, ((tg, lg), (to, lo), (nrel, nabs)) in enumerate(zip(gpu, ref, noise)):
         e = rel_l2(lg, lo)
@@ -83,6 +85,8 @@ def check_steps(gpu, ref, noise, what):
             lead = float(f32(lo)[to] - f32(lo)[tg])
             assert lead <= 2 * nabs, f"{what} step {i}: token {tg} vs {to}, oracle lead {lead:.3g} > 2 x {nabs:.3g}"
             tolerated += 1
+    print(f"{what}: {tolerated} of {len(gpu)} tokens differ from the oracle's as tolerated near-ties")
+    assert tolerated <= max_tolerated, f"{what}: {tolerated} near-tie mismatches of {len(gpu)}"
     return tolerated
 
 
@@ -285,25 +289,42 @@ def test_state_errors(ctx):
         emx.Qwen3(ctx, emx.Qwen3Config(hidden=256, layers=1, n_q=4, n_kv=2, inter=512, vocab=1024, head_dim=64))
 
 
+# Full-width BASELINE shapes.  C2 and C3 run all 28 layers at a 128-token
+# prompt; the longer prompt and the 30B / 32B widths keep every matrix and
+# head count of the BASELINE config but fewer layers, so that the CPU oracle
+# (run twice, for the noise floor) finishes in about a minute.
+FULL_CASES = [("c2", 128, None), ("c3", 128, None), ("c3", 2048, 2), ("c4", 64, 2), ("c5", 64, 1)]
+
+
 @pytest.mark.slow
-@pytest.mark.parametrize("name,prompt_len", [("c2", 128), ("c3", 128)])
-def test_full_config_greedy_parity_32_steps(ctx, name, prompt_len):
-    """The first 32 greedy decode tokens of the full-size random-init C2 / C3
-    shapes (KV capacity trimmed to the test's length), replayed through the
-    oracle: each GPU token is the oracle's argmax or within its noise floor."""
+@pytest.mark.parametrize("name,prompt_len,layers", FULL_CASES,
+                         ids=[f"{n}-p{p}" + (f"-L{L}" if L else "") for n, p, L in FULL_CASES])
+def test_full_config_greedy_parity_32_steps(ctx, name, prompt_len, layers):
+    """The first 32 greedy decode tokens of the full-width random-init
+    BASELINE shapes (KV capacity trimmed to the test's length; layers as
+    FULL_CASES gives), replayed through the oracle: each GPU token is the
+    oracle's argmax or within twice its noise floor, and at most 2 of the 33
+    tokens (prefill + 32 steps) may be such tolerated near-ties.  C3 at a
+    2048-token prompt runs the tcgen05 prefill above 128 rows and decode
+    attention split over several KV ranges; C4 the 128-expert top-8 routing
+    and gathered expert GEMVs; C5 the 5120 / 25600 widths."""
     import dataclasses
 
-    cfg = dataclasses.replace(emx.CONFIGS[name], kv_cap=256, max_prefill=prompt_len)
+    kw = dict(kv_cap=prompt_len + 64, max_prefill=prompt_len)
+    if layers:
+        kw["layers"] = layers
+    cfg = dataclasses.replace(emx.CONFIGS[name], **kw)
     rng = np.random.default_rng(11)
     prompt = rng.integers(0, cfg.vocab, prompt_len).astype(np.int32)
     m = emx.Qwen3(ctx, cfg)
     m.init_random(2024)
     chain = [m.prefill(prompt)]
     chain += [int(t) for t in m.decode(chain[0], 32)]
+    path = "persistent step" if m.fused else "kernel chain"
     m.close()
     ref = oracle_run(cfg, 2024, prompt, chain[:-1])
     noise = noise_floor(ref, oracle_run(cfg, 2024, prompt, chain[:-1], reverse=True))
-    check_steps([(t, r[1]) for t, r in zip(chain, ref)], ref, noise, name)
+    check_steps([(t, r[1]) for t, r in zip(chain, ref)], ref, noise, f"{name} prompt {prompt_len} ({path})")
 
 
 @pytest.mark.parametrize("cfg_name,prompt_len,chunk", [("dense_int4", 150, 64), ("mixed_int8", 150, 40),
