@@ -875,9 +875,16 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
       gemv_any(A.bits[kMatGu], A, H, smem, geo, g0, g1, seq, rot, tid);
       epilogue_fw<kOutSwiglu>(geo, pg_smem(smem, geo), g0, g1, res, A.hw, flag, H.xsc, tid);
     }
-    // the aux buffer of this layer is read for the last time above
+    // the aux buffer of this layer is read for the last time above.  It is
+    // handed back only once its load has landed, also in a CTA that read none
+    // of it: the producer's next load into the buffer must not overtake this
+    // one (two loads on one phase of the count-1 barrier would complete it
+    // once, and a later wait on it would never end)
     CSync::sync();
-    if (tid == 0) mbar_arrive(&H.auxempty[ab]);
+    if (tid == 0) {
+      wait_or_abort(&H.auxfull[ab], apar, &H.abort_flag, A.status);
+      mbar_arrive(&H.auxempty[ab]);
+    }
     // ---- down projection + residual
     if (d1 > d0) {
       const PGeom& geo = A.geo[kMatDown];
