@@ -6,12 +6,19 @@ on B200, through libemx.
     python bench.py --impl reference ...   # the CPU oracle (reference restatement) arm
 
 One step = one greedy decode token (the whole 28-layer forward + lm_head +
-argmax, replayed from a CUDA graph).  The timed region holds exactly K steps,
-bracketed by a barrier and a device synchronise, timed with CUDA events on
-the engine's stream; with N GPUs (torchrun) every rank runs its own replica
-(the 1.7B model is not sharded: "replicas only") and `value` is the sum of
-all ranks' tokens over the slowest rank's time.  Weights (1.1 GB) are larger
-than L2 (126 MB), so every step streams them from HBM.
+argmax: one persistent kernel launch, replayed from a CUDA graph).  The timed
+region holds exactly K steps, bracketed by a barrier and a device synchronise,
+timed with CUDA events on the engine's stream; with N GPUs (torchrun) every
+rank runs its own replica (the 1.7B model is not sharded: "replicas only") and
+`value` is the sum of all ranks' tokens over the slowest rank's time.  Weights
+(1.1 GB) are larger than L2 (126 MB), so every step streams them from HBM.
+
+Besides the headline the line carries: prefill tok/s at 128 / 2048 / 8192
+tokens, decode after 2048- and 8192-token prompts, the single quantized linear
+of BASELINE configs[0] (M = 1 and 512), the packed GEMV alone, end-to-end
+rates through the public API (per-step and streamed), and `sharded`: the
+32B-shape model tensor-parallel over the job's GPUs (every N of a scaling run),
+so the 1 -> 8 curve holds the collective's scaling, not only replicas.
 """
 import argparse
 import json
@@ -123,10 +130,25 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------ arms
-def cpu_baseline(cfg, seed, steps, threads=None, warmup=0):
+def cpu_model():
+    """The host CPU's model name (for the CPU baseline's record)."""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for ln in f:
+                if ln.startswith("model name"):
+                    return ln.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+
+    return platform.processor() or "unknown"
+
+
+def cpu_baseline(cfg, seed, prompt_len, steps, warmup=0, threads=None):
     """The CPU oracle (restatement of the reference path, OpenMP) on this host:
-    decode tok/s over a bounded sample (16-token prompt, `warmup` untimed then
-    `steps` timed greedy steps)."""
+    a prefill of `prompt_len` random ids (seeded as the GPU arm's prompt), then
+    `warmup` untimed and `steps` timed greedy decode steps.  Returns decode
+    tok/s, the threads used and the prefill seconds."""
     import numpy as np
     import oracle
 
@@ -134,8 +156,10 @@ def cpu_baseline(cfg, seed, steps, threads=None, warmup=0):
         oracle.lib().orc_set_num_threads(threads)
     ck = oracle.make_checkpoint(cfg, seed)
     m = oracle.Model(cfg, ck)
-    prompt = (np.arange(16, dtype=np.int32) * 7919) % cfg.vocab
+    prompt = np.random.default_rng(seed).integers(0, cfg.vocab, prompt_len).astype(np.int32)
+    t0 = time.perf_counter()
     t = m.prefill(prompt)
+    prefill_s = time.perf_counter() - t0
     for _ in range(warmup):
         t = m.decode(t)
     t0 = time.perf_counter()
@@ -143,36 +167,197 @@ def cpu_baseline(cfg, seed, steps, threads=None, warmup=0):
         t = m.decode(t)
     dt = time.perf_counter() - t0
     m.close()
-    return steps / dt, oracle.lib().orc_num_threads()
+    return steps / dt, oracle.lib().orc_num_threads(), prefill_s
 
 
 def run_reference(args, cfg, rank):
+    """The reference arm: the CPU restatement of the reference's algorithm (MLX
+    and mlx-c cannot be built here) on the GPU arm's workload -- the same
+    prompt length, then the same warm-up and timed decode steps (at most 64) --
+    with every host thread."""
     if rank != 0:
         return
-    # a bounded sample: the oracle decodes ~2-5 tok/s on the host cores
-    steps = max(1, min(args.steps, 8))
-    warm = max(0, min(args.warmup, 3))
-    v, cores = cpu_baseline(cfg, args.seed, steps, warmup=warm)
+    steps = max(1, min(args.steps, 64))
+    warm = max(0, min(args.warmup, 5))
+    v, cores, pre_s = cpu_baseline(cfg, args.seed, args.prompt, steps, warmup=warm)
+    cfg_w = workload(args, cfg)
+    cfg_w["decode_tokens"] = steps
+    sample = (f"{args.config}: {args.prompt}-token prompt ({pre_s:.1f} s), {warm} untimed then {steps} timed greedy "
+              f"decode steps on {cpu_model()} (CPU oracle restatement of the reference path; MLX itself is not "
+              "buildable here)")
     line = {"metric": METRIC, "value": v, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus, "steps": steps,
             "warmup": warm, "ms_per_step": 1000.0 / v, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16 activations, int4/int8 affine weights", "data": "synthetic",
-            "config": workload(args, cfg),
-            "cpu_baseline": {"value": v, "unit": UNIT, "cores": cores, "kind": "port",
-                             "sample": f"{args.config}: 16-token prompt, {warm} untimed then {steps} timed "
-                                       "greedy decode steps "
-                                       "(CPU oracle restatement of the reference path; MLX itself is not "
-                                       "buildable here)"},
+            "config": cfg_w,
+            "cpu_baseline": {"value": v, "unit": UNIT, "cores": cores, "kind": "port", "cpu_model": cpu_model(),
+                             "prefill_s": pre_s, "sample": sample},
             "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
 def workload(args, cfg):
+    """The config block both arms print (the driver compares them)."""
     return {"workload": f"{args.config} (Qwen3-1.7B shape)" if args.config == "c3" else args.config,
             "model": f"random-init {args.config}", "hidden": cfg.hidden, "layers": cfg.layers,
             "attn_bits": cfg.attn_bits, "mlp_bits": cfg.mlp_bits, "group_size": cfg.mlp_group,
             "global_batch": 1, "prompt": args.prompt, "decode_tokens": args.steps, "seq_len": args.prompt,
-            "kv_cap": cfg.kv_cap, "parallelism": f"replicas x{args.gpus}",
+            "parallelism": (f"{'expert' if cfg.n_experts else 'tensor'} parallel x{args.gpus}" if args.shard
+                            else f"replicas x{args.gpus}"),
             "l2": "inputs larger than L2 (1.1 GB of weights streamed per token)"}
+
+
+def profiled_traffic(kernel_tag):
+    """Per-launch DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of
+    the kernel from its committed ncu summary (profiles/<kernel_tag>.md, line
+    'dram bytes per launch: N'), or None."""
+    p = os.path.join(ROOT, "profiles", kernel_tag + ".md")
+    try:
+        with open(p) as f:
+            for ln in f:
+                if ln.lower().startswith("dram bytes per launch:"):
+                    return float(ln.split(":", 1)[1].split()[0].replace(",", ""))
+    except (OSError, ValueError):
+        pass
+    return None
+
+
+def timed_decode(m, ctx, st, torch, n, barrier=None):
+    """Device time (ms) of n decode steps from the model's current state,
+    CUDA events on the engine's stream, synchronised on both sides."""
+    ctx.synchronize()
+    if barrier:
+        barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    m.decode_device(n)
+    e1.record(st)
+    e1.synchronize()
+    return e0.elapsed_time(e1)
+
+
+def decode_at_context(ctx, st, torch, cfg, m, hbm, seed, ctx_len, steps=32):
+    """Decode tok/s and the step roofline after a ctx_len-token prompt (the
+    BASELINE C3 prompt lengths 2048 / 8192)."""
+    import numpy as np
+
+    if ctx_len > cfg.max_prefill or ctx_len + steps + 8 > cfg.kv_cap:
+        return None
+    ids = ctx.put(np.random.default_rng(seed + ctx_len).integers(0, cfg.vocab, ctx_len).astype(np.int32))
+    m.reset()
+    m.prefill_device(ids, ctx_len)
+    m.decode_device(3)
+    ms = timed_decode(m, ctx, st, torch, steps)
+    ids.free()
+    mean_ctx = ctx_len + 3 + (steps - 1) / 2.0
+    ach = decode_bytes(cfg, mean_ctx) / (ms / steps / 1000.0) / 1e9
+    return {"tok_s": steps / (ms / 1000.0), "ms_per_step": ms / steps,
+            "decode_context": [ctx_len + 3, ctx_len + 3 + steps],
+            "step_roofline": {"bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s", "frac": ach / hbm}}
+
+
+def c1_linear(ctx, st, torch, hbm, tflops):
+    """one quantized linear, N=6144, K=2048, int4 gs64,
+    through emx_quantized_matmul: M=1 (GB/s over 24 weight copies, > L2) and
+    M=512 (TFLOP/s)."""
+    import numpy as np
+
+    import emx
+
+    N, K, gs, bits = 6144, 2048, 64, 4
+    copies = 24
+    wsz, ssz = N * K * bits // 8, N * (K // gs) * 2
+    rng = np.random.default_rng(7)
+    res = {}
+    ws = []
+    for _ in range(copies):
+        w, s, b = ctx.alloc(wsz), ctx.alloc(ssz), ctx.alloc(ssz)
+        emx.lib().emx_memset(ctx.h, w.ptr, int(rng.integers(1, 255)), wsz)
+        emx.lib().emx_memset(ctx.h, s.ptr, 0x3C, ssz)
+        emx.lib().emx_memset(ctx.h, b.ptr, 0x00, ssz)
+        ws.append((w, s, b))
+    for M in (1, 512):
+        x, y = ctx.alloc(M * K * 2), ctx.alloc(M * N * 2)
+        emx.lib().emx_memset(ctx.h, x.ptr, 0x3C, M * K * 2)
+        for i in range(4):
+            w, s, b = ws[i % copies]
+            ctx.quantized_matmul(x, w, s, b, M, N, K, gs, bits, out=y)
+        ctx.synchronize()
+        n = 96 if M == 1 else 24
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for i in range(n):
+            w, s, b = ws[i % copies]
+            ctx.quantized_matmul(x, w, s, b, M, N, K, gs, bits, out=y)
+        e1.record(st)
+        e1.synchronize()
+        us = e0.elapsed_time(e1) * 1000.0 / n
+        if M == 1:
+            per = qbytes(N, K, bits, gs) + K * 2 + N * 2
+            ach = per / (us * 1e-6) / 1e9
+            res["m1"] = {"us_per_call": us, "bytes_per_call": per, "achieved": ach, "unit": "GB/s", "peak": hbm,
+                         "frac": ach / hbm, "bound": "hbm"}
+        else:
+            ach = 2.0 * M * N * K / (us * 1e-6) / 1e12
+            res["m512"] = {"us_per_call": us, "achieved": ach, "unit": "TFLOP/s", "peak": tflops,
+                           "frac": ach / tflops, "bound": "tensor"}
+        x.free()
+        y.free()
+    for w, s, b in ws:
+        w.free()
+        s.free()
+        b.free()
+    res["shape"] = {"N": N, "K": K, "bits": bits, "group_size": gs, "api": "emx_quantized_matmul"}
+    return res
+
+
+def sharded_c5(args, rank, world, dist, torch, hbm, steps=32, prompt=128):
+    """The 32B-shape dense model split tensor-parallel
+    across the job's GPUs (one GPU: the whole model), decode after a prompt:
+    tok/s from CUDA events, max over ranks, and the per-GPU step roofline.
+    Every rank takes part."""
+    import dataclasses
+
+    import numpy as np
+
+    import emx
+
+    cfg = dataclasses.replace(emx.CONFIGS["c5"], kv_cap=prompt + steps + 64, max_prefill=prompt)
+    dev = int(os.environ.get("LOCAL_RANK", "0"))
+    ctx = emx.Ctx(dev)
+    sp = emx.C.c_void_p()
+    emx.lib().emx_ctx_stream(ctx.h, emx.C.byref(sp))
+    st = torch.cuda.ExternalStream(sp.value, device=dev)
+    comm = None
+    if world > 1:
+        obj = [emx.Comm.unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        comm = emx.Comm(ctx, obj[0], world, rank)
+    m = emx.Qwen3(ctx, cfg, comm)
+    m.init_random(args.seed)
+    ids = ctx.put(np.random.default_rng(args.seed).integers(0, cfg.vocab, prompt).astype(np.int32))
+    m.prefill_device(ids, prompt)
+    m.decode_device(3)
+    barrier = dist.barrier if dist is not None else None
+    ms = timed_decode(m, ctx, st, torch, steps, barrier)
+    if dist is not None:
+        t = torch.tensor([ms], device=f"cuda:{dev}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    launches = m.step_launches()
+    ids.free()
+    m.close()
+    if comm is not None:
+        comm.close()
+    ctx.close()
+    mean_ctx = prompt + 3 + (steps - 1) / 2.0
+    per_gpu = decode_bytes(cfg, mean_ctx) / world
+    ach = per_gpu / (ms / steps / 1000.0) / 1e9
+    return {"model": "c5 (Qwen3-32B shape, int4 gs64, random-init)", "parallelism": f"tensor parallel x{world}",
+            "tok_s": steps / (ms / 1000.0), "ms_per_step": ms / steps, "steps": steps, "prompt": prompt,
+            "launches_per_step": launches,
+            "step_roofline": {"bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s", "frac": ach / hbm,
+                              "scope": "per GPU: 1/world of the weights + this rank's KV heads",
+                              "bytes_per_step": per_gpu}}
 
 
 def run_engine(args, cfg, rank, world, dist):
@@ -215,6 +400,8 @@ def run_engine(args, cfg, rank, world, dist):
                 r = gemm_kernel_roofline(ctx, st, cfg, torch, tf)
             elif args.kernel_only == "attn":
                 r = attn_kernel_roofline(ctx, st, cfg, torch, hbm)
+            elif args.kernel_only == "c1":
+                r = c1_linear(ctx, st, torch, hbm, tf)
             else:
                 r = gemv_kernel_roofline(ctx, st, cfg, torch, hbm)
             print(json.dumps(dict(r, peak_kind=kind)), flush=True)
@@ -270,14 +457,7 @@ def run_engine(args, cfg, rank, world, dist):
     launches = m.step_launches()
     barrier()
     with ClockSampler(dev) as clk:
-        ctx.synchronize()
-        barrier()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(st)
-        m.decode_device(args.steps)
-        e1.record(st)
-        e1.synchronize()
-        ms = e0.elapsed_time(e1)
+        ms = timed_decode(m, ctx, st, torch, args.steps, barrier)
         barrier()
     start_ctx = args.prompt + max(args.warmup, 3)
     ms_max = ms
@@ -297,60 +477,101 @@ def run_engine(args, cfg, rank, world, dist):
     for _ in range(n_e2e):
         tok = m.decode_step(tok)
     e2e_s = time.perf_counter() - t0
+    # the same through the per-token streaming entry point (steps in flight)
+    m.reset()
+    tok = m.prefill(prompt)
+    barrier()
+    t0 = time.perf_counter()
+    n_str = m.decode_stream(tok, n_e2e, lambda t, i: False)
+    str_s = time.perf_counter() - t0
     e2e = n_e2e / e2e_s
+    e2e_str = n_str / str_s
     if dist is not None:
-        t = torch.tensor([e2e_s], device=f"cuda:{dev}")
+        t = torch.tensor([e2e_s, str_s], device=f"cuda:{dev}")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e = streams * n_e2e / float(t.item())
+        e2e = streams * n_e2e / float(t[0].item())
+        e2e_str = streams * n_str / float(t[1].item())
     # ---- roofline of the decode step (all GEMVs + attention + lm_head)
-    hbm, _, kind = peaks()
+    hbm, tf, kind = peaks()
     mean_ctx = start_ctx + (args.steps - 1) / 2.0
     step_bytes = decode_bytes(cfg, mean_ctx) / (world if sharded else 1)  # per GPU
     achieved = step_bytes / (ms_max / args.steps / 1000.0) / 1e9
-    # ---- the dominant kernel alone: the gate_up GEMV shape over rotating copies (> L2)
-    kern = gemv_kernel_roofline(ctx, st, cfg, torch, hbm)
     fused = m.fused
+    extras = {}
+    if rank == 0 and not sharded:
+        for L in (2048, 8192):
+            r = decode_at_context(ctx, st, torch, cfg, m, hbm, args.seed, L)
+            if r:
+                extras[str(L)] = r
     m.close()
     if comm is not None:
         comm.close()
+    kern = c1 = None
+    if rank == 0:
+        kern = gemv_kernel_roofline(ctx, st, cfg, torch, hbm)
+        c1 = c1_linear(ctx, st, torch, hbm, tf)
+    ctx.close()
+    barrier()
+    sh = None
+    if not args.shard and not args.no_sharded:
+        sh = sharded_c5(args, rank, world, dist, torch, hbm)
     if rank != 0:
-        ctx.close()
         return
+    if fused:
+        tag = f"step_kernel_{args.config}"
+        kname = "step_kernel (the whole decode step: one persistent launch per token)"
+    else:
+        tag = f"decode_chain_{args.config}"
+        kname = "decode kernel chain (one CUDA graph per token)"
+    traffic = profiled_traffic(tag)
     line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": max(args.warmup, 3), "ms_per_step": ms_max / args.steps, "higher_is_better": True,
-            "scaling": "strong" if sharded else "weak", "vs_baseline": None, "dtype": "bf16 activations, int4/int8 affine weights",
+            "scaling": "strong" if sharded else "weak", "vs_baseline": None,
+            "dtype": "bf16 activations, int4/int8 affine weights",
             "data": "synthetic (seeded random-init weights and token ids)", "config": workload(args, cfg),
+            "decode_path": ("one persistent kernel per decode step" if fused
+                            else "one kernel per operation, CUDA graph"),
             "prefill_tok_s": pre, "decode_context": [start_ctx, start_ctx + args.steps],
-            "roofline": dict(kern, peak_kind=kind),
+            "roofline": {"kernel": kname, "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                         "frac": achieved / hbm, "traffic": traffic, "peak_kind": kind,
+                         "bytes_per_launch": step_bytes,
+                         "traffic_source": f"profiles/{tag}.md" if traffic else None,
+                         "scope": "algorithmic bytes of one decode step (weights + scales/biases + KV rows read + "
+                                  "norms) / its CUDA-event time"},
             "step_roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
-                              "frac": achieved / hbm, "traffic": None, "peak_kind": kind,
+                              "frac": achieved / hbm, "traffic": traffic, "peak_kind": kind,
                               "scope": "whole decode step (weights + scales/biases + KV read per token)",
                               "bytes_per_step": step_bytes},
+            "decode_long_context": extras,
+            "gemv_kernel": dict(kern, peak_kind=kind) if kern else None,
+            "c1_single_linear": c1,
             "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4,
                     "api": "emx_qwen3_decode_step", "steps": n_e2e},
+            "e2e_stream": {"value": e2e_str, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 8,
+                           "api": "emx_qwen3_decode_stream (per-token callback, steps in flight)",
+                           "steps": n_str},
             "gpu_launches": launches * args.steps, "launches_per_step": launches,
             "clocks": clk.summary()}
+    if sh:
+        line["sharded"] = sh
     if sharded:
-        line["config"]["parallelism"] = (f"expert parallel x{world}" if cfg.n_experts else f"tensor parallel x{world}")
         line["step_roofline"]["scope"] += ", per GPU (1/world of the weights)"
-    line["config"]["decode_path"] = ("one persistent kernel per decode step" if fused
-                                     else "one kernel per operation, CUDA graph")
     if world == 1 and not args.no_cpu_baseline:
-        v, cores = cpu_baseline(cfg, args.seed, args.cpu_steps)
-        line["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": cores, "kind": "port",
-                                "sample": f"{args.config}: 16-token prompt then {args.cpu_steps} greedy decode "
-                                          "steps on the CPU oracle (OpenMP)"}
+        v, cores, pre_s = cpu_baseline(cfg, args.seed, args.prompt, args.cpu_steps)
+        line["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": cores, "kind": "port", "cpu_model": cpu_model(),
+                                "prefill_s": pre_s,
+                                "sample": f"{args.config}: {args.prompt}-token prompt then {args.cpu_steps} greedy "
+                                          f"decode steps on the CPU oracle (OpenMP, {cores} threads, {cpu_model()})"}
     print(json.dumps(line), flush=True)
-    ctx.close()
 
 
 def gemv_kernel_roofline(ctx, st, cfg, torch, hbm):
-    """The dominant kernel of the decode step, pgemv_kernel (the packed batch-1
-    GEMV: ~80% of the step), alone on the step's most expensive shape, the
-    fused gate|up projection [2*inter, hidden]: 16 packed copies (> L2)
-    rotated over 160 launches, CUDA events on the context's stream.
-    Algorithmic bytes per launch: packed codes + bf16 scales and biases + x in
-    + y out."""
+    """The packed batch-1 GEMV (pgemv_kernel, the per-kernel decode chain's
+    GEMV; the persistent step runs the same inner loop) alone on the step's
+    most expensive shape, the fused gate|up projection [2*inter, hidden]: 16
+    packed copies (> L2) rotated over 160 launches, CUDA events on the
+    context's stream.  Algorithmic bytes per launch: packed codes + bf16
+    scales and biases + x in + y out."""
     import numpy as np
 
     import emx
@@ -486,8 +707,10 @@ def main():
                          "parallel for MoE; NCCL all-reduce) instead of N replicas")
     ap.add_argument("--per-op", action="store_true",
                     help="decode with one kernel per operation instead of the persistent step kernel")
+    ap.add_argument("--no-sharded", action="store_true",
+                    help="skip the tensor-parallel 32B-shape measurement added to every line")
     ap.add_argument("--kernel-only", nargs="?", const="gemv", default=None,
-                    choices=["gemv", "gemm", "attn", "prefill"],
+                    choices=["gemv", "gemm", "attn", "prefill", "c1"],
                     help="time one kernel alone and print its roofline: the packed decode GEMV (gate|up shape, "
                          "default), the prefill GEMM (gate|up shape, 2048 rows), decode attention (8192 rows), "
                          "or one whole prefill of --prompt tokens")
