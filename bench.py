@@ -375,6 +375,10 @@ def run_engine(args, cfg, rank, world, dist):
     st = torch.cuda.ExternalStream(stream_ptr.value, device=dev)
     if args.kernel_only == "prefill":
         # one warm prefill, then one timed: the launch list of a whole prefill
+        # (the KV cache sized to the prompt)
+        import dataclasses
+
+        cfg = dataclasses.replace(cfg, kv_cap=args.prompt + 64, max_prefill=max(args.prompt, 128))
         m = emx.Qwen3(ctx, cfg)
         m.init_random(args.seed)
         ids = ctx.put(np.random.default_rng(args.seed).integers(0, cfg.vocab, args.prompt).astype(np.int32))
@@ -389,6 +393,28 @@ def run_engine(args, cfg, rank, world, dist):
         ms = e0.elapsed_time(e1)
         if rank == 0:
             print(json.dumps({"prefill_tokens": args.prompt, "ms": ms, "tok_s": args.prompt / (ms / 1000.0)}),
+                  flush=True)
+        m.close()
+        ctx.close()
+        return
+    if args.kernel_only == "step":
+        # the decode step kernel alone: prefill --prompt tokens, --warmup
+        # steps, then --steps timed steps (a short command for the profiler;
+        # the KV cache sized to the run, so the device holds little besides
+        # the weights)
+        import dataclasses
+
+        cfg = dataclasses.replace(cfg, kv_cap=args.prompt + args.steps + max(args.warmup, 3) + 64,
+                                  max_prefill=max(args.prompt, 128))
+        m = emx.Qwen3(ctx, cfg)
+        m.init_random(args.seed)
+        ids = ctx.put(np.random.default_rng(args.seed).integers(0, cfg.vocab, args.prompt).astype(np.int32))
+        m.prefill_device(ids, args.prompt)
+        m.decode_device(max(args.warmup, 3))
+        ms = timed_decode(m, ctx, st, torch, args.steps)
+        if rank == 0:
+            print(json.dumps({"decode_steps": args.steps, "ms_per_step": ms / args.steps,
+                              "tok_s": args.steps / (ms / 1000.0), "launches_per_step": m.step_launches()}),
                   flush=True)
         m.close()
         ctx.close()
@@ -605,7 +631,8 @@ def gemv_kernel_roofline(ctx, st, cfg, torch, hbm):
     ach = per / (us * 1e-6) / 1e9
     return {"kernel": f"pgemv_kernel<{bits},{gs}> (gate|up shape, standalone: no PDL overlap with a neighbour)",
             "shape": [N, K], "bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s", "frac": ach / hbm,
-            "us_per_launch": us, "bytes_per_launch": per, "traffic": None}
+            "us_per_launch": us, "bytes_per_launch": per, "traffic": profiled_traffic("pgemv_gate_up_c3"),
+            "traffic_source": "profiles/pgemv_gate_up_c3.md"}
 
 
 def gemm_kernel_roofline(ctx, st, cfg, torch, tflops, M=2048):
@@ -710,10 +737,10 @@ def main():
     ap.add_argument("--no-sharded", action="store_true",
                     help="skip the tensor-parallel 32B-shape measurement added to every line")
     ap.add_argument("--kernel-only", nargs="?", const="gemv", default=None,
-                    choices=["gemv", "gemm", "attn", "prefill", "c1"],
+                    choices=["gemv", "gemm", "attn", "prefill", "c1", "step"],
                     help="time one kernel alone and print its roofline: the packed decode GEMV (gate|up shape, "
                          "default), the prefill GEMM (gate|up shape, 2048 rows), decode attention (8192 rows), "
-                         "or one whole prefill of --prompt tokens")
+                         "one whole prefill of --prompt tokens, or --steps decode steps (step)")
     args = ap.parse_args()
 
     import emx
