@@ -14,6 +14,7 @@
 #include "attn_prefill.cuh"
 #include "misc.cuh"
 #include "qgemm.cuh"
+#include "tc_gemm.cuh"
 #include "qgemv.cuh"
 
 namespace {
@@ -370,6 +371,33 @@ int emx_quantized_matvec_packed(emx_ctx* c, const void* x, const void* packed, v
   a.y = static_cast<bf16*>(y);
   a.status = c->status;
   EMX_CHECK_CUDA(pgemv_launch(a, plan, c->stream, false), "emx_quantized_matvec_packed");
+  return EMX_OK;
+}
+
+int emx_quantized_matmul_packed(emx_ctx* c, const void* x, const void* packed, void* y, int M, int N, int K, int gs,
+                                int bits) {
+  EMX_REQUIRE(c && x && packed && y, "emx_quantized_matmul_packed: null argument");
+  EMX_REQUIRE(M >= 1, "emx_quantized_matmul_packed: M=%d must be >= 1", M);
+  if (M == 1) return emx_quantized_matvec_packed(c, x, packed, y, N, K, gs, bits);
+  int rc = check_quant(N, K, gs, bits, "emx_quantized_matmul_packed");
+  if (rc) return rc;
+  EMX_REQUIRE(gs == 64, "emx_quantized_matmul_packed: M > 1 needs group size 64 (got %d)", gs);
+  EMX_REQUIRE(N % 16 == 0, "emx_quantized_matmul_packed: N=%d must be a multiple of 16", N);
+  EMX_REQUIRE(aligned16(packed) && aligned16(x), "emx_quantized_matmul_packed: x / packed must be 16-byte aligned");
+  TcGemmArgs t = {};
+  t.x = static_cast<const bf16*>(x);
+  t.M = M;
+  t.N = N;
+  t.K = K;
+  t.epi = kTcStore;
+  t.y = static_cast<bf16*>(y);
+  t.status = c->status;
+  t.bits = bits;
+  t.wp = static_cast<const unsigned char*>(packed);
+  t.S = (K / 64 + 7) / 8;
+  t.nrb = N / 16;
+  EMX_REQUIRE(tc_pgemm_supported(t), "emx_quantized_matmul_packed: unsupported shape M=%d N=%d K=%d", M, N, K);
+  EMX_CHECK_CUDA(tc_pgemm_launch(t, c->num_sms, c->stream), "emx_quantized_matmul_packed");
   return EMX_OK;
 }
 

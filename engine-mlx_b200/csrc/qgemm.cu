@@ -4,9 +4,10 @@
 // forward_qwen3.rs:66-162 calls it over the whole prompt).
 //
 // Short prompts with group size 64 (every BASELINE config): the tcgen05 GEMM
-// dequantises each k-block of its weight tile into shared memory (tc_qgemm in
-// tc_gemm.cu), K split across CTAs.  Otherwise W is dequantised bit-exactly
-// into a bf16 scratch buffer (the whole matrix, up to 1 GiB) and the tcgen05
+// dequantises each k-block of its weight tile into shared memory, K split
+// across the CTAs of a cluster — over the packed decode layout when the
+// caller has it (tc_pgemm), else over the MLX layout (tc_qgemm).  Otherwise W is
+// dequantised bit-exactly into a bf16 scratch buffer (the whole matrix, up to 1 GiB) and the tcgen05
 // GEMM multiplies.  Either way the residual add, SwiGLU or fp32 output is
 // fused into the epilogue.
 #include "qgemm.cuh"
@@ -19,8 +20,6 @@ namespace emx {
 struct GemmCtx {
   void* scratch = nullptr;  // dequantized weight
   size_t scratch_bytes = 0;
-  void* part = nullptr;  // split-K partials of the in-kernel dequant GEMM
-  size_t part_bytes = 0;
   int num_sms = 148;
 };
 
@@ -53,7 +52,6 @@ GemmCtx* gemm_ctx_create(size_t scratch_bytes) {
 void gemm_ctx_destroy(GemmCtx* c) {
   if (!c) return;
   if (c->scratch) cudaFree(c->scratch);
-  if (c->part) cudaFree(c->part);
   delete c;
 }
 
@@ -77,17 +75,18 @@ int gemm_run(GemmCtx* c, const GemmArgs& a, cudaStream_t st) {
   t.ws = a.s;
   t.wb = a.b;
   t.bits = a.bits;
-  if (a.gs == 64 && a.M <= 128 && tc_qgemm_supported(t)) {
-    size_t part = 0;
-    const int ks = tc_qgemm_splits(t, c->num_sms, &part);
-    if (ks > 1) {
-      int e = grow(&c->part, &c->part_bytes, part);
-      if (e) return e;
-      t.part = static_cast<float*>(c->part);
-      t.ksplit = ks;
-      const cudaError_t ce = tc_qgemm_launch(t, c->num_sms, st);
+  if (a.wp && a.gs == 64 && a.M <= 128) {
+    t.wp = a.wp;
+    t.S = (a.K / 64 + 7) / 8;
+    t.nrb = (a.N + 15) / 16;
+    if (tc_pgemm_supported(t)) {
+      const cudaError_t ce = tc_pgemm_launch(t, c->num_sms, st);
       return ce == cudaSuccess ? 0 : (int)ce;
     }
+  }
+  if (a.gs == 64 && a.M <= 128 && tc_qgemm_supported(t)) {
+    const cudaError_t ce = tc_qgemm_launch(t, c->num_sms, st);
+    return ce == cudaSuccess ? 0 : (int)ce;
   }
   const size_t need = (size_t)a.N * a.K * 2;
   if (need > ((size_t)1 << 30)) return -2;  // larger than any weight of the supported configs

@@ -21,6 +21,9 @@ struct GemmArgs {
   bf16* y;         // [M, N] (or [M, N/2] for SwiGLU)
   const bf16* res; // [M, N] for kGemmResid (may alias y)
   float* yf;       // [M, N] for kGemmF32
+  // optional: the same weights in the packed decode-GEMV layout (a dense
+  // matrix; gate|up interleaved per 16 rows for SwiGLU); read instead of w/s/b
+  const unsigned char* wp;
 };
 
 struct GemmCtx;  // per-context scratch + library handles

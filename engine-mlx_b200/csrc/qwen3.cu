@@ -963,6 +963,7 @@ int gemm(emx_qwen3* m, const QW& q, const bf16* x, int T, int epi, bf16* y, cons
   g.epi = epi;
   g.y = y;
   g.res = res;
+  if (q.map.blocks == 1) g.wp = q.pk;
   int rc = gemm_run(m->ctx->gemm, g, m->ctx->stream);
   if (rc) return fail(EMX_ERR_CUDA, "prefill gemm failed (%d)", rc);
   return EMX_OK;

@@ -32,8 +32,10 @@ struct TcGemmArgs {
   const bf16* ws;      // [N_w, K/64] scales
   const bf16* wb;      // [N_w, K/64] biases
   int bits;            // 4 or 8
-  float* part;         // split-K workspace (tc_qgemm_splits bytes) or nullptr
-  int ksplit;          // splits of K when part is set
+  // tc_pgemm: the weights in the packed decode-GEMV layout (group size 64)
+  const unsigned char* wp;  // packed tiles [row block][span]
+  int S;                    // spans (8 groups each) per row block
+  int nrb;                  // packed 16-row blocks (SwiGLU: gate and up blocks alternate)
 };
 
 // True when the shape is supported (K % 64 == 0, N % 32 == 0, 16-byte
@@ -46,11 +48,15 @@ cudaError_t tc_gemm_launch(const TcGemmArgs& a, int num_sms, cudaStream_t st);
 // dequantises each k-block of its weight tile into shared memory, bit-exactly
 // as the dequant pass would, so no bf16 copy of W is written.
 bool tc_qgemm_supported(const TcGemmArgs& a);
-// Splits of K that fill the machine when the output has fewer tiles than SMs
-// (1 otherwise) and the workspace they need; with part / ksplit set, the
-// launch writes fp32 partials and a second kernel sums them in split order
-// and applies the output step.
-int tc_qgemm_splits(const TcGemmArgs& a, int num_sms, size_t* part_bytes);
+// When the output has fewer tiles than SMs, K is split across the CTAs of a
+// thread-block cluster and the partials are summed (in split order) inside
+// the cluster; one launch either way.
 cudaError_t tc_qgemm_launch(const TcGemmArgs& a, int num_sms, cudaStream_t st);
+
+// The same GEMM over the packed decode-GEMV layout (wp, S, nrb): the prefill
+// reads the bytes the decode step reads.  SwiGLU output column n of logical
+// block n / 16 pairs gate row block 2 (n / 16) with up row block 2 (n / 16) + 1.
+bool tc_pgemm_supported(const TcGemmArgs& a);
+cudaError_t tc_pgemm_launch(const TcGemmArgs& a, int num_sms, cudaStream_t st);
 
 }  // namespace emx

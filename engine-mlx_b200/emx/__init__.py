@@ -70,6 +70,7 @@ _SIGS = {
     "emx_qpack_bytes": (C.c_int, [C.c_int] * 4 + [C.POINTER(C.c_size_t)]),
     "emx_qpack": (C.c_int, [C.c_void_p] * 5 + [C.c_int] * 4),
     "emx_quantized_matvec_packed": (C.c_int, [C.c_void_p] * 4 + [C.c_int] * 4),
+    "emx_quantized_matmul_packed": (C.c_int, [C.c_void_p] * 4 + [C.c_int] * 5),
     "emx_sdpa_decode": (C.c_int, [C.c_void_p] + [C.c_void_p] * 4 + [C.c_int] * 5 + [C.c_float]),
     "emx_sdpa_decode_noalloc": (C.c_int, [C.c_void_p] + [C.c_void_p] * 4 + [C.c_int] * 5 + [C.c_float]),
     "emx_silu": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t]),
@@ -271,6 +272,12 @@ class Ctx:
         y = self.alloc(N * 2)
         _check(lib().emx_quantized_matvec_packed(self.h, x.ptr, packed.ptr, y.ptr, N, K, group_size, bits))
         return y
+
+    def quantized_matmul_packed(self, x, packed, M, N, K, group_size, bits, out=None):
+        """y[M, N] = x[M, K] . dequant(w)^T over the packed layout (qpack)."""
+        out = out or self.alloc(M * N * 2)
+        _check(lib().emx_quantized_matmul_packed(self.h, x.ptr, packed.ptr, out.ptr, M, N, K, group_size, bits))
+        return out
 
     def dequantize(self, w, s, b, N, K, group_size, bits):
         out = self.alloc(N * K * 2)

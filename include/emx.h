@@ -103,6 +103,12 @@ int emx_qpack(emx_ctx* ctx, const void* w, const void* scales, const void* biase
  * tensor: y[N] = x[K] . dequant(w)^T, the decode GEMV the engine runs. */
 int emx_quantized_matvec_packed(emx_ctx* ctx, const void* x, const void* packed, void* y, int N, int K,
                                 int group_size, int bits);
+/* MlxCtx::quantized_matmul (transform.rs:77-89) over a packed tensor at any
+ * M: y[M,N] = x[M,K] . dequant(w)^T.  M == 1 is the decode GEMV above; M > 1
+ * is the prefill GEMM the engine runs over the same packed bytes (group size
+ * 64 only). */
+int emx_quantized_matmul_packed(emx_ctx* ctx, const void* x, const void* packed, void* y, int M, int N, int K,
+                                int group_size, int bits);
 /* MlxCtx::dequantize_weight (transform.rs:45-60): out bf16[N,K]. */
 int emx_dequantize(emx_ctx* ctx, const void* w, const void* scales, const void* biases, void* out, int N, int K,
                    int group_size, int bits);

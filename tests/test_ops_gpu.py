@@ -92,7 +92,38 @@ def _linear(seed, name, N, K, gs, bits):
     return oracle.gen_tensor(seed, name, N, K, bits, gs)
 
 
-@pytest.mark.parametrize("M", [1, 512])
+# Prefill shapes of the in-kernel-dequant GEMM (K split across a cluster):
+# the C3 gate|up, down (int4) and q|k|v, o (int8) projections at up to 128
+# rows, ragged row counts included.
+PREFILL_LINEARS = [(128, 6144, 2048, 4), (100, 2048, 6144, 4), (77, 4096, 2048, 8), (128, 2048, 2048, 8),
+                   (16, 12288, 2048, 4), (3, 512, 1024, 8)]
+
+
+@pytest.mark.parametrize("M,N,K,bits", PREFILL_LINEARS)
+def test_prefill_linear_shapes(ctx, M, N, K, bits):
+    q = _linear(11, f"prefill.{N}x{K}.{bits}", N, K, 64, bits)
+    rng = np.random.default_rng(M + N)
+    x = oracle.to_bf16(rng.standard_normal((M, K)).astype(np.float32))
+    ref = oracle.qmatmul(x, q["weight"], q["scales"], q["biases"], 64, bits)
+    y = ctx.quantized_matmul(ctx.put(x), ctx.put(q["weight"]), ctx.put(q["scales"]), ctx.put(q["biases"]), M, N, K,
+                             64, bits)
+    assert_close(y.read(np.uint16, (M, N)), ref, what=f"prefill linear {M}x{N}x{K} int{bits}")
+
+
+@pytest.mark.parametrize("M,N,K,bits", PREFILL_LINEARS + [(200, 1024, 2048, 4), (1, 2048, 2048, 8)])
+def test_prefill_linear_packed(ctx, M, N, K, bits):
+    """The prefill GEMM over the packed decode layout (emx_qpack) against the
+    oracle's MLX-layout matmul of the same tensor."""
+    q = _linear(11, f"prefill.{N}x{K}.{bits}", N, K, 64, bits)
+    rng = np.random.default_rng(M + N)
+    x = oracle.to_bf16(rng.standard_normal((M, K)).astype(np.float32))
+    ref = oracle.qmatmul(x, q["weight"], q["scales"], q["biases"], 64, bits)
+    pk = ctx.qpack(ctx.put(q["weight"]), ctx.put(q["scales"]), ctx.put(q["biases"]), N, K, 64, bits)
+    y = ctx.quantized_matmul_packed(ctx.put(x), pk, M, N, K, 64, bits)
+    assert_close(y.read(np.uint16, (M, N)), ref, what=f"packed prefill linear {M}x{N}x{K} int{bits}")
+
+
+@pytest.mark.parametrize("M", [1, 128, 512])
 def test_config1_single_linear(ctx, M):
     """x bf16 [M, 2048] ~N(0,1); W [6144, 2048] ~N(0, 0.02^2) int4 gs64."""
     N, K = 6144, 2048
