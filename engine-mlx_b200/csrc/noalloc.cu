@@ -29,10 +29,11 @@
 //     the process: calls that can overlap in time (two streams, two contexts
 //     on one device, two host threads) race on it.  Calls on one stream are
 //     ordered and safe;
-//   * the first call on a device looks the array's address up with
-//     cudaGetSymbolAddress, which may load the module; make that first call
-//     before any stream capture begins.  Later calls only read the cached
-//     address.
+//   * a call outside a stream capture looks the array's address up with
+//     cudaGetSymbolAddress (the first may load the module; after a
+//     cudaDeviceReset the next uncaptured call finds the reloaded array); a
+//     call inside a capture reuses the last address, so make one call before
+//     a capture begins and none across a device reset within a capture.
 #include <mutex>
 
 #include "attn_decode.cuh"
@@ -50,10 +51,18 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratch
 std::mutex g_addr_mu;
 void* g_addr[kMaxDevices] = {};
 
-// Device address of g_noalloc_scratch on `device` (looked up once).
-int scratch_address(int device, void** out) {
+// Device address of g_noalloc_scratch on `device`.  Looked up again on
+// every call made outside a stream capture (cheap once the module is loaded,
+// and right after a cudaDeviceReset reloaded it); inside a capture the
+// cached address is used.
+int scratch_address(int device, cudaStream_t st, void** out) {
   std::lock_guard<std::mutex> lk(g_addr_mu);
-  if (!g_addr[device]) {
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(st, &cap) != cudaSuccess) {
+    cudaGetLastError();
+    cap = cudaStreamCaptureStatusActive;  // unknown: do not touch the module
+  }
+  if (!g_addr[device] || cap == cudaStreamCaptureStatusNone) {
     int prev = 0;
     EMX_CHECK_CUDA(cudaGetDevice(&prev), "emx_sdpa_decode_noalloc setup");
     EMX_CHECK_CUDA(cudaSetDevice(device), "emx_sdpa_decode_noalloc setup");
@@ -95,7 +104,7 @@ extern "C" int emx_sdpa_decode_noalloc(emx_ctx* c, const void* q, const void* kc
              "emx_sdpa_decode_noalloc: n_q %d x %d splits needs %zu bytes of partials; the static scratch holds %zu",
              nq, splits, part, kNoAllocScratchBytes - kTicketBytes);
   void* base = nullptr;
-  int rc = scratch_address(c->device, &base);
+  int rc = scratch_address(c->device, c->stream, &base);
   if (rc) return rc;
   AttnDecodeArgs a = {};
   a.q_in = static_cast<const bf16*>(q);

@@ -141,9 +141,11 @@ int emx_sdpa_decode(emx_ctx* ctx, const void* q, const void* k_cache, const void
  * merge tickets live in one static 1 MiB device array (n_kv <= 64 and
  * n_q * splits * (head_dim + 2) * 4 bytes <= 1 MiB - 256, else
  * EMX_ERR_INVALID).  The array is shared per device, so calls that overlap
- * in time race; calls on one stream are safe.  The first call on a device
- * looks the array up (cudaGetSymbolAddress) and should come before any
- * stream capture begins. */
+ * in time race; calls on one stream are safe.  A call outside a stream
+ * capture looks the array up (cudaGetSymbolAddress; the first may load the
+ * module, and after a cudaDeviceReset it finds the reloaded array); a call
+ * inside a capture reuses the last address, so one call should precede any
+ * capture. */
 int emx_sdpa_decode_noalloc(emx_ctx* ctx, const void* q, const void* k_cache, const void* v_cache, void* out, int nq,
                             int nkv, int cap, int head_dim, int length, float scale);
 /* MlxCtx::silu / multiply / add (blas.rs:17-37), bf16 elementwise. */

@@ -1,9 +1,13 @@
 """Tensor- and expert-parallel decode on two GPUs against the unsharded oracle.
 
 The dense model is split by tensor parallelism (q/k/v and gate/up rows by
-heads / intermediate, o/down columns; fp32 partials summed by an NCCL
-all-reduce after o and down), the MoE model by expert parallelism (experts
-split across ranks, partial expert sums all-reduced).  Each rank is its own
+heads / intermediate, o/down columns); the fp32 partials after o and down
+are summed through NVLink peer memory inside the GEMVs (each rank stores its
+rows into every rank's exchange region and the consuming prologue adds the
+ranks' slots in rank order), with an NCCL all-reduce only as the fallback
+when the regions cannot be mapped.  The MoE model is split by expert
+parallelism (experts across ranks), its weighted expert sums exchanged the
+same way.  Each rank is its own
 process with its own context on its own GPU; both generate their shard of the
 same seeded weights.  Rank 0's logits must meet the single-GPU bars against
 the oracle of the whole model, and both ranks must produce the same greedy
