@@ -380,6 +380,11 @@ __global__ void moe_route_kernel(const bf16* logits, int E, int k, int normalize
   __shared__ float red[32];
   pdl_trigger();
   pdl_wait();
+  // one token per CTA: row blockIdx.x of logits [T][E], idx / w [T][k], n [T]
+  logits += (size_t)blockIdx.x * E;
+  idx += (size_t)blockIdx.x * k;
+  w += (size_t)blockIdx.x * k;
+  n += blockIdx.x;
   float m = -INFINITY;
   for (int i = threadIdx.x; i < E; i += blockDim.x) m = fmaxf(m, bf2f(logits[i]));
   m = warp_max(m);
@@ -424,6 +429,80 @@ __global__ void moe_route_kernel(const bf16* logits, int E, int k, int normalize
       }
     }
     *n = j;
+  }
+}
+
+// Batched MoE prefill, grouping: the (token, slot) pairs of each local
+// expert get consecutive positions, experts in order and, inside an expert,
+// tokens in order (deterministic); perm [T][k] holds each pair's position,
+// src [P] its token; tile list entries (expert, first position, end
+// position) cover every expert's positions in runs of `tile` rows.  One
+// thread per local expert (E_l <= 1024), one CTA.
+__global__ void moe_group_kernel(const int* idx, const int* n, int T, int k, int E_l, int tile, int* perm, int* src,
+                                 int4* tiles, int* n_tiles, int* n_pairs) {
+  __shared__ int cnt[1024];
+  __shared__ int off[1024];
+  __shared__ int toff[1024];
+  const int e = threadIdx.x;
+  int c = 0;
+  if (e < E_l)
+    for (int t = 0; t < T; ++t) {
+      const int nt = n[t];
+      for (int j = 0; j < nt; ++j) c += idx[t * k + j] == e;
+    }
+  if (e < 1024) cnt[e] = e < E_l ? c : 0;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int o = 0, to = 0;
+    for (int i = 0; i < E_l; ++i) {
+      off[i] = o;
+      toff[i] = to;
+      o += cnt[i];
+      to += (cnt[i] + tile - 1) / tile;
+    }
+    *n_tiles = to;
+    *n_pairs = o;
+  }
+  __syncthreads();
+  if (e < E_l) {
+    int pos = off[e];
+    for (int t = 0; t < T; ++t) {
+      const int nt = n[t];
+      for (int j = 0; j < nt; ++j)
+        if (idx[t * k + j] == e) {
+          perm[t * k + j] = pos;
+          src[pos] = t;
+          ++pos;
+        }
+    }
+    const int end = off[e] + cnt[e];
+    for (int i = 0, p0 = off[e]; p0 < end; ++i, p0 += tile) tiles[toff[e] + i] = make_int4(e, p0, end, 0);
+  }
+}
+
+// xs[p] = x[src[p]] for the *P grouped positions (rows of H bf16; the grid
+// covers Pmax positions).
+__global__ void moe_gather_kernel(const bf16* x, const int* src, const int* P_dev, int H, bf16* xs) {
+  const int per = H / 8;
+  const int P = *P_dev;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < (size_t)P * per; i += (size_t)gridDim.x * blockDim.x) {
+    const int p = (int)(i / per), c = (int)(i % per);
+    reinterpret_cast<uint4*>(xs + (size_t)p * H)[c] = reinterpret_cast<const uint4*>(x + (size_t)src[p] * H)[c];
+  }
+}
+
+// Per token: acc = sum over its slots in order of w * ys[perm]; then
+// x = bf16(x + acc) (out == nullptr), or out = acc as an fp32 partial (EP).
+__global__ void moe_combine_batch_kernel(bf16* x, const bf16* ys, const float* w, const int* n, const int* perm, int T,
+                                         int k, int H, float* out) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < (size_t)T * H; i += (size_t)gridDim.x * blockDim.x) {
+    const int t = (int)(i / H), c = (int)(i % H);
+    const int nt = n[t];
+    float acc = 0.f;
+    for (int j = 0; j < nt; ++j)
+      acc = __fadd_rn(acc, __fmul_rn(bf2f(ys[(size_t)perm[t * k + j] * H + c]), w[t * k + j]));
+    if (out) out[i] = acc;
+    else x[i] = f2bf(__fadd_rn(bf2f(x[i]), acc));
   }
 }
 
@@ -498,6 +577,35 @@ cudaError_t k_moe_route(const bf16* logits, int E, int k, int normalize, int e_b
   void* args[] = {(void*)&logits, (void*)&E, (void*)&k, (void*)&normalize, (void*)&e_base, (void*)&e_local,
                   (void*)&idx, (void*)&w, (void*)&n};
   return launch_pdl((const void*)moe_route_kernel, dim3(1), dim3(256), args, st, pdl);
+}
+
+cudaError_t k_moe_route_batch(const bf16* logits, int T, int E, int k, int normalize, int e_base, int e_local,
+                              int* idx, float* w, int* n, cudaStream_t st) {
+  if (T <= 0) return cudaSuccess;
+  if (E <= 0 || E > 1024 || k <= 0 || k > 64 || k > E) return cudaErrorInvalidValue;
+  moe_route_kernel<<<T, 256, 0, st>>>(logits, E, k, normalize, e_base, e_local, idx, w, n);
+  return cudaGetLastError();
+}
+
+cudaError_t k_moe_group(const int* idx, const int* n, int T, int k, int E_l, int tile, int* perm, int* src,
+                        int4* tiles, int* n_tiles, int* n_pairs, cudaStream_t st) {
+  if (E_l <= 0 || E_l > 1024 || T <= 0) return cudaErrorInvalidValue;
+  moe_group_kernel<<<1, (E_l + 31) / 32 * 32, 0, st>>>(idx, n, T, k, E_l, tile, perm, src, tiles, n_tiles, n_pairs);
+  return cudaGetLastError();
+}
+
+cudaError_t k_moe_gather(const bf16* x, const int* src, const int* P, int Pmax, int H, bf16* xs, cudaStream_t st) {
+  if (Pmax <= 0) return cudaSuccess;
+  if (H % 8 != 0) return cudaErrorInvalidValue;
+  moe_gather_kernel<<<blocks_for((size_t)Pmax * (H / 8), 256), 256, 0, st>>>(x, src, P, H, xs);
+  return cudaGetLastError();
+}
+
+cudaError_t k_moe_combine_batch(bf16* x, const bf16* ys, const float* w, const int* n, const int* perm, int T, int k,
+                                int H, float* out, cudaStream_t st) {
+  if (T <= 0) return cudaSuccess;
+  moe_combine_batch_kernel<<<blocks_for((size_t)T * H, 256), 256, 0, st>>>(x, ys, w, n, perm, T, k, H, out);
+  return cudaGetLastError();
 }
 
 cudaError_t k_add_f32(bf16* x, const float* add, size_t n, int round, cudaStream_t st) {

@@ -80,6 +80,21 @@ cudaError_t k_moe_combine_peer(const bf16* y, const float* w, const int* n, int 
 cudaError_t k_add_f32(bf16* x, const float* add, size_t n, int round, cudaStream_t st);
 // x[k] = bf16(x[k] + sum_{s < *n} w[s] * y[s, k]) — one token's MoE residual.
 cudaError_t k_moe_residual(bf16* x, const bf16* y, const float* w, const int* n, int H, cudaStream_t st);
+// Batched MoE prefill (crates/ops/src/moe.rs:174-207 routes each token
+// independently; here all T tokens at once): routing of T logits rows into
+// idx / w [T][k] and n [T]; grouping of the (token, slot) pairs by local
+// expert (perm [T][k] -> position, src [P] -> token, tile list of
+// (expert, first, end) runs of `tile` positions, counts in *n_tiles and
+// *n_pairs = P); the
+// gather of x rows into grouped order; and the weighted combine back into
+// the residual (or an fp32 partial when out is set).
+cudaError_t k_moe_route_batch(const bf16* logits, int T, int E, int k, int normalize, int e_base, int e_local,
+                              int* idx, float* w, int* n, cudaStream_t st);
+cudaError_t k_moe_group(const int* idx, const int* n, int T, int k, int E_l, int tile, int* perm, int* src,
+                        int4* tiles, int* n_tiles, int* n_pairs, cudaStream_t st);
+cudaError_t k_moe_gather(const bf16* x, const int* src, const int* P, int Pmax, int H, bf16* xs, cudaStream_t st);
+cudaError_t k_moe_combine_batch(bf16* x, const bf16* ys, const float* w, const int* n, const int* perm, int T, int k,
+                                int H, float* out, cudaStream_t st);
 
 // cache[nkv, cap, D] rows [offset, offset+T) <- upd[nkv, T, D].
 cudaError_t k_slice_update(bf16* cache, const bf16* upd, int nkv, int cap, int D, int offset, const int* offset_dev,

@@ -29,6 +29,7 @@
 #include "ctx.cuh"
 #include "misc.cuh"
 #include "qgemm.cuh"
+#include "tc_gemm.cuh"
 #include "pgemv.cuh"
 #include "step.cuh"
 #include "qgemv.cuh"
@@ -127,6 +128,12 @@ struct emx_qwen3 {
   float* ppart = nullptr;
   int* pids = nullptr;
   int max_T = 0;
+  // batched MoE prefill: routing [T][E] logits, [T][k] choices, grouped rows
+  bf16 *p_rlog = nullptr, *p_xs = nullptr, *p_hs = nullptr, *p_ys = nullptr;
+  int *p_idx = nullptr, *p_n = nullptr, *p_perm = nullptr, *p_src = nullptr, *p_cnt = nullptr;
+  float* p_w = nullptr;
+  int4* p_tiles = nullptr;
+  int p_max_tiles = 0;
   // state
   int offset = 0;
   cudaGraphExec_t gexec = nullptr;
@@ -627,6 +634,16 @@ int build(emx_qwen3* m) {
       (rc = alloc_t(m, T * m->nq * hd, &m->pattn)) || (rc = alloc_t(m, T, &m->pids)))
     return rc;
   if (!m->moe && (rc = alloc_t(m, T * 2 * m->I, &m->ph))) return rc;
+  if (m->moe) {
+    const size_t P = T * c.top_k;  // (token, slot) pairs
+    m->p_max_tiles = m->E_l + (int)((P + 127) / 128) + 1;
+    if ((rc = alloc_t(m, T * c.n_experts, &m->p_rlog)) || (rc = alloc_t(m, P * H, &m->p_xs)) ||
+        (rc = alloc_t(m, P * m->Im, &m->p_hs)) || (rc = alloc_t(m, P * H, &m->p_ys)) ||
+        (rc = alloc_t(m, P, &m->p_idx)) || (rc = alloc_t(m, T, &m->p_n)) || (rc = alloc_t(m, P, &m->p_perm)) ||
+        (rc = alloc_t(m, P, &m->p_src)) || (rc = alloc_t(m, 2, &m->p_cnt)) || (rc = alloc_t(m, P, &m->p_w)) ||
+        (rc = alloc_t(m, (size_t)m->p_max_tiles, &m->p_tiles)))
+      return rc;
+  }
   if ((m->tp || m->ep) && (rc = alloc_t(m, T * H, &m->ppart))) return rc;
   if (cudaMallocHost(reinterpret_cast<void**>(&m->pinned), sizeof(int32_t) * ((size_t)c.kv_cap + 8)) != cudaSuccess)
     return fail(EMX_ERR_OOM, "pinned staging buffer");
@@ -969,6 +986,63 @@ int gemm(emx_qwen3* m, const QW& q, const bf16* x, int T, int epi, bf16* y, cons
   return EMX_OK;
 }
 
+// The MoE block of one layer over T prompt rows (pxn normalised, px the
+// residual): routing of every row (crates/ops/src/moe.rs:103-166: softmax
+// over the router logits, stable top-k, renormalised weights), the rows
+// grouped by local expert, the experts' gate|up (SwiGLU) and down
+// projections as two grouped tensor-core GEMMs over the packed expert tiles,
+// then each row's weighted sum over its experts in slot order added to the
+// residual — the arithmetic moe_forward_batch applies token by token
+// (crates/ops/src/moe.rs:174-207).  Under expert parallelism the weighted
+// sums are fp32 partials summed across ranks by one all-reduce per layer.
+int moe_prefill(emx_qwen3* m, const LayerW& lw, int T) {
+  const emx_qwen3_config& c = m->c;
+  cudaStream_t st = m->ctx->stream;
+  const int H = m->H, k = c.top_k, Im = m->Im, P = T * k;
+  int rc;
+  if ((rc = gemm(m, lw.router, m->pxn, T, kGemmStore, m->p_rlog, nullptr))) return rc;
+  cudaError_t e = k_moe_route_batch(m->p_rlog, T, c.n_experts, k, c.norm_topk, m->e_base, m->E_l, m->p_idx, m->p_w,
+                                    m->p_n, st);
+  if (e != cudaSuccess) return fail_cuda(e, "prefill moe route");
+  if ((e = k_moe_group(m->p_idx, m->p_n, T, k, m->E_l, 128, m->p_perm, m->p_src, m->p_tiles, m->p_cnt, m->p_cnt + 1,
+                       st)) != cudaSuccess)
+    return fail_cuda(e, "prefill moe grouping");
+  if ((e = k_moe_gather(m->pxn, m->p_src, m->p_cnt + 1, P, H, m->p_xs, st)) != cudaSuccess)
+    return fail_cuda(e, "prefill moe gather");
+  auto grouped = [&](const QW& q, const bf16* x, int K, int N_out, int epi, bf16* y) -> int {
+    TcGemmArgs t = {};
+    t.x = x;
+    t.M = P;
+    t.N = N_out;
+    t.K = K;
+    t.epi = epi;
+    t.y = y;
+    t.status = m->ctx->status;
+    t.bits = q.bits;
+    t.wp = q.pk;
+    t.S = (K / 64 + 7) / 8;
+    t.nrb = q.map.R / 16;
+    t.tiles = m->p_tiles;
+    t.n_tiles = m->p_cnt;
+    t.expert_stride = (size_t)t.nrb * t.S * pgemv_tile_bytes(q.bits, q.gs);
+    if (q.gs != 64 || !tc_pgemm_supported(t)) return fail(EMX_ERR_INVALID, "prefill moe: unsupported expert shape");
+    const cudaError_t ce = tc_pgemm_grouped_launch(t, m->p_max_tiles, st);
+    return ce == cudaSuccess ? EMX_OK : fail_cuda(ce, "prefill moe experts");
+  };
+  if ((rc = grouped(lw.e_gu, m->p_xs, H, Im, kTcSwiglu, m->p_hs))) return rc;
+  if ((rc = grouped(lw.e_down, m->p_hs, Im, H, kTcStore, m->p_ys))) return rc;
+  if (m->ep) {
+    if ((e = k_moe_combine_batch(m->px, m->p_ys, m->p_w, m->p_n, m->p_perm, T, k, H, m->ppart, st)) != cudaSuccess)
+      return fail_cuda(e, "prefill moe combine");
+    if ((rc = comm_all_reduce(m->comm, m->ppart, (size_t)T * H, EMX_F32, st))) return rc;
+    if ((e = k_add_f32(m->px, m->ppart, (size_t)T * H, 0, st)) != cudaSuccess) return fail_cuda(e, "prefill residual");
+  } else if ((e = k_moe_combine_batch(m->px, m->p_ys, m->p_w, m->p_n, m->p_perm, T, k, H, nullptr, st)) !=
+             cudaSuccess) {
+    return fail_cuda(e, "prefill moe combine");
+  }
+  return EMX_OK;
+}
+
 // One forward pass over T prompt rows at the current offset.  attend_cache:
 // the rows also attend the cached rows before them (chunked prefill); else
 // the chunk attends only itself, as Qwen3Engine::prefill does
@@ -1036,52 +1110,8 @@ int prefill_impl(emx_qwen3* m, const int32_t* ids_dev, int T, bool attend_cache 
     if (!m->moe) {
       if ((rc = gemm(m, lw.gate_up, m->pxn, T, kGemmSwiglu, m->ph, nullptr))) return rc;
       if ((rc = row_parallel(lw.down, m->ph))) return rc;
-    } else {
-      // token by token through the decode-path MoE kernels (route, gathered
-      // expert SwiGLU, gathered expert down), as moe_forward_batch routes each
-      // token independently (crates/ops/src/moe.rs:174-207)
-      for (int t = 0; t < T; ++t) {
-        const bf16* xrow = m->pxn + (size_t)t * H;
-        GemvArgs ra = gemv_base(m, lw.router);
-        ra.pro = kProX;
-        ra.x = xrow;
-        ra.epi = kEpiStore;
-        ra.y = m->router_logits;
-        if ((e = pgemv_launch(ra, lw.p_router, st, false)) != cudaSuccess) return fail_cuda(e, "prefill router");
-        if ((e = k_moe_route(m->router_logits, c.n_experts, c.top_k, c.norm_topk, m->e_base, m->E_l, m->moe_idx,
-                             m->moe_w, m->moe_n, st, false)) != cudaSuccess)
-          return fail_cuda(e, "prefill route");
-        GemvArgs ga = gemv_base(m, lw.e_gu);
-        ga.N = c.top_k * 2 * m->Im;
-        ga.pro = kProX;
-        ga.x = xrow;
-        ga.epi = kEpiSwiglu;
-        ga.y = m->hb;
-        ga.slot_expert = m->moe_idx;
-        ga.n_slots = m->moe_n;
-        ga.slot_rows = m->Im;
-        if ((e = pgemv_launch(ga, lw.p_egu, st, false)) != cudaSuccess) return fail_cuda(e, "prefill experts");
-        GemvArgs da = gemv_base(m, lw.e_down);
-        da.N = c.top_k * H;
-        da.pro = kProX;
-        da.x = m->hb;
-        da.x_slots = c.top_k;
-        da.epi = kEpiStore;
-        da.y = m->moe_y;
-        da.slot_expert = m->moe_idx;
-        da.n_slots = m->moe_n;
-        da.slot_rows = H;
-        if ((e = pgemv_launch(da, lw.p_edown, st, false)) != cudaSuccess) return fail_cuda(e, "prefill experts");
-        if (m->ep) {
-          if ((e = k_moe_combine(m->moe_y, m->moe_w, m->moe_n, H, m->part, st, false)) != cudaSuccess)
-            return fail_cuda(e, "prefill combine");
-          if ((rc = comm_all_reduce(m->comm, m->part, (size_t)H, EMX_F32, st))) return rc;
-          if ((e = k_add_f32(m->px + (size_t)t * H, m->part, (size_t)H, 0, st)) != cudaSuccess)
-            return fail_cuda(e, "prefill residual");
-        } else if ((e = k_moe_residual(m->px + (size_t)t * H, m->moe_y, m->moe_w, m->moe_n, H, st)) != cudaSuccess) {
-          return fail_cuda(e, "prefill residual");
-        }
-      }
+    } else if ((rc = moe_prefill(m, lw, T))) {
+      return rc;
     }
   }
   // final norm + lm_head on the last row, greedy token, offset += T

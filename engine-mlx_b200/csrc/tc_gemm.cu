@@ -762,10 +762,11 @@ __device__ __forceinline__ uint32_t bytes02_bf16(uint32_t w) {
 }
 
 // Output step for 16 tokens of one weight row (feature n = lane's row):
-// v[t] = acc of token m0t + t.  SwiGLU: lanes 0-15 gate, 16-31 up of the
+// v[t] = acc of token m0t + t; rows from mend on are not stored.  SwiGLU: lanes 0-15 gate, 16-31 up of the
 // same 16 features.
 template <int EPI>
-__device__ __forceinline__ void w_store16(const TcGemmArgs& a, int n, int m0t, int lane, float (&v)[16], bool ok) {
+__device__ __forceinline__ void w_store16(const TcGemmArgs& a, int n, int m0t, int mend, int lane, float (&v)[16],
+                                          bool ok) {
   if (EPI == kTcSwiglu) {
     float h[16];
 #pragma unroll
@@ -779,14 +780,14 @@ __device__ __forceinline__ void w_store16(const TcGemmArgs& a, int n, int m0t, i
     if (!ok || lane >= 16 || n >= a.N) return;
 #pragma unroll
     for (int t = 0; t < 16; ++t)
-      if (m0t + t < a.M) a.y[(size_t)(m0t + t) * a.N + n] = f2bf(h[t]);
+      if (m0t + t < mend) a.y[(size_t)(m0t + t) * a.N + n] = f2bf(h[t]);
     return;
   }
   if (!ok || n >= a.N) return;
 #pragma unroll
   for (int t = 0; t < 16; ++t) {
     const int m = m0t + t;
-    if (m >= a.M) break;
+    if (m >= mend) break;
     const size_t o = (size_t)m * a.N + n;
     if (EPI == kTcF32) a.yf[o] = v[t];
     else if (EPI == kTcStore) a.y[o] = f2bf(v[t]);
@@ -811,8 +812,16 @@ __global__ void __launch_bounds__(kWThreads, 1)
   int* issued_c = issued_x + 1;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = blockIdx.x * NT;  // first token
-  const int nt = blockIdx.y;       // 8 packed row blocks
+  const int nt = blockIdx.y;  // 8 packed row blocks
+  int m0 = blockIdx.x * NT, mend = a.M;  // rows [m0, min(m0 + NT, mend)) of x
+  const unsigned char* wp = a.wp;
+  if (a.tiles) {  // grouped: this CTA's tile of one expert, or nothing
+    if ((int)blockIdx.x >= *a.n_tiles) return;
+    const int4 ti = a.tiles[blockIdx.x];
+    wp += (size_t)ti.x * a.expert_stride;
+    m0 = ti.y;
+    mend = ti.z;
+  }
   // spans [sp0, sp0 + nsl) of this CTA
   const int sp0 = (int)((long long)blockIdx.z * a.S / gridDim.z);
   const int nsl = (int)((long long)(blockIdx.z + 1) * a.S / gridDim.z) - sp0;
@@ -876,7 +885,7 @@ __global__ void __launch_bounds__(kWThreads, 1)
         if (lane == 0) mbar_arrive_expect_tx(&cfull[c], (uint32_t)(nrb * C::TILE));
         __syncwarp();
         if (lane < nrb)
-          bulk_g2s_hint(dst + lane * C::TILE, a.wp + ((size_t)(rb0 + lane) * a.S + sp0 + u) * C::TILE,
+          bulk_g2s_hint(dst + lane * C::TILE, wp + ((size_t)(rb0 + lane) * a.S + sp0 + u) * C::TILE,
                         (uint32_t)C::TILE, &cfull[c], pol);
       } else {
         const int hs = u & 1, sp = sp0 + (u >> 1);
@@ -884,7 +893,7 @@ __global__ void __launch_bounds__(kWThreads, 1)
         __syncwarp();
         const int j = lane & 7;
         if (lane < 16 && j < nrb) {
-          const unsigned char* tile = a.wp + ((size_t)(rb0 + j) * a.S + sp) * C::TILE;
+          const unsigned char* tile = wp + ((size_t)(rb0 + j) * a.S + sp) * C::TILE;
           if (lane < 8)
             bulk_g2s_hint(dst + j * (C::HALF_A + 512), tile + hs * C::HALF_A, (uint32_t)C::HALF_A, &cfull[c], pol);
           else
@@ -1067,7 +1076,7 @@ __global__ void __launch_bounds__(kWThreads, 1)
             }
           }
         }
-        w_store16<EPI>(a, n, m0 + oc * 32 + h * 16, lane, v, okd);
+        w_store16<EPI>(a, n, m0 + oc * 32 + h * 16, mend, lane, v, okd);
       }
     }
   }
@@ -1327,6 +1336,34 @@ cudaError_t tc_qgemm_launch(const TcGemmArgs& a, int num_sms, cudaStream_t st) {
 #undef EMX_Q
 }
 
+template <int BITS, int EPI>
+cudaError_t launch_pg(const TcGemmArgs& a, int max_tiles, cudaStream_t st) {
+  using C = WCfg<BITS, 128>;
+  CUtensorMap tx;
+  cudaError_t e = encode_2d(&tx, a.x, (uint64_t)a.K, (uint64_t)a.M, BM);
+  if (e != cudaSuccess) return e;
+  auto kern = tc_pgemm_kernel<BITS, EPI, 128>;
+  static bool attr_set = false;  // per instantiation
+  if (!attr_set) {
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    if (e != cudaSuccess) return e;
+    attr_set = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(max_tiles, (a.nrb + 7) / 8, 1);
+  cfg.blockDim = dim3(kWThreads);
+  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = 1;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, tx, a);
+}
+
 bool tc_pgemm_supported(const TcGemmArgs& a) {
   if (a.M <= 0 || a.K <= 0 || a.N <= 0 || a.nrb <= 0 || a.S <= 0) return false;
   if (a.K % BK != 0 || a.N % 16 != 0 || !(a.bits == 4 || a.bits == 8) || !a.wp) return false;
@@ -1352,6 +1389,23 @@ cudaError_t tc_pgemm_launch(const TcGemmArgs& a, int num_sms, cudaStream_t st) {
   }
   EMX_P(8)
 #undef EMX_P
+}
+
+cudaError_t tc_pgemm_grouped_launch(const TcGemmArgs& a, int max_tiles, cudaStream_t st) {
+  if (!tc_pgemm_supported(a) || !a.tiles || !a.n_tiles || max_tiles <= 0) return cudaErrorInvalidValue;
+  if (a.expert_stride % 16 != 0) return cudaErrorInvalidValue;
+  if (a.bits == 4) {
+    switch (a.epi) {
+      case kTcStore: return launch_pg<4, kTcStore>(a, max_tiles, st);
+      case kTcSwiglu: return launch_pg<4, kTcSwiglu>(a, max_tiles, st);
+      default: return cudaErrorInvalidValue;
+    }
+  }
+  switch (a.epi) {
+    case kTcStore: return launch_pg<8, kTcStore>(a, max_tiles, st);
+    case kTcSwiglu: return launch_pg<8, kTcSwiglu>(a, max_tiles, st);
+    default: return cudaErrorInvalidValue;
+  }
 }
 
 bool tc_gemm_supported(const TcGemmArgs& a) {

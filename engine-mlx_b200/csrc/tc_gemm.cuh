@@ -36,6 +36,12 @@ struct TcGemmArgs {
   const unsigned char* wp;  // packed tiles [row block][span]
   int S;                    // spans (8 groups each) per row block
   int nrb;                  // packed 16-row blocks (SwiGLU: gate and up blocks alternate)
+  // grouped (MoE) mode: CTA x takes tiles[x] = (expert, first row, end row)
+  // of x when x < *n_tiles (others exit); the expert's packed block starts
+  // expert * expert_stride bytes into wp; nrb counts one expert's row blocks
+  const int4* tiles;
+  const int* n_tiles;
+  size_t expert_stride;
 };
 
 // True when the shape is supported (K % 64 == 0, N % 32 == 0, 16-byte
@@ -58,5 +64,8 @@ cudaError_t tc_qgemm_launch(const TcGemmArgs& a, int num_sms, cudaStream_t st);
 // block n / 16 pairs gate row block 2 (n / 16) with up row block 2 (n / 16) + 1.
 bool tc_pgemm_supported(const TcGemmArgs& a);
 cudaError_t tc_pgemm_launch(const TcGemmArgs& a, int num_sms, cudaStream_t st);
+// Grouped mode (tiles / n_tiles / expert_stride set): one launch over up to
+// max_tiles row tiles of 128 rows, each against its own expert's weights.
+cudaError_t tc_pgemm_grouped_launch(const TcGemmArgs& a, int max_tiles, cudaStream_t st);
 
 }  // namespace emx
