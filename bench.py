@@ -16,9 +16,11 @@ rank runs its own replica (the 1.7B model is not sharded: "replicas only") and
 Besides the headline the line carries: prefill tok/s at 128 / 2048 / 8192
 tokens, decode after 2048- and 8192-token prompts, the single quantized linear
 of BASELINE configs[0] (M = 1 and 512), the packed GEMV alone, end-to-end
-rates through the public API (per-step and streamed), and `sharded`: the
+rates through the public API (per-step and streamed), `sharded`: the
 32B-shape model tensor-parallel over the job's GPUs (every N of a scaling run),
-so the 1 -> 8 curve holds the collective's scaling, not only replicas.
+so the 1 -> 8 curve holds the collective's scaling, not only replicas, and
+`moe`: the 30B-A3B-shape model expert-parallel over the job's GPUs, a
+1024-token prefill (grouped expert GEMMs) and decode after it.
 """
 import argparse
 import json
@@ -360,6 +362,69 @@ def sharded_c5(args, rank, world, dist, torch, hbm, steps=32, prompt=128):
                               "bytes_per_step": per_gpu}}
 
 
+def moe_c4(args, rank, world, dist, torch, hbm, steps=32, prompt=1024):
+    """The 30B-A3B-shape MoE model split expert-parallel
+    across the job's GPUs (one GPU: the whole model): a 1024-token prefill
+    (the grouped expert GEMMs) and decode after it, CUDA events, max over
+    ranks; the decode step roofline counts the active experts' bytes."""
+    import dataclasses
+
+    import numpy as np
+
+    import emx
+
+    cfg = dataclasses.replace(emx.CONFIGS["c4"], kv_cap=prompt + steps + 64, max_prefill=prompt)
+    dev = int(os.environ.get("LOCAL_RANK", "0"))
+    ctx = emx.Ctx(dev)
+    sp = emx.C.c_void_p()
+    emx.lib().emx_ctx_stream(ctx.h, emx.C.byref(sp))
+    st = torch.cuda.ExternalStream(sp.value, device=dev)
+    comm = None
+    if world > 1:
+        obj = [emx.Comm.unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        comm = emx.Comm(ctx, obj[0], world, rank)
+    m = emx.Qwen3(ctx, cfg, comm)
+    m.init_random(args.seed)
+    ids = ctx.put(np.random.default_rng(args.seed).integers(0, cfg.vocab, prompt).astype(np.int32))
+    m.prefill_device(ids, prompt)  # warm
+    times = []
+    for _ in range(2):
+        m.reset()
+        ctx.synchronize()
+        if dist is not None:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        m.prefill_device(ids, prompt)
+        e1.record(st)
+        e1.synchronize()
+        times.append(e0.elapsed_time(e1))
+    pre_ms = min(times)
+    m.decode_device(3)
+    barrier = dist.barrier if dist is not None else None
+    ms = timed_decode(m, ctx, st, torch, steps, barrier)
+    if dist is not None:
+        t = torch.tensor([ms, pre_ms], device=f"cuda:{dev}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, pre_ms = float(t[0].item()), float(t[1].item())
+    ids.free()
+    m.close()
+    if comm is not None:
+        comm.close()
+    ctx.close()
+    mean_ctx = prompt + 3 + (steps - 1) / 2.0
+    per_gpu = decode_bytes(cfg, mean_ctx) / world
+    ach = per_gpu / (ms / steps / 1000.0) / 1e9
+    return {"model": "c4 (Qwen3-30B-A3B shape, 128 experts top-8, int4 gs64, random-init)",
+            "parallelism": f"expert parallel x{world}", "prefill_tokens": prompt,
+            "prefill_tok_s": prompt / (pre_ms / 1000.0), "prefill_ms": pre_ms,
+            "decode_tok_s": steps / (ms / 1000.0), "ms_per_step": ms / steps, "steps": steps,
+            "step_roofline": {"bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s", "frac": ach / hbm,
+                              "scope": "per GPU: attention + router + the top-8 experts' weights, 1/world",
+                              "bytes_per_step": per_gpu}}
+
+
 def run_engine(args, cfg, rank, world, dist):
     import numpy as np
 
@@ -538,9 +603,11 @@ def run_engine(args, cfg, rank, world, dist):
         c1 = c1_linear(ctx, st, torch, hbm, tf)
     ctx.close()
     barrier()
-    sh = None
+    sh = mo = None
     if not args.shard and not args.no_sharded:
         sh = sharded_c5(args, rank, world, dist, torch, hbm)
+    if not args.shard and not args.no_moe:
+        mo = moe_c4(args, rank, world, dist, torch, hbm)
     if rank != 0:
         return
     if fused:
@@ -580,6 +647,8 @@ def run_engine(args, cfg, rank, world, dist):
             "clocks": clk.summary()}
     if sh:
         line["sharded"] = sh
+    if mo:
+        line["moe"] = mo
     if sharded:
         line["step_roofline"]["scope"] += ", per GPU (1/world of the weights)"
     if world == 1 and not args.no_cpu_baseline:
@@ -736,6 +805,8 @@ def main():
                     help="decode with one kernel per operation instead of the persistent step kernel")
     ap.add_argument("--no-sharded", action="store_true",
                     help="skip the tensor-parallel 32B-shape measurement added to every line")
+    ap.add_argument("--no-moe", action="store_true",
+                    help="skip the expert-parallel 30B-A3B-shape prefill + decode measurement added to every line")
     ap.add_argument("--kernel-only", nargs="?", const="gemv", default=None,
                     choices=["gemv", "gemm", "attn", "prefill", "c1", "step"],
                     help="time one kernel alone and print its roofline: the packed decode GEMV (gate|up shape, "
