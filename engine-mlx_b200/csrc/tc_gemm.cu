@@ -784,14 +784,24 @@ __device__ __forceinline__ void w_store16(const TcGemmArgs& a, int n, int m0t, i
     return;
   }
   if (!ok || n >= a.N) return;
+  if (EPI == kTcResid) {
+    // every residual value first (independent loads; y may alias res, and
+    // each element belongs to this thread alone), then the stores
+    float r[16];
+#pragma unroll
+    for (int t = 0; t < 16; ++t) r[t] = m0t + t < mend ? bf2f(a.res[(size_t)(m0t + t) * a.N + n]) : 0.f;
+#pragma unroll
+    for (int t = 0; t < 16; ++t)
+      if (m0t + t < mend) a.y[(size_t)(m0t + t) * a.N + n] = f2bf(__fadd_rn(r[t], bfround(v[t])));
+    return;
+  }
 #pragma unroll
   for (int t = 0; t < 16; ++t) {
     const int m = m0t + t;
     if (m >= mend) break;
     const size_t o = (size_t)m * a.N + n;
     if (EPI == kTcF32) a.yf[o] = v[t];
-    else if (EPI == kTcStore) a.y[o] = f2bf(v[t]);
-    else a.y[o] = f2bf(__fadd_rn(bf2f(a.res[o]), bfround(v[t])));
+    else a.y[o] = f2bf(v[t]);
   }
 }
 
