@@ -154,7 +154,7 @@ struct emx_qwen3 {
   StepPlan sp{};
   StepArgs sa{};
   uint64_t* step_words = nullptr;  // the persistent step's flag-word exchange buffers
-  unsigned* step_ctl = nullptr;    // epoch, abort word, attention tickets
+  unsigned* step_ctl = nullptr;    // epoch, abort word
   size_t step_nwords = 0, step_nctl = 0;
   unsigned long long step_epochs = 0;  // persistent steps since the words were cleared
 };
@@ -427,18 +427,19 @@ int setup_step(emx_qwen3* m) {
   }
   int rc;
   StepLayer* d_layers = nullptr;
-  float* part = nullptr;
   size_t words[5];
   step_exchange_words(sh, words);
   size_t nw = 0;
   for (size_t w : words) nw += w;
-  // exchange words, then epoch, abort word and the attention tickets
-  const size_t ctl = 2 + (size_t)m->nkv;
-  if ((rc = alloc_t(m, (size_t)c.layers, &d_layers)) || (rc = alloc_t(m, nw, &m->step_words)) ||
-      (rc = alloc_t(m, ctl, &m->step_ctl)) ||
-      (rc = alloc_t(m, (size_t)m->nkv * p.tmpl.max_splits * p.hpg * (m->hd + 4), &part)))
+  nw = (nw + 1) & ~(size_t)1;  // the partials start 16-byte aligned
+  // exchange words, then the attention splits' partials (flag words too, so
+  // the host's clearing covers them); epoch and abort word apart
+  const size_t npart = (size_t)m->nkv * p.tmpl.max_splits * p.hpg * (m->hd + 2);
+  const size_t ctl = 2;
+  if ((rc = alloc_t(m, (size_t)c.layers, &d_layers)) || (rc = alloc_t(m, nw + npart, &m->step_words)) ||
+      (rc = alloc_t(m, ctl, &m->step_ctl)))
     return rc;
-  m->step_nwords = nw;
+  m->step_nwords = nw + npart;
   m->step_nctl = ctl;
   std::vector<StepLayer> hl(c.layers);
   for (int l = 0; l < c.layers; ++l) {
@@ -477,10 +478,9 @@ int setup_step(emx_qwen3* m) {
   a.hw = a.xmw + words[3];
   a.epoch = m->step_ctl;
   a.abort_word = m->step_ctl + 1;
-  a.attn_tick = m->step_ctl + 2;
   a.logits = m->logits;
   a.rope_cs = m->rope_cs;
-  a.attn_part = part;
+  a.attn_pw = w + nw;
   a.pos = m->pos;
   a.hist = m->hist;
   a.hist_n = m->hist_n;

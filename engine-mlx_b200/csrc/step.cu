@@ -23,9 +23,8 @@
 //     write of row `pos` (by the split that owns it), and an online softmax
 //     kept by each warp over its rows of the 32-row tiles (no barrier per
 //     tile), merged across warps once.  One split per head writes its
-//     normalised output; with
-//     more, each stores its partial and the last to finish (ticket) merges
-//     the head.
+//     normalised output; with more, each writes its partial in flag words
+//     and then merges a slice of the head's output from all of them.
 // The last CTA through the lm_head's argmax ticket writes the token, moves
 // the position and adds one to the epoch, so the next step's flags differ.
 // Every wait is bounded (kWaitLimitNs); a CTA that gives up raises a global
@@ -46,11 +45,12 @@ constexpr int kNT = kCons * 32;       // consumer threads
 constexpr int kThreads = kNT + 32;    // + the producer warp
 constexpr int kHD = 128;
 constexpr int kAT = 64;               // attention rows per tile (stage)
-constexpr int kRowsPerSplit = 256;    // cache rows per attention split before another is added
+constexpr int kRowsPerSplit = 256;    // up to this many cache rows: one attention split per KV head
+constexpr int kRowsPerSplitLong = 128;  // beyond: one split per this many rows (up to max_splits)
 constexpr int kMaxSplitsMerge = 32;   // splits one head's merge takes (one per lane)
 constexpr int kVOff = kAT * kHD * 2;  // V rows' offset inside a slot
 constexpr int kMaxSlots = 8;
-constexpr int kPartStride = kHD + 4;  // floats per (split, head) partial: m, l, pad, pad, output[128]
+constexpr int kPartWords = kHD + 2;  // flag words per (split, q head) partial: m, l, output[128]
 // ring slot: 8 int4 tiles or 4 int8 tiles (16 MMA units), or 64 K + 64 V rows
 constexpr int kSlotBytes = 36864;
 using CSync = SyncNamed<kNT>;
@@ -79,6 +79,7 @@ struct AttnSm {
   float wm[kCons][HPG], wl[kCons][HPG];  // per-warp running max and sum
   float4 sacc[kCons][HPG][32];           // per-warp partial outputs, lane l = dims 4l..4l+3
   float swt[HPG][kMaxSplitsMerge];  // merge weights of a head's splits
+  float2 mraw[2 * kNT];             // the merge's inputs: (m, l) pairs, then partial output pairs
   bf16 knew[kHD];
   bf16 vnew[kHD];
 };
@@ -98,7 +99,7 @@ __device__ __forceinline__ void split_range(int L, int splits, int split, int& p
 
 // Attention splits per KV head for the new row p (rows 0..p attend).
 __device__ __forceinline__ int attn_splits(const StepArgs& A, int p) {
-  const int s = (p + kRowsPerSplit) / kRowsPerSplit;
+  const int s = p < kRowsPerSplit ? 1 : (p + kRowsPerSplitLong) / kRowsPerSplitLong;
   return s < A.max_splits ? s : A.max_splits;
 }
 
@@ -106,6 +107,12 @@ __device__ __forceinline__ int attn_splits(const StepArgs& A, int p) {
 __device__ __forceinline__ void fw_store(uint64_t* p, uint32_t d, unsigned flag) {
   const uint64_t v = ((uint64_t)flag << 32) | d;
   asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+// Two words (16-byte aligned) in one 128-bit store, each with the flag.
+__device__ __forceinline__ void fw_store2(uint64_t* p, uint32_t d0, uint32_t d1, unsigned flag) {
+  const uint64_t v0 = ((uint64_t)flag << 32) | d0, v1 = ((uint64_t)flag << 32) | d1;
+  asm volatile("st.relaxed.gpu.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(v0), "l"(v1) : "memory");
 }
 
 __device__ __forceinline__ void fw_load2(const uint64_t* p, uint64_t& a, uint64_t& b) {
@@ -288,25 +295,39 @@ __device__ void load_res_fw(const uint64_t* src, int H_, unsigned flag, bf16* re
 
 // ------------------------------------------------------------- GEMV phases
 // The stages of logical blocks [lb0, lb1) from the ring (consumer threads);
-// ends with a consumer barrier.
+// ends with a consumer barrier.  The geometry, the ring's slot and phase
+// and the counters live in registers for the whole phase: every asm block
+// with a memory clobber (the mbarrier ops) would otherwise force them to be
+// re-read per stage.
 template <int BITS>
-__device__ __noinline__ void gemv_run(const StepArgs& A, StepHdr& H, unsigned char* smem, const PGeom& geo,
-                                      int lb0, int lb1, int& seq, int& rot, int tid) {
+__device__ __noinline__ void gemv_run(const StepArgs& A, StepHdr& H, unsigned char* smem, const PGeom& geo_ref,
+                                      int lb0, int lb1, int& seq_ref, int& rot_ref, int tid) {
   const int warp = tid >> 5, lane = tid & 31;
+  const PGeom geo = geo_ref;
   const PgSmem sm = pg_smem(smem, geo);
   const int lbt = geo.halves * geo.S;
   const int T1 = lb1 * lbt;
   unsigned char* ring = smem + A.off_ring;
+  const int NS = A.nslots, SB = A.slot_bytes;
+  int* const status = A.status;
+  int seq = seq_ref, rot = rot_ref;
+  int slot = seq % NS;
+  uint32_t par = (uint32_t)((seq / NS) & 1);
   for (int a0 = lb0 * lbt; a0 < T1; a0 += geo.stage_tiles) {
     const int a1 = min(T1, a0 + geo.stage_tiles);
-    const int s = seq++;
-    const int slot = s % A.nslots;
-    if (wait_or_abort(&H.full[slot], (uint32_t)((s / A.nslots) & 1), &H.abort_flag, A.status))
-      pg_stage<BITS, 64>(geo, sm, ring + (size_t)slot * A.slot_bytes, a0, a1, lb0, warp, lane, kCons, rot);
-    rot = (rot + (a1 - a0) * 2) % kCons;
+    if (wait_or_abort(&H.full[slot], par, &H.abort_flag, status))
+      pg_stage<BITS, 64>(geo, sm, ring + (size_t)slot * SB, a0, a1, lb0, warp, lane, kCons, rot);
+    rot = (rot + (a1 - a0) * 2) & (kCons - 1);
     __syncwarp();
     if (lane == 0) mbar_arrive(&H.empty[slot]);
+    ++seq;
+    if (++slot == NS) {
+      slot = 0;
+      par ^= 1u;
+    }
   }
+  seq_ref = seq;
+  rot_ref = rot;
   CSync::sync();
 }
 
@@ -375,6 +396,64 @@ __device__ void epilogue_fw(const PGeom& geo, const PgSmem& sm, int lb0, int lb1
     const uint32_t bits = f2bits(y);
     const uint32_t hi = __shfl_down_sync(0xffffffffu, bits, 1);
     if (li < nrow && (li & 1) == 0) fw_store(dst + (size_t)(lb0 * 16 + li) / 2, bits | (hi << 16), flag);
+  }
+}
+
+// The merge of a KV head's split partials (flag words at hw: [split][q
+// head][m, l, output[128]]), distributed over the splits: split `split` of
+// `ns` merges output words [split * W / ns, (split + 1) * W / ns) of the
+// head's W.  Every split of the head is resident and writes its partial
+// before it waits here, so the waits end once the slowest split's words
+// land; no ticket, no fence.  Arithmetic: weights 2^(m_s - M) / sum_s
+// 2^(m_s - M) l_s (M the max), then the weighted partials summed in split
+// order.  One thread holds at most two load pairs, all issued before any
+// is checked.
+template <int HPG>
+__device__ __noinline__ void attn_merge_slice(const StepArgs& A, StepHdr& H, AttnSm<HPG>& S, const uint64_t* hw,
+                                              uint64_t* out, int split, int ns, unsigned flag, int tid) {
+  constexpr int W = HPG * kHD / 2;
+  const int warp = tid >> 5, lane = tid & 31;
+  const int w0 = split * W / ns, w1 = (split + 1) * W / ns;
+  const int nml = ns * HPG, tot = nml + (w1 - w0) * ns;  // <= 2 * kNT
+  auto addr = [&](int t) -> const uint64_t* {
+    if (t < nml) return hw + (size_t)t * kPartWords;  // t = split * HPG + q head
+    const int u = t - nml, i = w0 + u / ns, s2 = u % ns;
+    const int h = (2 * i) / kHD, d = (2 * i) % kHD;
+    return hw + ((size_t)s2 * HPG + h) * kPartWords + 2 + d;
+  };
+  const int ta = tid, tb = tid + kNT;
+  uint64_t a0 = 0, a1 = 0, b0 = 0, b1 = 0;
+  if (ta < tot) fw_load2(addr(ta), a0, a1);
+  if (tb < tot) fw_load2(addr(tb), b0, b1);
+  if (ta < tot) {
+    if (!fw_ok(a0, a1, flag) && !fw_wait2(addr(ta), flag, a0, a1, A, H)) a0 = a1 = 0;
+    S.mraw[ta] = make_float2(__uint_as_float((uint32_t)a0), __uint_as_float((uint32_t)a1));
+  }
+  if (tb < tot) {
+    if (!fw_ok(b0, b1, flag) && !fw_wait2(addr(tb), flag, b0, b1, A, H)) b0 = b1 = 0;
+    S.mraw[tb] = make_float2(__uint_as_float((uint32_t)b0), __uint_as_float((uint32_t)b1));
+  }
+  CSync::sync();
+  for (int h = warp; h < HPG; h += kCons) {
+    const float ms = lane < ns ? S.mraw[lane * HPG + h].x : -INFINITY;
+    const float ls = lane < ns ? S.mraw[lane * HPG + h].y : 0.f;
+    const float M = warp_max(ms);
+    const float w = ms == -INFINITY ? 0.f : ex2f(ms - M);
+    const float den = warp_sum(fmaf(w, ls, 0.f));
+    if (lane < ns) S.swt[h][lane] = __fdiv_rn(w, den);
+  }
+  CSync::sync();
+  if (tid < w1 - w0) {
+    const int i = w0 + tid;
+    const int h = (2 * i) / kHD;
+    const float2* v = &S.mraw[nml + tid * ns];
+    float o0 = 0.f, o1 = 0.f;
+    for (int s2 = 0; s2 < ns; ++s2) {
+      const float sw = S.swt[h][s2];
+      o0 = fmaf(sw, v[s2].x, o0);
+      o1 = fmaf(sw, v[s2].y, o1);
+    }
+    fw_store(out + i, (uint32_t)f2bits(bfround(o0)) | ((uint32_t)f2bits(bfround(o1)) << 16), flag);
   }
 }
 
@@ -613,51 +692,21 @@ __device__ __noinline__ void attn_phase(const StepArgs& A, StepHdr& H, unsigned 
     }
     return;
   }
-  // several splits: this split's partial (m, l, unnormalised output); the
-  // last split of the head to finish merges them all
-  float* part = A.attn_part + ((size_t)kvh * A.max_splits + split) * HPG * kPartStride;
-  for (int i = tid; i < HPG * kHD / 2; i += kNT) {
-    const int h = (2 * i) / kHD, d = (2 * i) % kHD;
-    float M, Lh, n0, n1;
-    merged(h, d, M, Lh, n0, n1);
-    *reinterpret_cast<float2*>(part + h * kPartStride + 4 + d) = make_float2(n0, n1);
-    if (d == 0) {
-      part[h * kPartStride + 0] = M;
-      part[h * kPartStride + 1] = Lh;
+  // several splits: each writes its partial (m, l and the unnormalised
+  // output of every q head) in flag words, then merges one slice of the
+  // head's output words from all the splits' partials
+  uint64_t* const hw = A.attn_pw + (size_t)kvh * A.max_splits * HPG * kPartWords;
+  {
+    uint64_t* pw = hw + (size_t)split * HPG * kPartWords;
+    for (int i = tid; i < HPG * kHD / 2; i += kNT) {
+      const int h = (2 * i) / kHD, d = (2 * i) % kHD;
+      float M, Lh, n0, n1;
+      merged(h, d, M, Lh, n0, n1);
+      fw_store2(pw + h * kPartWords + 2 + d, __float_as_uint(n0), __float_as_uint(n1), flag);
+      if (d == 0) fw_store2(pw + h * kPartWords, __float_as_uint(M), __float_as_uint(Lh), flag);
     }
   }
-  __threadfence();
-  CSync::sync();
-  if (tid == 0) H.flag = (atomicAdd(&A.attn_tick[kvh], 1u) == (unsigned)ns - 1) ? 1u : 0u;
-  CSync::sync();
-  if (!H.flag) return;
-  __threadfence();
-  const float* hb = A.attn_part + (size_t)kvh * A.max_splits * HPG * kPartStride;
-  // weights 2^(m_s - M) / sum_s 2^(m_s - M) l_s, one warp per q head
-  for (int h = warp; h < HPG; h += kCons) {
-    const float* pm = hb + (size_t)lane * HPG * kPartStride + h * kPartStride;
-    const float ms = lane < ns ? __ldcg(pm) : -INFINITY;
-    const float ls = lane < ns ? __ldcg(pm + 1) : 0.f;
-    const float M = warp_max(ms);
-    const float w = ms == -INFINITY ? 0.f : ex2f(ms - M);
-    const float den = warp_sum(fmaf(w, ls, 0.f));
-    if (lane < ns) S.swt[h][lane] = __fdiv_rn(w, den);
-  }
-  if (tid == 0) A.attn_tick[kvh] = 0u;
-  __threadfence();
-  CSync::sync();
-  for (int i = tid; i < HPG * kHD / 2; i += kNT) {
-    const int h = (2 * i) / kHD, d = (2 * i) % kHD;
-    float o0 = 0.f, o1 = 0.f;
-#pragma unroll 4
-    for (int s2 = 0; s2 < ns; ++s2) {
-      const float2 v = __ldcg(reinterpret_cast<const float2*>(hb + ((size_t)s2 * HPG + h) * kPartStride + 4 + d));
-      const float sw = S.swt[h][s2];
-      o0 = fmaf(sw, v.x, o0);
-      o1 = fmaf(sw, v.y, o1);
-    }
-    fw_store(out + i, (uint32_t)f2bits(bfround(o0)) | ((uint32_t)f2bits(bfround(o1)) << 16), flag);
-  }
+  attn_merge_slice<HPG>(A, H, S, hw, out, split, ns, flag, tid);
 }
 
 // ------------------------------------------------------------ producer
@@ -773,9 +822,19 @@ __device__ __forceinline__ void argmax_pair(float& bv, int& bi, float ov, int oi
 
 // ---------------------------------------------------------------- kernel
 template <int HPG>
-__global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant__ StepArgs A) {
+__global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant__ StepArgs Ap) {
   extern __shared__ __align__(128) unsigned char smem[];
   StepHdr& H = *reinterpret_cast<StepHdr*>(smem);
+  {
+    // the arguments into shared memory: the noinline phases read them through
+    // a reference, and a reference to the parameter itself is a generic load
+    // of the constant space (slow) where a shared one is a few cycles
+    uint32_t* dst = reinterpret_cast<uint32_t*>(smem + Ap.off_args);
+    const uint32_t* src = reinterpret_cast<const uint32_t*>(&Ap);
+    for (int i = threadIdx.x; i < (int)(sizeof(StepArgs) / 4); i += blockDim.x) dst[i] = src[i];
+    __syncthreads();
+  }
+  const StepArgs& A = *reinterpret_cast<const StepArgs*>(smem + Ap.off_args);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int G = (int)gridDim.x, v = (int)blockIdx.x;
   const int L = A.n_layers;
@@ -1040,6 +1099,8 @@ int step_make_plan(const StepShape& sh, int num_sms, int budget, StepPlan* plan)
   }
   const int ab = hpg == 1 ? attn_bytes<1>() : hpg == 2 ? attn_bytes<2>() : attn_bytes<4>();
   end = std::max(end, A.off_u + ab);
+  A.off_args = round128(end);
+  end = A.off_args + (int)sizeof(StepArgs);
   A.off_ring = round128(end);
   const int nslots = std::min(kMaxSlots, (budget - A.off_ring) / kSlotBytes);
   if (nslots < 2) return -1;

@@ -62,8 +62,7 @@ struct StepArgs {
   int cap, nq, nkv;
   float scale;        // 1 / sqrt(head_dim)
   float scale_log2e;  // scale * log2 e: scores in the base-2 domain
-  float* attn_part;     // [n_kv][max_splits][hpg][132]: m, l, pad, pad, unnormalised output
-  unsigned* attn_tick;  // [n_kv], zero between uses
+  uint64_t* attn_pw;  // split partials in flag words [n_kv][max_splits][hpg][130]: m, l, unnormalised output
   int max_splits;
   int* pos;  // device offset; += 1 at the end of the step
   int* hist;
@@ -75,6 +74,7 @@ struct StepArgs {
   int nsm;  // grid = one CTA per SM
   int slot_bytes, nslots;
   int off_aux, aux_stride, off_res, off_u, off_ring;
+  int off_args;  // this structure's copy in shared memory
   int* status;
 };
 
