@@ -46,7 +46,7 @@ constexpr int kThreads = kNT + 32;    // + the producer warp
 constexpr int kHD = 128;
 constexpr int kAT = 64;               // attention rows per tile (stage)
 constexpr int kRowsPerSplit = 256;    // up to this many cache rows: one attention split per KV head
-constexpr int kRowsPerSplitLong = 128;  // beyond: one split per this many rows (up to max_splits)
+constexpr int kRowsPerSplitLong = 64;  // beyond: one split per tile of rows (up to max_splits)
 constexpr int kMaxSplitsMerge = 32;   // splits one head's merge takes (one per lane)
 constexpr int kVOff = kAT * kHD * 2;  // V rows' offset inside a slot
 constexpr int kMaxSlots = 8;
