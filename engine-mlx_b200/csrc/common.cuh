@@ -190,6 +190,13 @@ __device__ __forceinline__ void mma_f16_16816(float (&d)[4], uint32_t a0, uint32
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// 2^x in one instruction (approximate, ~2 ulp; 0 for large negative x).
+__device__ __forceinline__ float ex2f(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // (v & mask) | magic in one LOP3.
 __device__ __forceinline__ uint32_t lop3_and_or(uint32_t v, uint32_t mask, uint32_t magic) {
   uint32_t r;

@@ -123,13 +123,6 @@ __device__ __forceinline__ bool fw_ok(uint64_t a, uint64_t b, unsigned flag) {
   return (unsigned)(a >> 32) == flag && (unsigned)(b >> 32) == flag;
 }
 
-// 2^x in one instruction (approximate, ~2 ulp; 0 for large negative x).
-__device__ __forceinline__ float ex2f(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-
 __device__ __forceinline__ bool aborted(StepHdr& H) { return *reinterpret_cast<volatile int*>(&H.abort_flag) != 0; }
 
 // Polls the two words at p (16-byte aligned) until both carry `flag`.  False
