@@ -358,8 +358,9 @@ int emx_qwen3_is_compiled(emx_qwen3* m, int* compiled);
 /* No reference counterpart (the reference's decode step is one traced MLX
  * closure, crates/serve/src/compiled.rs:79-287, whatever its kernels):
  * set_fused(m, 1) runs the whole decode step of a dense model on one GPU as
- * one persistent kernel (grid barriers between phases) instead of one kernel
- * per operation (the default).  It fails with EMX_ERR_INVALID when the model
+ * one persistent kernel whose phases hand off through flag words (the
+ * default wherever the model has such a plan); set_fused(m, 0) selects one
+ * kernel per operation.  Setting 1 fails with EMX_ERR_INVALID when the model
  * has no such plan (MoE, sharded, group size != 64, head_dim != 128, more
  * than 4 q heads per KV head). */
 int emx_qwen3_set_fused(emx_qwen3* m, int fused);
