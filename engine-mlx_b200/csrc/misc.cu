@@ -398,22 +398,42 @@ __global__ void moe_route_kernel(const bf16* logits, int E, int k, int normalize
   s = block_sum(s, red);
   for (int i = threadIdx.x; i < E; i += blockDim.x) pr[i] = bfround(__fdiv_rn(expf(bf2f(logits[i]) - m), s));
   __syncthreads();
-  if (threadIdx.x == 0) {
-    int sel[64];
-    float sw[64];
+  int sel[64];
+  float sw[64];
+  if (threadIdx.x < 32) {
+    // k rounds of an argmax over the probabilities by one warp: the largest
+    // value, the lowest index among equal ones (a NaN is never taken; with
+    // nothing to take, index 0), then that entry is removed -- the order a
+    // sequential scan for the first maximum gives
+    const int lane = threadIdx.x;
     for (int r = 0; r < k; ++r) {
-      int bi = -1;
       float bv = -INFINITY;
-      for (int i = 0; i < E; ++i)
-        if (pr[i] > bv || (bi < 0 && pr[i] == bv)) {
-          bv = pr[i];
+      int bi = E;  // none yet
+      for (int i = lane; i < E; i += 32) {
+        const float v = pr[i];
+        if (v > bv || (bi == E && v == bv)) {
+          bv = v;
           bi = i;
         }
-      if (bi < 0) bi = 0;
+      }
+#pragma unroll
+      for (int o = 16; o; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > bv || (ov == bv && oi < bi)) {
+          bv = ov;
+          bi = oi;
+        }
+      }
+      if (bi >= E) bi = 0;
       sel[r] = bi;
       sw[r] = pr[bi];
-      pr[bi] = -INFINITY;
+      __syncwarp();
+      if (lane == 0) pr[bi] = -INFINITY;
+      __syncwarp();
     }
+  }
+  if (threadIdx.x == 0) {
     if (normalize) {
       float sum = 0.f;
       for (int r = 0; r < k; ++r) sum = __fadd_rn(sum, sw[r]);
