@@ -66,16 +66,21 @@ int gemm_run(GemmCtx* c, const GemmArgs& a, cudaStream_t st) {
   t.y = a.y;
   t.res = a.res;
   t.yf = a.yf;
-  // Up to 128 rows (one row tile; group size 64): the GEMM dequantises inside
-  // the kernel, K split across CTAs to fill the machine.  Longer prompts
-  // amortise one dequantisation pass over their row tiles (measured: the
-  // in-kernel path is 27% faster at 128 rows, 10% slower at 512, where each
-  // of the 4 row tiles would dequantise the same weights).
+  // With the packed copy (group size 64) the GEMM dequantises inside the
+  // kernel up to kPackedMaxRows rows (K split across a cluster when the row
+  // tiles leave SMs idle): against a dequantisation pass into bf16 scratch +
+  // tc_gemm it measured 1.2-2.5x faster per GEMM from 256 to 2048 rows on the
+  // C3 shapes (gate|up at 2048 rows 131.6 -> 106.5 us; a whole 512-token
+  // prefill 6.31 -> 4.52 ms), while at 4096 / 8192 rows, where every row
+  // tile dequantises the same weights again, the prefill was 3% / 7% slower.
+  // Without it, up to 128 rows dequantise the MLX layout inside the kernel,
+  // longer prompts through the scratch pass.
+  constexpr int kPackedMaxRows = 2048;
   t.wq = a.w;
   t.ws = a.s;
   t.wb = a.b;
   t.bits = a.bits;
-  if (a.wp && a.gs == 64 && a.M <= 128) {
+  if (a.wp && a.gs == 64 && a.M <= kPackedMaxRows) {
     t.wp = a.wp;
     t.S = (a.K / 64 + 7) / 8;
     t.nrb = (a.N + 15) / 16;
