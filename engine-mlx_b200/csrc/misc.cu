@@ -312,54 +312,67 @@ __global__ void embed_kernel(const uint32_t* w, const bf16* s, const bf16* b, co
 
 // One warp per (token, head): heads [0, nq) are q, [nq, nq+nkv) are k (normed,
 // roped, written to the cache), [nq+nkv, nq+2nkv) are v (copied to the cache).
+// Lane l holds elements 4l..4l+3 (one 8-byte load and store); the RoPE
+// angles come from the (cos, sin) table when given (the same sincosf values).
 __global__ void prefill_qkv_kernel(const PrefillQkvArgs a) {
   const int lane = threadIdx.x & 31;
   const int items_per_tok = a.nq + 2 * a.nkv;
   const int item = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (item >= a.T * items_per_tok) return;
   const int t = item / items_per_tok, h = item % items_per_tok;
-  const int hd = a.hd;  // 128
+  constexpr int hd = 128;
   const bf16* src = a.qkv + (size_t)t * items_per_tok * hd + (size_t)h * hd;
   const int pos = a.offset + t;
+  const uint2 raw = *reinterpret_cast<const uint2*>(src + lane * 4);
   if (h >= a.nq + a.nkv) {
     const int kvh = h - a.nq - a.nkv;
-    bf16* dst = a.vc + ((size_t)kvh * a.cap + pos) * hd;
-    for (int d = lane; d < hd; d += 32) dst[d] = src[d];
+    *reinterpret_cast<uint2*>(a.vc + ((size_t)kvh * a.cap + pos) * hd + lane * 4) = raw;
     return;
   }
   const bool is_k = h >= a.nq;
   const bf16* nw = is_k ? a.k_norm : a.q_norm;
-  float v[4];
+  float v[4] = {__uint_as_float(raw.x << 16), __uint_as_float(raw.x & 0xffff0000u), __uint_as_float(raw.y << 16),
+                __uint_as_float(raw.y & 0xffff0000u)};
   float ss = 0.f;
 #pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    v[e] = bf2f(src[lane * 4 + e]);
-    ss = fmaf(v[e], v[e], ss);
-  }
+  for (int e = 0; e < 4; ++e) ss = fmaf(v[e], v[e], ss);
   ss = warp_sum(ss);
   const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)hd), a.eps)));
   float nv[4], pv[4];
+  if (nw) {
+    const uint2 wr = *reinterpret_cast<const uint2*>(nw + lane * 4);
+    const float wv[4] = {__uint_as_float(wr.x << 16), __uint_as_float(wr.x & 0xffff0000u),
+                         __uint_as_float(wr.y << 16), __uint_as_float(wr.y & 0xffff0000u)};
 #pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    const int d = lane * 4 + e;
-    nv[e] = nw ? bfround(__fmul_rn(bfround(__fmul_rn(v[e], inv)), bf2f(nw[d]))) : v[e];
+    for (int e = 0; e < 4; ++e) nv[e] = bfround(__fmul_rn(bfround(__fmul_rn(v[e], inv)), wv[e]));
+  } else {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) nv[e] = v[e];
   }
 #pragma unroll
   for (int e = 0; e < 4; ++e) pv[e] = __shfl_xor_sync(0xffffffffu, nv[e], 16);
   const float fp = (float)pos;
   bf16* dst = is_k ? a.kc + ((size_t)(h - a.nq) * a.cap + pos) * hd : a.q_out + ((size_t)h * a.T + t) * hd;
+  float o[4];
 #pragma unroll
   for (int e = 0; e < 4; ++e) {
     const int d = lane * 4 + e;
     const int i = d & (hd / 2 - 1);
-    const float th = __fmul_rn(fp, a.inv_freq[i]);
     float sn, cs;
-    sincosf(th, &sn, &cs);
-    float o;
-    if (d < hd / 2) o = __fsub_rn(__fmul_rn(nv[e], cs), __fmul_rn(pv[e], sn));
-    else o = __fadd_rn(__fmul_rn(pv[e], sn), __fmul_rn(nv[e], cs));
-    dst[d] = f2bf(o);
+    if (a.rope_cs) {
+      const float2 c2 = a.rope_cs[(size_t)pos * (hd / 2) + i];
+      cs = c2.x;
+      sn = c2.y;
+    } else {
+      sincosf(__fmul_rn(fp, a.inv_freq[i]), &sn, &cs);
+    }
+    if (d < hd / 2) o[e] = __fsub_rn(__fmul_rn(nv[e], cs), __fmul_rn(pv[e], sn));
+    else o[e] = __fadd_rn(__fmul_rn(pv[e], sn), __fmul_rn(nv[e], cs));
   }
+  uint2 out;
+  out.x = (uint32_t)f2bits(o[0]) | ((uint32_t)f2bits(o[1]) << 16);
+  out.y = (uint32_t)f2bits(o[2]) | ((uint32_t)f2bits(o[3]) << 16);
+  *reinterpret_cast<uint2*>(dst + lane * 4) = out;
 }
 
 __global__ void slice_update_kernel(bf16* cache, const bf16* upd, int nkv, int cap, int D, int offset,

@@ -52,6 +52,7 @@ struct PrefillQkvArgs {
   const bf16* k_norm;
   float eps;
   const float* inv_freq;
+  const float2* rope_cs;  // optional: (cos, sin) per [position][hd / 2], the same values as sincosf here
   int T, nq, nkv, hd;
   int offset;
   bf16* q_out;  // [nq, T, hd]

@@ -1070,6 +1070,7 @@ int prefill_impl(emx_qwen3* m, const int32_t* ids_dev, int T, bool attend_cache 
     pa.k_norm = lw.k_norm;
     pa.eps = c.eps;
     pa.inv_freq = m->inv_freq;
+    pa.rope_cs = m->rope_cs;
     pa.T = T;
     pa.nq = m->nq;
     pa.nkv = m->nkv;
