@@ -450,11 +450,15 @@ def run_engine(args, cfg, rank, world, dist):
         m.prefill_device(ids, args.prompt)
         m.reset()
         ctx.synchronize()
+        if args.profile_range:
+            torch.cuda.profiler.start()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(st)
         m.prefill_device(ids, args.prompt)
         e1.record(st)
         e1.synchronize()
+        if args.profile_range:
+            torch.cuda.profiler.stop()
         ms = e0.elapsed_time(e1)
         if rank == 0:
             print(json.dumps({"prefill_tokens": args.prompt, "ms": ms, "tok_s": args.prompt / (ms / 1000.0)}),
@@ -473,10 +477,18 @@ def run_engine(args, cfg, rank, world, dist):
                                   max_prefill=max(args.prompt, 128))
         m = emx.Qwen3(ctx, cfg)
         m.init_random(args.seed)
+        if args.per_op and m.fused:
+            m.fused = False
+        if args.eager:
+            m.compiled = False
         ids = ctx.put(np.random.default_rng(args.seed).integers(0, cfg.vocab, args.prompt).astype(np.int32))
         m.prefill_device(ids, args.prompt)
         m.decode_device(max(args.warmup, 3))
+        if args.profile_range:
+            torch.cuda.profiler.start()
         ms = timed_decode(m, ctx, st, torch, args.steps)
+        if args.profile_range:
+            torch.cuda.profiler.stop()
         if rank == 0:
             print(json.dumps({"decode_steps": args.steps, "ms_per_step": ms / args.steps,
                               "tok_s": args.steps / (ms / 1000.0), "launches_per_step": m.step_launches()}),
@@ -807,6 +819,9 @@ def main():
                     help="skip the tensor-parallel 32B-shape measurement added to every line")
     ap.add_argument("--no-moe", action="store_true",
                     help="skip the expert-parallel 30B-A3B-shape prefill + decode measurement added to every line")
+    ap.add_argument("--profile-range", action="store_true",
+                    help="with --kernel-only step / prefill: bracket the timed region with cudaProfilerStart / "
+                         "Stop (for ncu --profile-from-start off)")
     ap.add_argument("--kernel-only", nargs="?", const="gemv", default=None,
                     choices=["gemv", "gemm", "attn", "prefill", "c1", "step"],
                     help="time one kernel alone and print its roofline: the packed decode GEMV (gate|up shape, "

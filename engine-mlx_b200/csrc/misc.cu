@@ -465,6 +465,94 @@ __global__ void moe_route_kernel(const bf16* logits, int E, int k, int normalize
   }
 }
 
+// The same routing for up to 32 * EPL experts by one warp, everything in
+// registers: lane l holds experts l, l + 32, ...  The softmax sum follows
+// the 256-thread kernel's reduction exactly (a butterfly over each group of
+// 32 experts, then a butterfly over the eight group sums), so both kernels
+// give the same bits, and so does the selection (largest value, lowest
+// index among equal ones, per round).
+template <int EPL>
+__global__ void moe_route_warp_kernel(const bf16* logits, int E, int k, int normalize, int e_base, int e_local,
+                                      int* idx, float* w, int* n) {
+  pdl_trigger();
+  pdl_wait();
+  const int lane = threadIdx.x;
+  logits += (size_t)blockIdx.x * E;
+  idx += (size_t)blockIdx.x * k;
+  w += (size_t)blockIdx.x * k;
+  n += blockIdx.x;
+  float lg[EPL];
+  float m = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < EPL; ++j) {
+    const int i = lane + 32 * j;
+    lg[j] = i < E ? bf2f(logits[i]) : -INFINITY;
+    m = fmaxf(m, lg[j]);
+  }
+  m = warp_max(m);
+  float part = 0.f;  // lane j: the sum of group j
+#pragma unroll
+  for (int j = 0; j < EPL; ++j) {
+    const float e = lane + 32 * j < E ? expf(lg[j] - m) : 0.f;
+    const float t = warp_sum(e);
+    if (lane == j) part = t;
+  }
+  const float s = warp_sum(part);
+  float pr[EPL];
+#pragma unroll
+  for (int j = 0; j < EPL; ++j)
+    pr[j] = lane + 32 * j < E ? bfround(__fdiv_rn(expf(lg[j] - m), s)) : -INFINITY;
+  int sel[64];
+  float sw[64];
+  for (int r = 0; r < k; ++r) {
+    float bv = -INFINITY;
+    int bi = E;  // none yet
+#pragma unroll
+    for (int j = 0; j < EPL; ++j) {
+      const int i = lane + 32 * j;
+      if (i < E && (pr[j] > bv || (bi == E && pr[j] == bv))) {
+        bv = pr[j];
+        bi = i;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > bv || (ov == bv && oi < bi)) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    if (bi >= E) {  // nothing to take: index 0 and its value
+      bi = 0;
+      bv = __shfl_sync(0xffffffffu, pr[0], 0);
+    }
+    sel[r] = bi;
+    sw[r] = bv;
+#pragma unroll
+    for (int j = 0; j < EPL; ++j)
+      if (lane + 32 * j == bi) pr[j] = -INFINITY;
+  }
+  if (lane == 0) {
+    if (normalize) {
+      float sum = 0.f;
+      for (int r = 0; r < k; ++r) sum = __fadd_rn(sum, sw[r]);
+      if (sum > 1e-20f)
+        for (int r = 0; r < k; ++r) sw[r] = __fdiv_rn(sw[r], sum);
+    }
+    int j = 0;
+    for (int r = 0; r < k; ++r) {
+      if (sel[r] >= e_base && sel[r] < e_base + e_local) {
+        idx[j] = sel[r] - e_base;
+        w[j] = sw[r];
+        ++j;
+      }
+    }
+    *n = j;
+  }
+}
+
 // Batched MoE prefill, grouping: the (token, slot) pairs of each local
 // expert get consecutive positions, experts in order and, inside an expert,
 // tokens in order (deterministic); perm [T][k] holds each pair's position,
@@ -609,6 +697,8 @@ cudaError_t k_moe_route(const bf16* logits, int E, int k, int normalize, int e_b
   if (E <= 0 || E > 1024 || k <= 0 || k > 64 || k > E) return cudaErrorInvalidValue;
   void* args[] = {(void*)&logits, (void*)&E, (void*)&k, (void*)&normalize, (void*)&e_base, (void*)&e_local,
                   (void*)&idx, (void*)&w, (void*)&n};
+  if (E <= 128) return launch_pdl((const void*)moe_route_warp_kernel<4>, dim3(1), dim3(32), args, st, pdl);
+  if (E <= 256) return launch_pdl((const void*)moe_route_warp_kernel<8>, dim3(1), dim3(32), args, st, pdl);
   return launch_pdl((const void*)moe_route_kernel, dim3(1), dim3(256), args, st, pdl);
 }
 
@@ -616,7 +706,12 @@ cudaError_t k_moe_route_batch(const bf16* logits, int T, int E, int k, int norma
                               int* idx, float* w, int* n, cudaStream_t st) {
   if (T <= 0) return cudaSuccess;
   if (E <= 0 || E > 1024 || k <= 0 || k > 64 || k > E) return cudaErrorInvalidValue;
-  moe_route_kernel<<<T, 256, 0, st>>>(logits, E, k, normalize, e_base, e_local, idx, w, n);
+  if (E <= 128)
+    moe_route_warp_kernel<4><<<T, 32, 0, st>>>(logits, E, k, normalize, e_base, e_local, idx, w, n);
+  else if (E <= 256)
+    moe_route_warp_kernel<8><<<T, 32, 0, st>>>(logits, E, k, normalize, e_base, e_local, idx, w, n);
+  else
+    moe_route_kernel<<<T, 256, 0, st>>>(logits, E, k, normalize, e_base, e_local, idx, w, n);
   return cudaGetLastError();
 }
 
