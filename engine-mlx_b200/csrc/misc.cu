@@ -9,6 +9,7 @@
 // (blas.rs:17-31), argmax (array.rs:6-10), softmax_axis (elementwise.rs:68-72),
 // take/embed (core.rs:5-14), slice_update / scatter_single (slice.rs:78-115).
 #include "misc.cuh"
+#include "moe_route.cuh"
 
 #include <algorithm>
 
@@ -465,92 +466,14 @@ __global__ void moe_route_kernel(const bf16* logits, int E, int k, int normalize
   }
 }
 
-// The same routing for up to 32 * EPL experts by one warp, everything in
-// registers: lane l holds experts l, l + 32, ...  The softmax sum follows
-// the 256-thread kernel's reduction exactly (a butterfly over each group of
-// 32 experts, then a butterfly over the eight group sums), so both kernels
-// give the same bits, and so does the selection (largest value, lowest
-// index among equal ones, per round).
+// The routing for up to 32 * EPL experts by one warp (route_warp).
 template <int EPL>
 __global__ void moe_route_warp_kernel(const bf16* logits, int E, int k, int normalize, int e_base, int e_local,
                                       int* idx, float* w, int* n) {
   pdl_trigger();
   pdl_wait();
-  const int lane = threadIdx.x;
-  logits += (size_t)blockIdx.x * E;
-  idx += (size_t)blockIdx.x * k;
-  w += (size_t)blockIdx.x * k;
-  n += blockIdx.x;
-  float lg[EPL];
-  float m = -INFINITY;
-#pragma unroll
-  for (int j = 0; j < EPL; ++j) {
-    const int i = lane + 32 * j;
-    lg[j] = i < E ? bf2f(logits[i]) : -INFINITY;
-    m = fmaxf(m, lg[j]);
-  }
-  m = warp_max(m);
-  float part = 0.f;  // lane j: the sum of group j
-#pragma unroll
-  for (int j = 0; j < EPL; ++j) {
-    const float e = lane + 32 * j < E ? expf(lg[j] - m) : 0.f;
-    const float t = warp_sum(e);
-    if (lane == j) part = t;
-  }
-  const float s = warp_sum(part);
-  float pr[EPL];
-#pragma unroll
-  for (int j = 0; j < EPL; ++j)
-    pr[j] = lane + 32 * j < E ? bfround(__fdiv_rn(expf(lg[j] - m), s)) : -INFINITY;
-  int sel[64];
-  float sw[64];
-  for (int r = 0; r < k; ++r) {
-    float bv = -INFINITY;
-    int bi = E;  // none yet
-#pragma unroll
-    for (int j = 0; j < EPL; ++j) {
-      const int i = lane + 32 * j;
-      if (i < E && (pr[j] > bv || (bi == E && pr[j] == bv))) {
-        bv = pr[j];
-        bi = i;
-      }
-    }
-#pragma unroll
-    for (int o = 16; o; o >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-      if (ov > bv || (ov == bv && oi < bi)) {
-        bv = ov;
-        bi = oi;
-      }
-    }
-    if (bi >= E) {  // nothing to take: index 0 and its value
-      bi = 0;
-      bv = __shfl_sync(0xffffffffu, pr[0], 0);
-    }
-    sel[r] = bi;
-    sw[r] = bv;
-#pragma unroll
-    for (int j = 0; j < EPL; ++j)
-      if (lane + 32 * j == bi) pr[j] = -INFINITY;
-  }
-  if (lane == 0) {
-    if (normalize) {
-      float sum = 0.f;
-      for (int r = 0; r < k; ++r) sum = __fadd_rn(sum, sw[r]);
-      if (sum > 1e-20f)
-        for (int r = 0; r < k; ++r) sw[r] = __fdiv_rn(sw[r], sum);
-    }
-    int j = 0;
-    for (int r = 0; r < k; ++r) {
-      if (sel[r] >= e_base && sel[r] < e_base + e_local) {
-        idx[j] = sel[r] - e_base;
-        w[j] = sw[r];
-        ++j;
-      }
-    }
-    *n = j;
-  }
+  route_warp<EPL>(logits + (size_t)blockIdx.x * E, false, E, k, normalize, e_base, e_local,
+                  idx + (size_t)blockIdx.x * k, w + (size_t)blockIdx.x * k, n + blockIdx.x);
 }
 
 // Batched MoE prefill, grouping: the (token, slot) pairs of each local

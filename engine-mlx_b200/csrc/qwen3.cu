@@ -1478,6 +1478,10 @@ int emx_qwen3_reset(emx_qwen3* m) {
   Q_REQUIRE(m, "emx_qwen3_reset: null model");
   m->offset = 0;
   EMX_CHECK_CUDA(cudaMemsetAsync(m->state, 0, sizeof(int) * 64, m->ctx->stream), "reset");
+  // last-CTA tickets back to zero (a chain that gave up on a wait may have
+  // left one part-way)
+  EMX_CHECK_CUDA(cudaMemsetAsync(m->am_ticket, 0, sizeof(unsigned) * 16, m->ctx->stream), "reset");
+  EMX_CHECK_CUDA(cudaMemsetAsync(m->attn_ticket, 0, sizeof(unsigned) * m->nkv, m->ctx->stream), "reset");
   const int rc = clear_step_words(m);  // also ends a persistent step that gave up on a wait
   if (rc) return rc;
   return ctx_sync_check(m->ctx, "emx_qwen3_reset");
