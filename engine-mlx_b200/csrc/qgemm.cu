@@ -73,8 +73,10 @@ int gemm_run(GemmCtx* c, const GemmArgs& a, cudaStream_t st) {
   // C3 shapes (gate|up at 2048 rows 131.6 -> 106.5 us; a whole 512-token
   // prefill 6.31 -> 4.52 ms), while at 4096 / 8192 rows, where every row
   // tile dequantises the same weights again, the prefill was 3% / 7% slower.
-  // Without it, up to 128 rows dequantise the MLX layout inside the kernel,
-  // longer prompts through the scratch pass.
+  // Without it, up to 256 rows dequantise the MLX layout inside the kernel
+  // (against the scratch pass: N=6144 K=2048 at 256 rows 29.3 -> 23.0 us,
+  // a tie at 512, the scratch pass ahead from 1024), longer inputs through
+  // the scratch pass.
   constexpr int kPackedMaxRows = 2048;
   t.wq = a.w;
   t.ws = a.s;
@@ -89,7 +91,7 @@ int gemm_run(GemmCtx* c, const GemmArgs& a, cudaStream_t st) {
       return ce == cudaSuccess ? 0 : (int)ce;
     }
   }
-  if (a.gs == 64 && a.M <= 128 && tc_qgemm_supported(t)) {
+  if (a.gs == 64 && a.M <= 256 && tc_qgemm_supported(t)) {
     const cudaError_t ce = tc_qgemm_launch(t, c->num_sms, st);
     return ce == cudaSuccess ? 0 : (int)ce;
   }
