@@ -99,7 +99,9 @@ PREFILL_LINEARS = [(128, 6144, 2048, 4), (100, 2048, 6144, 4), (77, 4096, 2048, 
                    (16, 12288, 2048, 4), (3, 512, 1024, 8)]
 
 
-@pytest.mark.parametrize("M,N,K,bits", PREFILL_LINEARS)
+# the MLX-layout entry dequantises inside the kernel up to 256 rows (two row
+# tiles), beyond that through bf16 scratch
+@pytest.mark.parametrize("M,N,K,bits", PREFILL_LINEARS + [(200, 2048, 6144, 4), (256, 4096, 2048, 8)])
 def test_prefill_linear_shapes(ctx, M, N, K, bits):
     q = _linear(11, f"prefill.{N}x{K}.{bits}", N, K, 64, bits)
     rng = np.random.default_rng(M + N)
@@ -110,10 +112,12 @@ def test_prefill_linear_shapes(ctx, M, N, K, bits):
     assert_close(y.read(np.uint16, (M, N)), ref, what=f"prefill linear {M}x{N}x{K} int{bits}")
 
 
-@pytest.mark.parametrize("M,N,K,bits", PREFILL_LINEARS + [(200, 1024, 2048, 4), (1, 2048, 2048, 8)])
+@pytest.mark.parametrize("M,N,K,bits", PREFILL_LINEARS + [(200, 1024, 2048, 4), (1, 2048, 2048, 8),
+                                                      (600, 2048, 2048, 4), (1100, 1024, 2048, 8)])
 def test_prefill_linear_packed(ctx, M, N, K, bits):
     """The prefill GEMM over the packed decode layout (emx_qpack) against the
-    oracle's MLX-layout matmul of the same tensor."""
+    oracle's MLX-layout matmul of the same tensor; the model takes it up to
+    2048 rows (256-token row tiles above 128, ragged ones included)."""
     q = _linear(11, f"prefill.{N}x{K}.{bits}", N, K, 64, bits)
     rng = np.random.default_rng(M + N)
     x = oracle.to_bf16(rng.standard_normal((M, K)).astype(np.float32))
