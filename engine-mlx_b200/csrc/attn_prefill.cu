@@ -235,15 +235,22 @@ __global__ void __launch_bounds__(kThreads) attn_prefill_kernel(const AttnPrefil
 //                        steps) into one of two tensor-memory S buffers,
 //                        issued before O += P_{j-1}.V_{j-1} so that the tensor
 //                        pipe computes the next scores while the softmax
-//                        warps work; P from shared memory, V as an MN-major
-//                        operand; owns the 512-column TMEM allocation;
+//                        warps work; P is operand A straight from tensor
+//                        memory (it overwrites its own tile's S), V an
+//                        MN-major operand; owns the 512-column TMEM
+//                        allocation;
 //   warps 2-9            softmax: two threads per query row (warps w and w+4
 //                        share a TMEM lane quadrant), each with 64 of the 128
 //                        columns; it reads its S half-row with tcgen05.ld,
 //                        masks (the diagonal tile only), keeps the running max in
 //                        the log2 domain and writes P as bf16 hi + lo parts
 //                        (P.V keeps ~16 significant bits of each
-//                        probability) to shared memory.  The max used for the
+//                        probability) over the S buffer it just read, so
+//                        the two S buffers double-buffer P as well: tile
+//                        j's exponentials run while O += P_{j-1}.V_{j-1}
+//                        does (the MMAs execute in issue order, so S_{j+2}
+//                        lands in that buffer only after P_j was read).
+//                        The max used for the
 //                        exponentials only moves when the tile max exceeds it
 //                        by more than 8 (O and l are then rescaled in place),
 //                        so P <= 2^8 and the final O / l is exact whatever
@@ -252,13 +259,12 @@ constexpr int kTBM = 128, kTBN = 128;
 constexpr int kTcThreads = 320;
 constexpr int kBlk = kTBM * 64 * 2;  // 128 rows x 64 columns (128 B rows, swizzled): 16 KB
 constexpr int kTileB = 2 * kBlk;     // 128 rows x 128 columns
-constexpr int kOffK = kTileB;        // Q | (K V) x 2 | P hi | P lo | barriers
-constexpr int kOffP = kOffK + 4 * kTileB;
-constexpr int kOffBar = kOffP + 2 * kTileB;
+constexpr int kOffK = kTileB;        // Q | (K V) x 2 | barriers
+constexpr int kOffBar = kOffK + 4 * kTileB;
 constexpr int kOffX = kOffBar + 128;  // softmax exchange: [2 halves][128 rows] floats
 constexpr int kTcSmem = 1024 + kOffX + 2 * kTBM * 4;
 constexpr float kRescale = 8.0f;     // log2 growth allowed before O is rescaled
-constexpr uint32_t kTmemCols = 512;  // S0 [0,128), O [128,256), S1 [256,384)
+constexpr uint32_t kTmemCols = 512;  // S0 [0,128), O [128,256), S1 [256,384); P_j over S_{j&1}: hi [0,64), lo [64,128)
 
 __device__ __forceinline__ uint64_t desc_kmajor(const void* p) {
   const uint64_t a = (smem_u32(p) >> 4) & 0x3FFFu;
@@ -291,6 +297,15 @@ __device__ __forceinline__ void umma(uint32_t d, uint64_t a, uint64_t b, uint32_
       "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
       "l"(a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
+// The same with operand A in tensor memory (lane = row, two bf16 of K per column).
+__device__ __forceinline__ void umma_ta(uint32_t d, uint32_t a_tmem, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d),
+      "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc)
       : "memory");
 }
 
@@ -335,6 +350,18 @@ __device__ __forceinline__ void tst32(uint32_t taddr, const float (&v)[32]) {
       : "memory");
 }
 
+__device__ __forceinline__ void tst32u(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+      "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+      "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+
 // 2^x by the hardware's base-2 exponential (softmax weights; their bf16
 // hi + lo split keeps ~16 bits, well inside its accuracy).
 __device__ __forceinline__ float ex2_approx(float x) {
@@ -352,7 +379,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   unsigned char* sQ = smem;
-  unsigned char* sP = smem + kOffP;  // P hi tile, then P lo tile
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + kOffBar);
   uint64_t* q_full = bar + 0;
   uint64_t* kv_full = bar + 1;   // [2] per K/V stage
@@ -442,12 +468,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       tfence_after();
       const unsigned char* V = smem + kOffK + b * 2 * kTileB + kTileB;
 #pragma unroll
-      for (int part = 0; part < 2; ++part) {
-        const unsigned char* P = sP + part * kTileB;
+      for (int part = 0; part < 2; ++part) {  // P hi, then P lo, in S buffer b
 #pragma unroll
-        for (int k = 0; k < 8; ++k)  // 16 keys per step: P block k/4 (+32 B), V rows 16k.. (+2 KB)
-          umma(tmem + 128, desc_kmajor(P + (k >> 2) * kBlk) + 2 * (k & 3), desc_mnmajor(V + k * 2048), id_pv,
-               (j > 0 || part > 0 || k > 0) ? 1u : 0u);
+        for (int k = 0; k < 8; ++k)  // 16 keys per step: 8 P columns, V rows 16k.. (+2 KB)
+          umma_ta(tmem + 128, tmem + s_col(b) + (uint32_t)(part * 64 + k * 8), desc_mnmajor(V + k * 2048), id_pv,
+                  (j > 0 || part > 0 || k > 0) ? 1u : 0u);
       }
       umma_commit(&kv_empty[b]);
       umma_commit(pv_done);
@@ -519,13 +544,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         break;
       }
       mx = fmaxf(mx, xch[(hf ^ 1) * kTBM + r]);
-      pair_sync();  // both read before either writes the next tile's max
-      // the O update of tile j-1 has read P and written O before either is touched
-      if (j > 0) ok = mbar_wait_bounded(pv_done, (uint32_t)((j - 1) & 1), status) && ok;
-      tfence_after();
+      pair_sync();  // both read before either writes the next tile's max (and both S halves are out)
       if (mx != -INFINITY && mx > m_used + kRescale) {
         const float alpha = m_used == -INFINITY ? 0.f : ex2_approx(m_used - mx);
         if (j > 0 && m_used != -INFINITY) {
+          // the O update of tile j-1 has written O before it is rescaled
+          ok = mbar_wait_bounded(pv_done, (uint32_t)((j - 1) & 1), status) && ok;
+          tfence_after();
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
             float v[32];
@@ -540,15 +565,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         l *= alpha;
         m_used = mx;
       }
-      // P = exp2(s - m_used) as bf16 hi + lo: keys [64 hf, 64 hf + 64) of row
-      // r are swizzle block hf of the K-major P tiles
-      unsigned char* Pr = sP + hf * kBlk + (r >> 3) * 1024 + (r & 7) * 128;
+      // P = exp2(s - m_used) as bf16 hi + lo over this tile's S buffer: keys
+      // [64 hf, 64 hf + 64) of row r in columns 32 hf.. (hi) and 64 + 32 hf..
+      // (lo), two keys per column
+      {
+        uint32_t hi[32], lo[32];
 #pragma unroll
-      for (int ch = 0; ch < 8; ++ch) {  // 16-byte chunk: 8 keys
-        uint32_t hi[4], lo[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int c = ch * 8 + 2 * e;
+        for (int e = 0; e < 32; ++e) {
+          const int c = 2 * e;
           const float p0 = s[c] == -INFINITY ? 0.f : ex2_approx(s[c] - m_used);
           const float p1 = s[c + 1] == -INFINITY ? 0.f : ex2_approx(s[c + 1] - m_used);
           l += p0;
@@ -557,11 +581,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           hi[e] = pack_bf16(h0, h1);
           lo[e] = pack_bf16(p0 - h0, p1 - h1);
         }
-        const int off = ((ch ^ (r & 7)) << 4);
-        *reinterpret_cast<uint4*>(Pr + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-        *reinterpret_cast<uint4*>(Pr + kTileB + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+        const uint32_t tp = tmem + ((uint32_t)(quad * 32) << 16) + s_col(b) + (uint32_t)(hf * 32);
+        tst32u(tp, hi);
+        tst32u(tp + 64, lo);
+        tmem_wait_st_();
       }
-      fence_proxy_async();
+      // O += P_{j-1}.V_{j-1} has finished (it is normally done by now): one
+      // completion of pv_done per tile keeps its phases in step
+      if (j > 0) ok = mbar_wait_bounded(pv_done, (uint32_t)((j - 1) & 1), status) && ok;
       tfence_before();
       mbar_arrive(p_full);
     }
