@@ -405,6 +405,8 @@ template <int HPG>
 __device__ __noinline__ void attn_merge_slice(const StepArgs& A, StepHdr& H, AttnSm<HPG>& S, const uint64_t* hw,
                                               uint64_t* out, int split, int ns, unsigned flag, int tid) {
   constexpr int W = HPG * kHD / 2;
+  // (m, l) of every (split, q head), then at most W / ns + 1 words per split
+  static_assert(kMaxSplitsMerge * HPG + W + kMaxSplitsMerge <= 2 * kNT, "two load pairs per thread at most");
   const int warp = tid >> 5, lane = tid & 31;
   const int w0 = split * W / ns, w1 = (split + 1) * W / ns;
   const int nml = ns * HPG, tot = nml + (w1 - w0) * ns;  // <= 2 * kNT
