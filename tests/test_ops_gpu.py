@@ -266,6 +266,27 @@ def test_softmax_and_route(ctx):
     assert np.allclose(w.read(np.float32, (8,)), OPS["route_w"], rtol=1e-5, atol=1e-7)
 
 
+@pytest.mark.parametrize("E", [128, 256, 300])
+def test_route_ties_take_the_lowest_index(ctx, E):
+    """Experts with equal router probabilities are taken lowest index first
+    (the oracle's stable top-k), for the one-warp routing (up to 256
+    experts) and the block one (more)."""
+    x = np.full(E, oracle.to_bf16(np.array([-10.0], np.float32))[0], np.uint16)
+    hi = oracle.to_bf16(np.array([3.0], np.float32))[0]
+    mid = oracle.to_bf16(np.array([2.0], np.float32))[0]
+    for i in (3, 7, 40, 64, 100):
+        x[i] = hi
+    for i in (1, 90, E - 1):
+        x[i] = mid
+    p = oracle.softmax_bf16(x)
+    want_idx, want_w = oracle.topk((p.astype(np.uint32) << 16).view(np.float32), 8, True)
+    idx, w = ctx.moe_route(ctx.put(x), E, 8, True)
+    got_idx = idx.read(np.int32, (8,))
+    assert np.array_equal(got_idx, want_idx), (got_idx, want_idx)
+    assert list(got_idx) == [3, 7, 40, 64, 100, 1, 90, E - 1]
+    assert np.allclose(w.read(np.float32, (8,)), want_w, rtol=1e-5, atol=1e-7)
+
+
 # ----------------------------------------------------------------- attention
 @pytest.mark.parametrize("tnd", [False, True])
 def test_sdpa_causal(ctx, tnd):
