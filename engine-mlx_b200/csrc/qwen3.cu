@@ -398,7 +398,7 @@ int clear_step_words(emx_qwen3* m) {
 }
 
 // Plans the persistent decode step when the model qualifies (dense, one GPU,
-// group size 64 everywhere, head_dim 128, 1/2/4 q heads per KV head, one
+// group size 64 everywhere, head_dim 128, 1/2/4/8 q heads per KV head, one
 // norm group) and sets up its argument block and exchange words; it is then
 // the default decode path (sampling still runs the per-kernel chain).
 int setup_step(emx_qwen3* m) {

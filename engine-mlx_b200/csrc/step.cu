@@ -72,6 +72,12 @@ struct StepHdr {
   float2 rcs[kHD / 2];  // (cos, sin) of this step's RoPE angles
 };
 
+// Load pairs per thread of a split merge: (m, l) of every (split, q head),
+// then at most W / ns + 1 output words from each split (W = 64 HPG).
+__host__ __device__ constexpr int merge_loads(int hpg) {
+  return (kMaxSplitsMerge * hpg + hpg * kHD / 2 + kMaxSplitsMerge + kNT - 1) / kNT;
+}
+
 template <int HPG>
 struct AttnSm {
   float qs[HPG][kHD];      // q * scale * log2 e
@@ -79,7 +85,7 @@ struct AttnSm {
   float wm[kCons][HPG], wl[kCons][HPG];  // per-warp running max and sum
   float4 sacc[kCons][HPG][32];           // per-warp partial outputs, lane l = dims 4l..4l+3
   float swt[HPG][kMaxSplitsMerge];  // merge weights of a head's splits
-  float2 mraw[2 * kNT];             // the merge's inputs: (m, l) pairs, then partial output pairs
+  float2 mraw[merge_loads(HPG) * kNT];  // the merge's inputs: (m, l) pairs, then partial output pairs
   bf16 knew[kHD];
   bf16 vnew[kHD];
 };
@@ -399,34 +405,37 @@ __device__ void epilogue_fw(const PGeom& geo, const PgSmem& sm, int lb0, int lb1
 // before it waits here, so the waits end once the slowest split's words
 // land; no ticket, no fence.  Arithmetic: weights 2^(m_s - M) / sum_s
 // 2^(m_s - M) l_s (M the max), then the weighted partials summed in split
-// order.  One thread holds at most two load pairs, all issued before any
-// is checked.
+// order.  A thread holds at most merge_loads(HPG) load pairs, all issued
+// before any is checked.
 template <int HPG>
 __device__ __noinline__ void attn_merge_slice(const StepArgs& A, StepHdr& H, AttnSm<HPG>& S, const uint64_t* hw,
                                               uint64_t* out, int split, int ns, unsigned flag, int tid) {
   constexpr int W = HPG * kHD / 2;
-  // (m, l) of every (split, q head), then at most W / ns + 1 words per split
-  static_assert(kMaxSplitsMerge * HPG + W + kMaxSplitsMerge <= 2 * kNT, "two load pairs per thread at most");
+  constexpr int NL = merge_loads(HPG);
   const int warp = tid >> 5, lane = tid & 31;
   const int w0 = split * W / ns, w1 = (split + 1) * W / ns;
-  const int nml = ns * HPG, tot = nml + (w1 - w0) * ns;  // <= 2 * kNT
+  const int nml = ns * HPG, tot = nml + (w1 - w0) * ns;  // <= NL * kNT
   auto addr = [&](int t) -> const uint64_t* {
     if (t < nml) return hw + (size_t)t * kPartWords;  // t = split * HPG + q head
     const int u = t - nml, i = w0 + u / ns, s2 = u % ns;
     const int h = (2 * i) / kHD, d = (2 * i) % kHD;
     return hw + ((size_t)s2 * HPG + h) * kPartWords + 2 + d;
   };
-  const int ta = tid, tb = tid + kNT;
-  uint64_t a0 = 0, a1 = 0, b0 = 0, b1 = 0;
-  if (ta < tot) fw_load2(addr(ta), a0, a1);
-  if (tb < tot) fw_load2(addr(tb), b0, b1);
-  if (ta < tot) {
-    if (!fw_ok(a0, a1, flag) && !fw_wait2(addr(ta), flag, a0, a1, A, H)) a0 = a1 = 0;
-    S.mraw[ta] = make_float2(__uint_as_float((uint32_t)a0), __uint_as_float((uint32_t)a1));
+  uint64_t v0[NL], v1[NL];
+#pragma unroll
+  for (int q = 0; q < NL; ++q) {
+    const int t = tid + q * kNT;
+    v0[q] = v1[q] = 0;
+    if (t < tot) fw_load2(addr(t), v0[q], v1[q]);
   }
-  if (tb < tot) {
-    if (!fw_ok(b0, b1, flag) && !fw_wait2(addr(tb), flag, b0, b1, A, H)) b0 = b1 = 0;
-    S.mraw[tb] = make_float2(__uint_as_float((uint32_t)b0), __uint_as_float((uint32_t)b1));
+#pragma unroll
+  for (int q = 0; q < NL; ++q) {
+    const int t = tid + q * kNT;
+    if (t < tot) {
+      uint64_t u0 = v0[q], u1 = v1[q];  // scalars: the wait takes them by reference
+      if (!fw_ok(u0, u1, flag) && !fw_wait2(addr(t), flag, u0, u1, A, H)) u0 = u1 = 0;
+      S.mraw[t] = make_float2(__uint_as_float((uint32_t)u0), __uint_as_float((uint32_t)u1));
+    }
   }
   CSync::sync();
   for (int h = warp; h < HPG; h += kCons) {
@@ -1042,6 +1051,7 @@ const void* kernel_for(int hpg) {
     case 1: return reinterpret_cast<const void*>(step_kernel<1>);
     case 2: return reinterpret_cast<const void*>(step_kernel<2>);
     case 4: return reinterpret_cast<const void*>(step_kernel<4>);
+    case 8: return reinterpret_cast<const void*>(step_kernel<8>);
     default: return nullptr;
   }
 }
@@ -1060,7 +1070,7 @@ int step_make_plan(const StepShape& sh, int num_sms, int budget, StepPlan* plan)
   static_assert(sizeof(StepArgs) <= 4096, "step arguments exceed the kernel parameter space");
   if (sh.gs != 64 || sh.hd != kHD || sh.nkv <= 0 || sh.nq % sh.nkv != 0 || num_sms <= 0) return -1;
   const int hpg = sh.nq / sh.nkv;
-  if (hpg != 1 && hpg != 2 && hpg != 4) return -1;
+  if (hpg != 1 && hpg != 2 && hpg != 4 && hpg != 8) return -1;
   if (sh.H % 64 != 0 || sh.I % 64 != 0) return -1;
   StepPlan P{};
   StepArgs& A = P.tmpl;
@@ -1092,7 +1102,7 @@ int step_make_plan(const StepShape& sh, int num_sms, int budget, StepPlan* plan)
     end = std::max(end, pgeom_layout(A.geo[m], 64, A.off_u));
     A.bits[m] = bits;
   }
-  const int ab = hpg == 1 ? attn_bytes<1>() : hpg == 2 ? attn_bytes<2>() : attn_bytes<4>();
+  const int ab = hpg == 1 ? attn_bytes<1>() : hpg == 2 ? attn_bytes<2>() : hpg == 4 ? attn_bytes<4>() : attn_bytes<8>();
   end = std::max(end, A.off_u + ab);
   A.off_args = round128(end);
   end = A.off_args + (int)sizeof(StepArgs);

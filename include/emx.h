@@ -362,7 +362,7 @@ int emx_qwen3_is_compiled(emx_qwen3* m, int* compiled);
  * default wherever the model has such a plan); set_fused(m, 0) selects one
  * kernel per operation.  Setting 1 fails with EMX_ERR_INVALID when the model
  * has no such plan (MoE, sharded, group size != 64, head_dim != 128, more
- * than 4 q heads per KV head). */
+ * than 8 q heads per KV head). */
 int emx_qwen3_set_fused(emx_qwen3* m, int fused);
 int emx_qwen3_is_fused(emx_qwen3* m, int* fused);
 int emx_qwen3_step_launches(emx_qwen3* m, int* n);
