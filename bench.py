@@ -408,6 +408,7 @@ def moe_c4(args, rank, world, dist, torch, hbm, steps=32, prompt=1024):
         t = torch.tensor([ms, pre_ms], device=f"cuda:{dev}")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms, pre_ms = float(t[0].item()), float(t[1].item())
+    path = "persistent step (one launch per token)" if m.fused else "kernel chain"
     ids.free()
     m.close()
     if comm is not None:
@@ -419,7 +420,7 @@ def moe_c4(args, rank, world, dist, torch, hbm, steps=32, prompt=1024):
     return {"model": "c4 (Qwen3-30B-A3B shape, 128 experts top-8, int4 gs64, random-init)",
             "parallelism": f"expert parallel x{world}", "prefill_tokens": prompt,
             "prefill_tok_s": prompt / (pre_ms / 1000.0), "prefill_ms": pre_ms,
-            "decode_tok_s": steps / (ms / 1000.0), "ms_per_step": ms / steps, "steps": steps,
+            "decode_tok_s": steps / (ms / 1000.0), "ms_per_step": ms / steps, "steps": steps, "decode_path": path,
             "step_roofline": {"bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s", "frac": ach / hbm,
                               "scope": "per GPU: attention + router + the top-8 experts' weights, 1/world",
                               "bytes_per_step": per_gpu}}

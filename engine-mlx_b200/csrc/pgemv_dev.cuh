@@ -45,6 +45,8 @@ struct PGeom {
   int nw_bytes;  // room for the norm weights (fetched before the wait)
   unsigned long long lbt_magic;  // ceil(2^32 / (halves * S)): tile -> logical block
   unsigned long long lps_magic;  // ceil(2^32 / (slot rows / 16)): logical block -> x slot
+  int xsl_mod;  // 0: slots of consecutive blocks; else blocks interleave the slots (x slot = block % xsl_mod,
+                // read by pg_stage<..., true>)
   int off_x, off_nw, off_zero, off_xs, off_red, off_buf;
 };
 
@@ -86,6 +88,7 @@ inline void pgeom_make(PGeom* g, int K, int bits, int gs, int epi, int lb_total,
   const unsigned long long lbt = (unsigned long long)g->halves * g->S;
   g->lbt_magic = (0x100000000ull + lbt - 1) / lbt;
   g->lps_magic = 0;
+  g->xsl_mod = 0;
 }
 
 // Barrier over the threads that take part in a phase: the whole CTA, or the
@@ -341,9 +344,9 @@ __device__ __forceinline__ void pg_pad(const PGeom& geo, const PgSmem& sm, int t
   }
 }
 
-// The staged bf16 source of x slots [0, nslots) (chunk c of a slot staged
-// by thread c % nthr), max |x| per thread in `mx`: one reduction fixes the
-// scale, then each thread converts the chunks it staged to the fp16 layout.
+// The staged bf16 source of x slots [0, nslots) (by any of the threads: the
+// reduction's barrier orders it), max |x| per thread in `mx`: one reduction
+// fixes the scale, then the threads convert the chunks to the fp16 layout.
 template <int GS, class Sync>
 __device__ __forceinline__ void pg_convert_staged(const PGeom& geo, const PgSmem& sm, int nslots, float mx,
                                                   float* scratch, float* xsc, int tid, int nthr) {
@@ -351,21 +354,23 @@ __device__ __forceinline__ void pg_convert_staged(const PGeom& geo, const PgSmem
   const int e = pg_scale_exp(r.y);
   const float sc = pg_pow2(-e);
   if (tid == 0) *xsc = pg_pow2(e);
-  const int nch = geo.K / 8;
-  for (int slot = 0; slot < nslots; ++slot) {
+  // all slots' chunks in one sweep (K is whole groups, so a group's chunks
+  // stay in consecutive lanes)
+  const int nch = geo.K / 8, tot = nslots * nch;
 #pragma unroll 1
-    for (int it = 0; it * nthr < nch; ++it) {
-      const int c = it * nthr + tid;
-      const bool valid = c < nch;
-      float v[8];
-      if (valid) {
-        unpack8f(*reinterpret_cast<const uint4*>(pg_xchunk<GS>(geo, sm, slot, c)), v);
-      } else {
+  for (int it = 0; it * nthr < tot; ++it) {
+    const int i = it * nthr + tid;
+    const bool valid = i < tot;
+    const int slot = nslots > 1 ? i / nch : 0;
+    const int c = i - slot * nch;
+    float v[8];
+    if (valid) {
+      unpack8f(*reinterpret_cast<const uint4*>(pg_xchunk<GS>(geo, sm, slot, c)), v);
+    } else {
 #pragma unroll
-        for (int e2 = 0; e2 < 8; ++e2) v[e2] = 0.f;
-      }
-      pg_emit<GS>(geo, sm, slot, c, valid, v, sc);
+      for (int e2 = 0; e2 < 8; ++e2) v[e2] = 0.f;
     }
+    pg_emit<GS>(geo, sm, slot, c, valid, v, sc);
   }
 }
 
@@ -593,7 +598,7 @@ __device__ __forceinline__ void pg_prologue(const GemvArgs& a, const PGeom& geo,
 // with fewer units than warps still spread over all of them; each warp runs
 // two units at once, interleaved quad by quad (eight independent accumulator
 // chains; one unit's drain overlaps the other's math).
-template <int BITS, int GS>
+template <int BITS, int GS, bool XSL_MOD = false>
 __device__ __forceinline__ void pg_stage(const PGeom& geo, const PgSmem& sm, const unsigned char* sbase, int a0,
                                          int a1, int lb0, int warp, int lane, int nwarps, int rot) {
   constexpr int SPAN_K = 8 * GS;
@@ -624,7 +629,11 @@ __device__ __forceinline__ void pg_stage(const PGeom& geo, const PgSmem& sm, con
     const int rem = gt - lb * lb_tiles;
     const int h = rem >= S ? 1 : 0;
     const int sp = rem - h * S;
-    const int xsl = (int)(((unsigned long long)lb * geo.lps_magic) >> 32);  // 0 unless x_slots > 1
+    // 0 unless x_slots > 1.  Interleaved slots take an integer remainder: the
+    // multiply-shift form of the same quotient gave a warp's later units of a
+    // stage the wrong slot here (measured against the per-kernel chain; the
+    // cause was not found), the remainder is exact
+    const int xsl = XSL_MOD ? lb % geo.xsl_mod : (int)(((unsigned long long)lb * geo.lps_magic) >> 32);
     const unsigned char* tile = sbase + (size_t)ti * geo.tile_bytes;
     Unit r;
     r.aw = tile + hs * (A_BYTES / 2) + lane * 16;

@@ -397,16 +397,20 @@ int clear_step_words(emx_qwen3* m) {
   return EMX_OK;
 }
 
-// Plans the persistent decode step when the model qualifies (dense, one GPU,
-// group size 64 everywhere, head_dim 128, 1/2/4/8 q heads per KV head, one
-// norm group) and sets up its argument block and exchange words; it is then
-// the default decode path (sampling still runs the per-kernel chain).
+// Plans the persistent decode step when the model qualifies (one GPU, group
+// size 64 everywhere, head_dim 128, 1/2/4/8 q heads per KV head, one norm
+// group; dense, or MoE with up to 256 experts and top-16) and sets up its
+// argument block and exchange words; it is then the default decode path
+// (sampling still runs the per-kernel chain).
 int setup_step(emx_qwen3* m) {
   const emx_qwen3_config& c = m->c;
-  if (m->moe || m->world > 1 || c.norm_groups != 1) return EMX_OK;
+  if (m->world > 1 || c.norm_groups != 1) return EMX_OK;
   const QW& lmw = c.tied ? m->embed : m->lm;
   const LayerW& l0 = m->L[0];
-  if (l0.qkv.gs != 64 || l0.o.gs != 64 || l0.gate_up.gs != 64 || l0.down.gs != 64 || lmw.gs != 64) return EMX_OK;
+  const QW& gu0 = m->moe ? l0.e_gu : l0.gate_up;
+  const QW& dn0 = m->moe ? l0.e_down : l0.down;
+  if (l0.qkv.gs != 64 || l0.o.gs != 64 || gu0.gs != 64 || dn0.gs != 64 || lmw.gs != 64) return EMX_OK;
+  if (m->moe && l0.router.gs != 64) return EMX_OK;
   StepShape sh{};
   sh.H = m->H;
   sh.I = m->I;
@@ -417,8 +421,14 @@ int setup_step(emx_qwen3* m) {
   sh.gs = 64;
   sh.layers = c.layers;
   sh.cap = c.kv_cap;
-  const int bits[5] = {l0.qkv.bits, l0.o.bits, l0.gate_up.bits, l0.down.bits, lmw.bits};
-  for (int i = 0; i < 5; ++i) sh.bits[i] = bits[i];
+  const int bits[kStepMats] = {l0.qkv.bits, l0.o.bits, gu0.bits, dn0.bits, lmw.bits, m->moe ? l0.router.bits : 0};
+  for (int i = 0; i < kStepMats; ++i) sh.bits[i] = bits[i];
+  if (m->moe) {
+    sh.n_experts = c.n_experts;
+    sh.top_k = c.top_k;
+    sh.moe_inter = m->Im;
+    sh.norm_topk = c.norm_topk ? 1 : 0;
+  }
   StepPlan p{};
   const int nsm = m->ctx->num_sms;
   if (step_make_plan(sh, nsm, kStepBudget1, &p) || step_occupancy(p) < 1) {
@@ -427,7 +437,7 @@ int setup_step(emx_qwen3* m) {
   }
   int rc;
   StepLayer* d_layers = nullptr;
-  size_t words[5];
+  size_t words[kStepBuffers];
   step_exchange_words(sh, words);
   size_t nw = 0;
   for (size_t w : words) nw += w;
@@ -447,8 +457,9 @@ int setup_step(emx_qwen3* m) {
     StepLayer& s = hl[l];
     s.w[0] = lw.qkv.pk;
     s.w[1] = lw.o.pk;
-    s.w[2] = lw.gate_up.pk;
-    s.w[3] = lw.down.pk;
+    s.w[2] = m->moe ? lw.e_gu.pk : lw.gate_up.pk;
+    s.w[3] = m->moe ? lw.e_down.pk : lw.down.pk;
+    s.router = m->moe ? lw.router.pk : nullptr;
     s.in_norm = lw.in_norm;
     s.post_norm = lw.post_norm;
     s.q_norm = lw.q_norm;
@@ -476,6 +487,7 @@ int setup_step(emx_qwen3* m) {
   a.attw = a.qkvw + words[1];
   a.xmw = a.attw + words[2];
   a.hw = a.xmw + words[3];
+  a.rlw = a.hw + words[4];
   a.epoch = m->step_ctl;
   a.abort_word = m->step_ctl + 1;
   a.logits = m->logits;
@@ -1702,7 +1714,7 @@ int emx_qwen3_is_compiled(emx_qwen3* m, int* compiled) {
 
 int emx_qwen3_set_fused(emx_qwen3* m, int fused) {
   Q_REQUIRE(m, "emx_qwen3_set_fused: null model");
-  Q_REQUIRE(!fused || m->step_ok, "emx_qwen3_set_fused: this model has no persistent step (MoE, sharded or shape)");
+  Q_REQUIRE(!fused || m->step_ok, "emx_qwen3_set_fused: this model has no persistent step (sharded or shape)");
   if (m->fused != (fused != 0) && m->gexec) {
     cudaGraphExecDestroy(m->gexec);
     m->gexec = nullptr;

@@ -60,6 +60,7 @@ struct StepHdr {
   uint64_t empty[kMaxSlots];
   uint64_t auxfull[2];
   uint64_t auxempty[2];
+  uint64_t routed;  // MoE: this layer's top-k is in eidx / ew (consumer warp 0 -> producer)
   int abort_flag;
   int p;           // position of the new token
   int tok;         // this step's token
@@ -70,6 +71,9 @@ struct StepHdr {
   int wi[kCons];
   float scratch[32];
   float2 rcs[kHD / 2];  // (cos, sin) of this step's RoPE angles
+  int en;               // MoE: experts selected (top_k)
+  int eidx[kStepMaxTopK];
+  float ew[kStepMaxTopK];
 };
 
 // Load pairs per thread of a split merge: (m, l) of every (split, q head),
@@ -105,7 +109,11 @@ __device__ __forceinline__ void split_range(int L, int splits, int split, int& p
 
 // Attention splits per KV head for the new row p (rows 0..p attend).
 __device__ __forceinline__ int attn_splits(const StepArgs& A, int p) {
-  const int s = p < kRowsPerSplit ? 1 : (p + kRowsPerSplitLong) / kRowsPerSplitLong;
+  // a split's cost grows with its q heads: with 4 or 8 per KV head the
+  // splits start at 128 or 64 rows
+  const int hpg = A.nq / A.nkv;
+  const int one = hpg <= 2 ? kRowsPerSplit : kRowsPerSplit * 2 / hpg;
+  const int s = p < one ? 1 : (p + kRowsPerSplitLong) / kRowsPerSplitLong;
   return s < A.max_splits ? s : A.max_splits;
 }
 
@@ -158,12 +166,15 @@ __device__ __noinline__ bool fw_wait2(const uint64_t* p, unsigned flag, uint64_t
 // Reads the 8-element chunks [0, nch) of a bf16 vector held in flag words
 // (chunk c = words 4c..4c+3) carrying `flag` into shared memory: chunk c goes
 // to dst + (c / cpg) * gstride + (c % cpg) * 16 (the x-slot layout of a GEMV,
-// or a plain vector with cpg = nch).  Thread tid takes chunks tid, tid + kNT,
+// or a plain vector with cpg = nch); with SLOTS, chunk c is chunk i = c % cps
+// of slot c / cps, which goes to dst + slot * sbytes + (i / cpg) * gstride +
+// (i % cpg) * 16 (SLOTS: cps > 0).  Thread tid takes chunks tid, tid + kNT,
 // ...; up to four chunks are polled together: each round issues the loads of
 // every chunk not yet seen, then checks them.  On abort the thread stops (the
 // caller's next barrier and abort check end the phase).
 __device__ __noinline__ void fw_read_vec(const uint64_t* src, int nch, unsigned flag, unsigned char* dst, int cpg,
-                                         int gstride, const StepArgs& A, StepHdr& H, int tid) {
+                                         int gstride, const StepArgs& A, StepHdr& H, int tid, int cps = 0,
+                                         int sbytes = 0) {
   constexpr int kPass = 4;  // chunks whose loads are in flight together
   for (int c0 = tid; c0 < nch; c0 += kPass * kNT) {
     uint64_t w[kPass][4];
@@ -186,7 +197,8 @@ __device__ __noinline__ void fw_read_vec(const uint64_t* src, int nch, unsigned 
         if ((pend & (1u << j)) && fw_ok(w[j][0], w[j][1], flag) && fw_ok(w[j][2], w[j][3], flag)) {
           pend &= ~(1u << j);
           const int c = c0 + j * kNT;
-          *reinterpret_cast<uint4*>(dst + (size_t)(c / cpg) * gstride + (c % cpg) * 16) =
+          const int sl = cps ? c / cps : 0, i = c - sl * cps;
+          *reinterpret_cast<uint4*>(dst + (size_t)sl * sbytes + (size_t)(i / cpg) * gstride + (i % cpg) * 16) =
               make_uint4((uint32_t)w[j][0], (uint32_t)w[j][1], (uint32_t)w[j][2], (uint32_t)w[j][3]);
         }
       }
@@ -286,10 +298,98 @@ __device__ void stage_raw_fw(const PGeom& geo, const PgSmem& sm, const uint64_t*
   pg_pad<64>(geo, sm, tid, kNT);
 }
 
+// The same for the MoE experts' SwiGLU outputs: one x slot per selected
+// expert, one scale for all slots.
+__device__ __noinline__ void stage_raw_slots(const PGeom& geo, const PgSmem& sm, const uint64_t* src,
+                                             unsigned flag, const StepArgs& A, StepHdr& H, int tid) {
+  const int nch = geo.K / 8, ns = geo.x_slots;
+  fw_read_vec(src, ns * nch, flag, sm.xsm, 8, geo.gstride, A, H, tid, nch, geo.xslot_bytes);
+  float mx = 0.f;
+  for (int i = tid; i < ns * nch; i += kNT) {
+    const int sl = i / nch;
+    float v[8];
+    unpack8f(*reinterpret_cast<const uint4*>(pg_xchunk<64>(geo, sm, sl, i - sl * nch)), v);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) mx = fmaxf(mx, fabsf(v[e]));
+  }
+  pg_convert_staged<64, CSync>(geo, sm, ns, mx, H.scratch, &H.xsc, tid, kNT);
+  pg_pad<64>(geo, sm, tid, kNT);
+}
+
 // The residual vector from flag words into res.
 __device__ void load_res_fw(const uint64_t* src, int H_, unsigned flag, bf16* res, const StepArgs& A, StepHdr& H,
                             int tid) {
   fw_read_vec(src, H_ / 8, flag, reinterpret_cast<unsigned char*>(res), H_ / 8, 0, A, H, tid);
+}
+
+// The MoE routing of a layer by the consumer threads, one expert each:
+// p_e = bf16(exp(l_e - max) / sum_e exp(l_e - max)), then the top_k by rank
+// (the number of experts ahead of e in (value desc, index asc) order; NaN
+// never ranks), which selects and orders them as k rounds of a stable
+// argmax do (the largest value, the lowest index among equal ones; with
+// nothing left to take, index 0 with its value if that is NaN, else -inf),
+// then with norm_topk the weights divided by their sum
+// (crates/ops/src/moe.rs:112-128).  The softmax sum is a butterfly per 32
+// experts, then one over the group sums, as in the per-kernel routing, so
+// both give the same bits.  Into eidx / ew / en, published to the producer
+// through `routed`; lg: E bf16 of scratch.  Ends with a consumer barrier;
+// false on abort.
+__device__ __noinline__ bool route_block(const StepArgs& A, StepHdr& H, bf16* lg, unsigned flag, int tid) {
+  const int E = A.n_experts, k = A.top_k, lane = tid & 31, warp = tid >> 5;
+  if (tid < E / 4) {  // words 2t, 2t + 1: experts 4t..4t+3
+    uint64_t a, b;
+    if (fw_wait2(A.rlw + 2 * tid, flag, a, b, A, H)) {
+      reinterpret_cast<uint32_t*>(lg)[2 * tid] = (uint32_t)a;
+      reinterpret_cast<uint32_t*>(lg)[2 * tid + 1] = (uint32_t)b;
+    }
+  }
+  if (tid < k) H.eidx[tid] = -1;
+  CSync::sync();
+  if (aborted(H)) return false;
+  const float x = tid < E ? bf2f(lg[tid]) : -INFINITY;
+  float m = warp_max(x);
+  if (lane == 0) H.scratch[warp] = m;
+  CSync::sync();
+  m = H.scratch[0];
+#pragma unroll
+  for (int w = 1; w < kCons; ++w) m = fmaxf(m, H.scratch[w]);
+  const float t = warp_sum(tid < E ? expf(x - m) : 0.f);
+  CSync::sync();
+  if (lane == 0) H.scratch[warp] = t;
+  CSync::sync();
+  const float s = warp_sum(lane < kCons ? H.scratch[lane] : 0.f);
+  const float pr = tid < E ? bfround(__fdiv_rn(expf(x - m), s)) : 0.f;
+  if (tid < E) lg[tid] = f2bf(pr);  // every thread has its logit in x
+  CSync::sync();
+  if (tid < E && pr == pr) {
+    int rank = 0;
+    for (int j = 0; j < E; ++j) {
+      const float q = bf2f(lg[j]);
+      rank += (q > pr || (q == pr && j < tid)) ? 1 : 0;
+    }
+    if (rank < k) {
+      H.eidx[rank] = tid;
+      H.ew[rank] = pr;
+    }
+  }
+  CSync::sync();
+  if (tid == 0) {
+    const float p0 = bf2f(lg[0]);
+    float sum = 0.f;
+    for (int r = 0; r < k; ++r) {
+      if (H.eidx[r] < 0) {  // fewer than k experts with a value
+        H.eidx[r] = 0;
+        H.ew[r] = p0 != p0 ? p0 : -INFINITY;
+      }
+      sum = __fadd_rn(sum, H.ew[r]);
+    }
+    if (A.norm_topk && sum > 1e-20f)
+      for (int r = 0; r < k; ++r) H.ew[r] = __fdiv_rn(H.ew[r], sum);
+    H.en = k;
+    mbar_arrive(&H.routed);
+  }
+  CSync::sync();
+  return true;
 }
 
 // ------------------------------------------------------------- GEMV phases
@@ -298,7 +398,7 @@ __device__ void load_res_fw(const uint64_t* src, int H_, unsigned flag, bf16* re
 // and the counters live in registers for the whole phase: every asm block
 // with a memory clobber (the mbarrier ops) would otherwise force them to be
 // re-read per stage.
-template <int BITS>
+template <int BITS, bool XSL_MOD = false>
 __device__ __noinline__ void gemv_run(const StepArgs& A, StepHdr& H, unsigned char* smem, const PGeom& geo_ref,
                                       int lb0, int lb1, int& seq_ref, int& rot_ref, int tid) {
   const int warp = tid >> 5, lane = tid & 31;
@@ -315,7 +415,7 @@ __device__ __noinline__ void gemv_run(const StepArgs& A, StepHdr& H, unsigned ch
   for (int a0 = lb0 * lbt; a0 < T1; a0 += geo.stage_tiles) {
     const int a1 = min(T1, a0 + geo.stage_tiles);
     if (wait_or_abort(&H.full[slot], par, &H.abort_flag, status))
-      pg_stage<BITS, 64>(geo, sm, ring + (size_t)slot * SB, a0, a1, lb0, warp, lane, kCons, rot);
+      pg_stage<BITS, 64, XSL_MOD>(geo, sm, ring + (size_t)slot * SB, a0, a1, lb0, warp, lane, kCons, rot);
     rot = (rot + (a1 - a0) * 2) & (kCons - 1);
     __syncwarp();
     if (lane == 0) mbar_arrive(&H.empty[slot]);
@@ -330,12 +430,13 @@ __device__ __noinline__ void gemv_run(const StepArgs& A, StepHdr& H, unsigned ch
   CSync::sync();
 }
 
+template <bool XSL_MOD = false>
 __device__ __forceinline__ void gemv_any(int bits, const StepArgs& A, StepHdr& H, unsigned char* smem,
                                          const PGeom& geo, int lb0, int lb1, int& seq, int& rot, int tid) {
   if (bits == 8)
-    gemv_run<8>(A, H, smem, geo, lb0, lb1, seq, rot, tid);
+    gemv_run<8, XSL_MOD>(A, H, smem, geo, lb0, lb1, seq, rot, tid);
   else
-    gemv_run<4>(A, H, smem, geo, lb0, lb1, seq, rot, tid);
+    gemv_run<4, XSL_MOD>(A, H, smem, geo, lb0, lb1, seq, rot, tid);
 }
 
 enum OutKind : int { kOutStore = 0, kOutResid = 1, kOutSwiglu = 2 };
@@ -713,8 +814,97 @@ __device__ __noinline__ void attn_phase(const StepArgs& A, StepHdr& H, unsigned 
   attn_merge_slice<HPG>(A, H, S, hw, out, split, ns, flag, tid);
 }
 
+// Logical blocks [d0, d1) of the down phase for CTA v of G.  MoE: whole
+// row blocks of H, each the top_k slots' blocks in slot order (block
+// rb * top_k + j: rows rb of expert slot j), so a CTA sums its rows over the
+// experts itself.
+template <bool MOE>
+__device__ __forceinline__ void down_range(const StepArgs& A, int v, int G, int& d0, int& d1) {
+  if (MOE) {
+    cta_range(A.H / 16, v, G, d0, d1);
+    d0 *= A.top_k;
+    d1 *= A.top_k;
+  } else {
+    cta_range(A.geo[kMatDown].lb_total, v, G, d0, d1);
+  }
+}
+
+// A MoE layer's post-attention norm, router GEMV, top-k and the selected
+// experts' gate|up + SwiGLU (consumer threads; the router reads the x staged
+// for gate|up).  A CTA routes when it has expert work (its producer needs
+// the experts, its down epilogue the weights); that work is what the next
+// layer's router waits for, so the router logits it reads are not rewritten
+// under it.  False on abort.
+__device__ __noinline__ bool moe_router_gu(const StepArgs& A, StepHdr& H, unsigned char* smem, bf16* res,
+                                           const bf16* aux, int ab, uint32_t apar, int l, unsigned flag, int& seq,
+                                           int& rot, int tid) {
+  const int G = (int)gridDim.x, v = (int)blockIdx.x;
+  int g0, g1, d0, d1, r0, r1;
+  cta_range(A.geo[kMatGu].lb_total, v, G, g0, g1);
+  down_range<true>(A, v, G, d0, d1);
+  cta_range(A.geo[kMatRouter].lb_total, v, G, r0, r1);
+  const bool routes = g1 > g0 || d1 > d0;
+  if (g1 > g0 || r1 > r0) load_res_fw(A.xmw, A.H, flag, res, A, H, tid);
+  CSync::sync();
+  if (aborted(H)) return false;
+  const PGeom& geo = A.geo[kMatGu];
+  if (g1 > g0 || r1 > r0) {
+    wait_or_abort(&H.auxfull[ab], apar, &H.abort_flag, A.status);
+    stage_norm(geo, pg_smem(smem, geo), res, aux + A.H, A.eps, H, tid);
+    CSync::sync();
+  }
+  if (r1 > r0) {
+    const PGeom& rg = A.geo[kMatRouter];
+    gemv_any(A.bits[kMatRouter], A, H, smem, rg, r0, r1, seq, rot, tid);
+    epilogue_fw<kOutStore>(rg, pg_smem(smem, rg), r0, r1, res, A.rlw, flag, H.xsc, tid);
+  }
+  if (routes && !route_block(A, H, res, flag, tid)) return false;
+  if (g1 > g0) {
+    gemv_any(A.bits[kMatGu], A, H, smem, geo, g0, g1, seq, rot, tid);
+    epilogue_fw<kOutSwiglu>(geo, pg_smem(smem, geo), g0, g1, res, A.hw, flag, H.xsc, tid);
+  }
+  return true;
+}
+
+// A MoE layer's expert down projections over the logical blocks [d0, d1)
+// of down_range (x slot j = slot j's SwiGLU output) and the block's output:
+// row n = bf16(xm_n + sum_j w_j bf16(y_jn)), the products summed in slot
+// order in fp32 (crates/ops/src/moe.rs:196-207; the per-kernel chain's
+// add-and-norm prologue does the same sum), out as the layer's residual.
+// The CTA's xm rows go into res first.  False on abort.
+__device__ __noinline__ bool moe_down(const StepArgs& A, StepHdr& H, unsigned char* smem, bf16* res, int d0,
+                                      int d1, unsigned flag, int& seq, int& rot, int tid) {
+  const PGeom& geo = A.geo[kMatDown];
+  const int k = A.top_k, rb0 = d0 / k, nrow = (d1 - d0) / k * 16;
+  fw_read_vec(A.xmw + (size_t)rb0 * 8, nrow / 8, flag, reinterpret_cast<unsigned char*>(res + rb0 * 16), nrow / 8,
+              0, A, H, tid);
+  stage_raw_slots(geo, pg_smem(smem, geo), A.hw, flag, A, H, tid);
+  CSync::sync();
+  if (aborted(H)) return false;
+  gemv_any<true>(A.bits[kMatDown], A, H, smem, geo, d0, d1, seq, rot, tid);
+  const PgSmem sm = pg_smem(smem, geo);
+  const int SKP = geo.S * 2;
+  const float xs = H.xsc;
+  for (int i0 = 0; i0 < nrow; i0 += kNT) {
+    const int li = i0 + tid;
+    float y = 0.f;
+    if (li < nrow) {
+      const int rbl = li >> 4, r = li & 15;
+      float add = 0.f;
+      for (int j = 0; j < k; ++j)
+        add = __fadd_rn(add, __fmul_rn(bfround(row_value(sm.red, (rbl * k + j) * 16 + r, SKP, xs)), H.ew[j]));
+      y = bfround(__fadd_rn(bf2f(res[rb0 * 16 + li]), add));
+    }
+    const uint32_t bits = f2bits(y);
+    const uint32_t hi = __shfl_down_sync(0xffffffffu, bits, 1);
+    if (li < nrow && (li & 1) == 0) fw_store(A.xw + (size_t)(rb0 * 16 + li) / 2, bits | (hi << 16), flag);
+  }
+  return true;
+}
+
 // ------------------------------------------------------------ producer
 // Every stage of the step for this CTA, in the order the consumers take them.
+template <bool MOE>
 __device__ __noinline__ void producer(const StepArgs& A, StepHdr& H, unsigned char* smem, int v, int G, int p,
                                       int ns) {
   const int NS = A.nslots, SB = A.slot_bytes;
@@ -741,6 +931,42 @@ __device__ __noinline__ void producer(const StepArgs& A, StepHdr& H, unsigned ch
       const uint32_t bytes = (uint32_t)((a1 - a0) * geo.tile_bytes);
       mbar_arrive_expect_tx(&H.full[slot], bytes);
       bulk_g2s_hint(ring + (size_t)slot * SB, w + (size_t)a0 * geo.tile_bytes, bytes, &H.full[slot], pol);
+      ++s;
+    }
+    return true;
+  };
+  // the top_k selected experts' stages.  gate|up: logical block lb of the
+  // gathered matrix is block lb % lps of expert eidx[lb / lps] (lps blocks per
+  // expert, contiguous), so a stage takes one copy per expert it touches;
+  // down (down_range): block lb is block lb / top_k of expert
+  // eidx[lb % top_k], one copy per block
+  auto gemv_experts = [&](int mat, const unsigned char* w, int lps, int l) -> bool {
+    const PGeom& geo = A.geo[mat];
+    const bool inter = mat == kMatDown;
+    const int k = A.top_k;
+    int b0, b1;
+    if (inter)
+      down_range<true>(A, v, G, b0, b1);
+    else
+      cta_range(geo.lb_total, v, G, b0, b1);
+    if (b1 <= b0) return true;
+    if (!wait_or_abort(&H.routed, (uint32_t)(l & 1), &H.abort_flag, A.status)) return false;
+    const int lbt = geo.halves * geo.S;
+    const size_t tb = geo.tile_bytes, lb_bytes = (size_t)lbt * tb;
+    for (int a0 = b0 * lbt; a0 < b1 * lbt; a0 += geo.stage_tiles) {
+      const int a1 = min(b1 * lbt, a0 + geo.stage_tiles);
+      const int slot = acquire();
+      if (slot < 0) return false;
+      mbar_arrive_expect_tx(&H.full[slot], (uint32_t)((a1 - a0) * tb));
+      for (int tl = a0; tl < a1;) {
+        const int lb = tl / lbt;
+        const int j = inter ? lb % k : lb / lps, blk = inter ? lb / k : lb - j * lps;
+        const unsigned char* src = w + ((size_t)H.eidx[j] * lps + blk) * lb_bytes + (size_t)(tl - lb * lbt) * tb;
+        const int end = min(a1, inter ? (lb + 1) * lbt : (j + 1) * lps * lbt);
+        bulk_g2s_hint(ring + (size_t)slot * SB + (size_t)(tl - a0) * tb, src, (uint32_t)((end - tl) * tb),
+                      &H.full[slot], pol);
+        tl = end;
+      }
       ++s;
     }
     return true;
@@ -805,8 +1031,12 @@ __device__ __noinline__ void producer(const StepArgs& A, StepHdr& H, unsigned ch
   for (int l = 0; ok && l < A.n_layers; ++l) {
     const StepLayer& LW = A.layers[l];
     if (l + 1 < A.n_layers) prefetch_kv(A.layers[l + 1]);
-    ok = aux(l) && gemv(kMatQkv, LW.w[0]) && attn(LW) && gemv(kMatO, LW.w[1]) && gemv(kMatGu, LW.w[2]) &&
-         gemv(kMatDown, LW.w[3]);
+    ok = aux(l) && gemv(kMatQkv, LW.w[0]) && attn(LW) && gemv(kMatO, LW.w[1]);
+    if (!MOE)
+      ok = ok && gemv(kMatGu, LW.w[2]) && gemv(kMatDown, LW.w[3]);
+    else
+      ok = ok && gemv(kMatRouter, LW.router) && gemv_experts(kMatGu, LW.w[2], A.egu_lps, l) &&
+           gemv_experts(kMatDown, LW.w[3], A.edown_lps, l);
   }
   if (ok) ok = aux(A.n_layers) && gemv(kMatLm, A.lm_w);
   // never leave with copies in flight into this CTA's shared memory
@@ -825,7 +1055,7 @@ __device__ __forceinline__ void argmax_pair(float& bv, int& bi, float ov, int oi
 }
 
 // ---------------------------------------------------------------- kernel
-template <int HPG>
+template <int HPG, bool MOE>
 __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant__ StepArgs Ap) {
   extern __shared__ __align__(128) unsigned char smem[];
   StepHdr& H = *reinterpret_cast<StepHdr*>(smem);
@@ -852,6 +1082,8 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
       mbar_init(&H.auxfull[b], 1);
       mbar_init(&H.auxempty[b], 1);
     }
+    mbar_init(&H.routed, 1);
+    H.en = 0;
     H.abort_flag = *reinterpret_cast<volatile unsigned*>(A.abort_word) ? 1 : 0;
     fence_mbar_init();
     H.p = *reinterpret_cast<volatile int*>(A.pos);
@@ -874,7 +1106,7 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
   __syncthreads();
   const int ns = attn_splits(A, p);
   if (warp == kCons) {
-    if (lane == 0) producer(A, H, smem, v, G, p, ns);
+    if (lane == 0) producer<MOE>(A, H, smem, v, G, p, ns);
     return;
   }
 
@@ -886,7 +1118,7 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
   cta_range(A.geo[kMatQkv].lb_total, v, G, q0, q1);
   cta_range(A.geo[kMatO].lb_total, v, G, o0, o1);
   cta_range(A.geo[kMatGu].lb_total, v, G, g0, g1);
-  cta_range(A.geo[kMatDown].lb_total, v, G, d0, d1);
+  down_range<MOE>(A, v, G, d0, d1);
   for (int l = 0; l < L; ++l) {
     const StepLayer& LW = A.layers[l];
     const unsigned flag = H.ebase + (unsigned)l + 1u;
@@ -924,13 +1156,17 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
       gemv_any(A.bits[kMatO], A, H, smem, geo, o0, o1, seq, rot, tid);
       epilogue_fw<kOutResid>(geo, pg_smem(smem, geo), o0, o1, res, A.xmw, flag, H.xsc, tid);
     }
-    // ---- post-attention norm + gate|up + SwiGLU: x of the MLP into res
-    // (the down residual too)
     CSync::sync();
-    if (g1 > g0 || d1 > d0) load_res_fw(A.xmw, A.H, flag, res, A, H, tid);
+    if (MOE) {
+      if (!moe_router_gu(A, H, smem, res, aux, ab, apar, l, flag, seq, rot, tid)) return;
+    } else if (g1 > g0 || d1 > d0) {
+      // ---- post-attention norm + gate|up + SwiGLU: x of the MLP into res
+      // (the down residual too)
+      load_res_fw(A.xmw, A.H, flag, res, A, H, tid);
+    }
     CSync::sync();
     if (aborted(H)) return;
-    if (g1 > g0) {
+    if (!MOE && g1 > g0) {
       const PGeom& geo = A.geo[kMatGu];
       wait_or_abort(&H.auxfull[ab], apar, &H.abort_flag, A.status);
       stage_norm(geo, pg_smem(smem, geo), res, aux + A.H, A.eps, H, tid);
@@ -948,8 +1184,11 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
       wait_or_abort(&H.auxfull[ab], apar, &H.abort_flag, A.status);
       mbar_arrive(&H.auxempty[ab]);
     }
-    // ---- down projection + residual
-    if (d1 > d0) {
+    // ---- down projection + residual (MoE: the selected experts' down
+    // projections, combined in the next input)
+    if (MOE) {
+      if (d1 > d0 && !moe_down(A, H, smem, res, d0, d1, flag, seq, rot, tid)) return;
+    } else if (d1 > d0) {
       const PGeom& geo = A.geo[kMatDown];
       stage_raw_fw(geo, pg_smem(smem, geo), A.hw, flag, A, H, tid);
       CSync::sync();
@@ -1046,24 +1285,33 @@ int attn_bytes() {
   return (int)sizeof(AttnSm<HPG>);
 }
 
-const void* kernel_for(int hpg) {
-  switch (hpg) {
-    case 1: return reinterpret_cast<const void*>(step_kernel<1>);
-    case 2: return reinterpret_cast<const void*>(step_kernel<2>);
-    case 4: return reinterpret_cast<const void*>(step_kernel<4>);
-    case 8: return reinterpret_cast<const void*>(step_kernel<8>);
+// The kernel of a plan: q heads per KV head, and dense or MoE (a compile-time
+// switch: the dense kernel carries none of the MoE phases).
+const void* kernel_for(int hpg, bool moe) {
+  switch (hpg * 2 + (moe ? 1 : 0)) {
+    case 2: return reinterpret_cast<const void*>(step_kernel<1, false>);
+    case 3: return reinterpret_cast<const void*>(step_kernel<1, true>);
+    case 4: return reinterpret_cast<const void*>(step_kernel<2, false>);
+    case 5: return reinterpret_cast<const void*>(step_kernel<2, true>);
+    case 8: return reinterpret_cast<const void*>(step_kernel<4, false>);
+    case 9: return reinterpret_cast<const void*>(step_kernel<4, true>);
+    case 16: return reinterpret_cast<const void*>(step_kernel<8, false>);
+    case 17: return reinterpret_cast<const void*>(step_kernel<8, true>);
     default: return nullptr;
   }
 }
 
 }  // namespace
 
-void step_exchange_words(const StepShape& sh, size_t words[5]) {
+void step_exchange_words(const StepShape& sh, size_t words[kStepBuffers]) {
+  const bool moe = sh.n_experts > 0;
   words[0] = (size_t)sh.H / 2;
   words[1] = (size_t)(sh.nq + 2 * sh.nkv) * kHD / 2;
   words[2] = (size_t)sh.nq * kHD / 2;
   words[3] = (size_t)sh.H / 2;
-  words[4] = (size_t)sh.I / 2;
+  words[4] = moe ? (size_t)sh.top_k * sh.moe_inter / 2 : (size_t)sh.I / 2;
+  words[5] = moe ? (size_t)sh.n_experts / 2 : 0;
+  for (int i = 0; i < kStepBuffers; ++i) words[i] = (words[i] + 1) & ~(size_t)1;  // 16-byte aligned starts
 }
 
 int step_make_plan(const StepShape& sh, int num_sms, int budget, StepPlan* plan) {
@@ -1071,7 +1319,13 @@ int step_make_plan(const StepShape& sh, int num_sms, int budget, StepPlan* plan)
   if (sh.gs != 64 || sh.hd != kHD || sh.nkv <= 0 || sh.nq % sh.nkv != 0 || num_sms <= 0) return -1;
   const int hpg = sh.nq / sh.nkv;
   if (hpg != 1 && hpg != 2 && hpg != 4 && hpg != 8) return -1;
-  if (sh.H % 64 != 0 || sh.I % 64 != 0) return -1;
+  const bool moe = sh.n_experts > 0;
+  if (sh.H % 64 != 0 || (!moe && sh.I % 64 != 0)) return -1;
+  // MoE: routing by one warp (up to 256 experts), the top-k slots' indices in
+  // shared memory, expert widths in whole 64-wide groups
+  if (moe && (sh.n_experts > kStepMaxExperts || sh.n_experts % 16 != 0 || sh.top_k < 1 ||
+              sh.top_k > kStepMaxTopK || sh.top_k > sh.n_experts || sh.moe_inter % 64 != 0))
+    return -1;
   StepPlan P{};
   StepArgs& A = P.tmpl;
   memset(&A, 0, sizeof(A));
@@ -1083,24 +1337,44 @@ int step_make_plan(const StepShape& sh, int num_sms, int budget, StepPlan* plan)
   A.aux_stride = round128(4 * sh.H + 512);
   A.off_res = A.off_aux + 2 * A.aux_stride;
   A.off_u = A.off_res + round128(2 * sh.H);
-  const int N[5] = {(sh.nq + 2 * sh.nkv) * kHD, sh.H, 2 * sh.I, sh.H, sh.vocab};
-  const int K[5] = {sh.H, sh.nq * kHD, sh.H, sh.I, sh.H};
-  const int epi[5] = {kEpiStore, kEpiResid, kEpiSwiglu, kEpiResid, kEpiArgmax};
+  // MoE: gate|up over top_k slots of 2 moe_inter rows, down over the
+  // top_k slots' blocks of each row block (x slot = block % top_k), and the
+  // router
+  const int Im = sh.moe_inter, k = sh.top_k;
+  const int N[kStepMats] = {(sh.nq + 2 * sh.nkv) * kHD, sh.H, moe ? 2 * k * Im : 2 * sh.I, moe ? k * sh.H : sh.H,
+                            sh.vocab, moe ? sh.n_experts : 0};
+  const int K[kStepMats] = {sh.H, sh.nq * kHD, sh.H, moe ? Im : sh.I, sh.H, sh.H};
+  const int epi[kStepMats] = {kEpiStore, kEpiResid, kEpiSwiglu, moe ? kEpiStore : kEpiResid, kEpiArgmax, kEpiStore};
   int end = A.off_u;
-  for (int m = 0; m < 5; ++m) {
+  for (int m = 0; m < (moe ? kStepMats : kStepMats - 1); ++m) {
     const int bits = sh.bits[m];
     if (bits != 4 && bits != 8) return -1;
     if (K[m] % 64 != 0) return -1;
     const int halves = epi[m] == kEpiSwiglu ? 2 : 1;
     if ((N[m] / halves) % 16 != 0) return -1;
     const int W = N[m] / halves / 16;
-    const int lbs_max = (W + num_sms - 1) / num_sms;
+    const int lbs_max =
+        moe && m == kMatDown ? (sh.H / 16 + num_sms - 1) / num_sms * k : (W + num_sms - 1) / num_sms;
     const int tb = ptile_bytes(bits, 64);
     const int st = kSlotBytes / tb;
     if (st < 1) return -1;
-    pgeom_make(&A.geo[m], K[m], bits, 64, epi[m], W, st, 0, 1, lbs_max, false);
+    const int xs = moe && m == kMatDown ? k : 1;
+    pgeom_make(&A.geo[m], K[m], bits, 64, epi[m], W, st, 0, xs, lbs_max, false);
+    if (xs > 1) A.geo[m].xsl_mod = k;
     end = std::max(end, pgeom_layout(A.geo[m], 64, A.off_u));
     A.bits[m] = bits;
+  }
+  if (moe) {
+    // the router reads the gate|up phase's staged x: the same place
+    const PGeom &r = A.geo[kMatRouter], &g = A.geo[kMatGu];
+    if (r.off_x != g.off_x || r.off_zero != g.off_zero || r.off_xs != g.off_xs || r.xslot_bytes != g.xslot_bytes)
+      return -1;
+    A.moe = 1;
+    A.n_experts = sh.n_experts;
+    A.top_k = k;
+    A.norm_topk = sh.norm_topk;
+    A.egu_lps = Im / 16;
+    A.edown_lps = sh.H / 16;
   }
   const int ab = hpg == 1 ? attn_bytes<1>() : hpg == 2 ? attn_bytes<2>() : hpg == 4 ? attn_bytes<4>() : attn_bytes<8>();
   end = std::max(end, A.off_u + ab);
@@ -1127,7 +1401,7 @@ int step_make_plan(const StepShape& sh, int num_sms, int budget, StepPlan* plan)
 }
 
 int step_occupancy(const StepPlan& p) {
-  const void* k = kernel_for(p.hpg);
+  const void* k = kernel_for(p.hpg, p.tmpl.moe != 0);
   if (!k) return 0;
   if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, p.smem) != cudaSuccess) return 0;
   int n = 0;
@@ -1136,7 +1410,7 @@ int step_occupancy(const StepPlan& p) {
 }
 
 cudaError_t step_launch(const StepArgs& a, const StepPlan& p, cudaStream_t st, bool coop) {
-  const void* k = kernel_for(p.hpg);
+  const void* k = kernel_for(p.hpg, p.tmpl.moe != 0);
   if (!k) return cudaErrorInvalidValue;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, p.smem);
   if (e != cudaSuccess) return e;

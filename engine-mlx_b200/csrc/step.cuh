@@ -1,10 +1,12 @@
-// step.cuh — the whole batch-1 decode step of a dense model as one
+// step.cuh — the whole batch-1 decode step of a single-GPU model as one
 // persistent kernel.
 //
-// Replaces, for a dense single-GPU model, the per-layer kernel chain of the
-// decode step (qkv GEMV -> attention -> o GEMV -> gate|up GEMV -> down GEMV,
-// then the lm_head with argmax; the traced step of
-// crates/serve/src/compiled.rs:127-201).  One CTA per SM stays resident for
+// Replaces the per-layer kernel chain of the decode step (qkv GEMV ->
+// attention -> o GEMV -> gate|up GEMV -> down GEMV, or for a mixture of
+// experts router GEMV -> top-k -> the selected experts' gate|up and down
+// GEMVs; then the lm_head with argmax; the traced step of
+// crates/serve/src/compiled.rs:127-201, the MoE block of
+// crates/ops/src/moe.rs:103-207).  One CTA per SM stays resident for
 // the whole step.  Each CTA's producer warp streams the packed weights (and
 // the KV rows its attention split reads) of phase after phase into a
 // shared-memory ring without waiting for the phases to start: weights do not
@@ -24,7 +26,9 @@
 namespace emx {
 
 struct StepLayer {
-  const unsigned char* w[4];  // packed qkv, o, gate|up, down (pgemv layout)
+  const unsigned char* w[4];  // packed qkv, o, gate|up, down (pgemv layout; MoE: the expert tensors
+                              // [experts][rows / 16][tiles])
+  const unsigned char* router;  // packed MoE router [experts][hidden] (nullptr: dense)
   const bf16* in_norm;        // [H]
   const bf16* post_norm;      // [H]
   const bf16* q_norm;         // [128] or nullptr
@@ -33,13 +37,17 @@ struct StepLayer {
   bf16* vc;
 };
 
-enum StepMat : int { kMatQkv = 0, kMatO = 1, kMatGu = 2, kMatDown = 3, kMatLm = 4 };
+enum StepMat : int { kMatQkv = 0, kMatO = 1, kMatGu = 2, kMatDown = 3, kMatLm = 4, kMatRouter = 5 };
+constexpr int kStepMats = 6;
+constexpr int kStepMaxTopK = 16;
+constexpr int kStepMaxExperts = 256;
 
 struct StepArgs {
   const StepLayer* layers;  // device array [n_layers]
   int n_layers;
-  pg::PGeom geo[5];  // per matrix kind, offsets in this kernel's layout
-  int bits[5];
+  pg::PGeom geo[kStepMats];  // per matrix kind, offsets in this kernel's layout (MoE: gate|up and
+                             // down are the gathered expert matrices, top_k slots)
+  int bits[kStepMats];
   const unsigned char* lm_w;  // packed lm_head (the embedding when tied)
   const bf16* final_norm;
   const uint32_t* emb_w;  // quantized embedding table
@@ -54,7 +62,10 @@ struct StepArgs {
   uint64_t* qkvw;  // fused q|k|v projection [(nq + 2 nkv) * 64]
   uint64_t* attw;  // attention output [nq * 64]
   uint64_t* xmw;   // residual after the attention block [H / 2]
-  uint64_t* hw;    // SwiGLU output [I / 2]
+  uint64_t* hw;    // SwiGLU output [I / 2] (MoE: [top_k][moe_inter / 2])
+  uint64_t* rlw;   // MoE router logits [experts / 2]
+  int moe, n_experts, top_k, norm_topk;
+  int egu_lps, edown_lps;  // logical blocks per expert slot of the gate|up and down matrices
   unsigned* epoch;  // steps since the words were cleared (the last CTA adds one)
   unsigned* abort_word;  // nonzero: a CTA gave up on a wait; every CTA leaves
   bf16* logits;          // [vocab]
@@ -80,7 +91,8 @@ struct StepArgs {
 
 struct StepShape {
   int H, I, nq, nkv, hd, vocab, gs, layers, cap;
-  int bits[5];  // qkv, o, gate|up, down, lm_head
+  int bits[kStepMats];  // qkv, o, gate|up, down, lm_head, router
+  int n_experts, top_k, moe_inter, norm_topk;  // n_experts 0: dense (I the MLP width)
 };
 
 struct StepPlan {
@@ -88,8 +100,9 @@ struct StepPlan {
   StepArgs tmpl;  // geometry and layout (pointers unset)
 };
 
-// Flag-word counts of the exchange buffers (xw, qkvw, attw, xmw, hw in order).
-void step_exchange_words(const StepShape& sh, size_t words[5]);
+constexpr int kStepBuffers = 6;
+// Flag-word counts of the exchange buffers (xw, qkvw, attw, xmw, hw, rlw in order).
+void step_exchange_words(const StepShape& sh, size_t words[kStepBuffers]);
 // Plans the step within `budget` bytes of shared memory per CTA; 0 on success.
 int step_make_plan(const StepShape& sh, int num_sms, int budget, StepPlan* plan);
 // CTAs of the step kernel that fit on one SM (0: the plan cannot launch).

@@ -357,12 +357,14 @@ int emx_qwen3_set_compiled(emx_qwen3* m, int compiled);
 int emx_qwen3_is_compiled(emx_qwen3* m, int* compiled);
 /* No reference counterpart (the reference's decode step is one traced MLX
  * closure, crates/serve/src/compiled.rs:79-287, whatever its kernels):
- * set_fused(m, 1) runs the whole decode step of a dense model on one GPU as
- * one persistent kernel whose phases hand off through flag words (the
- * default wherever the model has such a plan); set_fused(m, 0) selects one
- * kernel per operation.  Setting 1 fails with EMX_ERR_INVALID when the model
- * has no such plan (MoE, sharded, group size != 64, head_dim != 128, more
- * than 8 q heads per KV head). */
+ * set_fused(m, 1) runs the whole decode step of a model on one GPU as one
+ * persistent kernel whose phases hand off through flag words (dense, or MoE
+ * with its router, top-k and the selected experts' projections inside the
+ * same launch; the default wherever the model has such a plan);
+ * set_fused(m, 0) selects one kernel per operation.  Setting 1 fails with
+ * EMX_ERR_INVALID when the model has no such plan (sharded, group size != 64,
+ * head_dim != 128, more than 8 q heads per KV head, more than 256 experts or
+ * top-16). */
 int emx_qwen3_set_fused(emx_qwen3* m, int fused);
 int emx_qwen3_is_fused(emx_qwen3* m, int* fused);
 int emx_qwen3_step_launches(emx_qwen3* m, int* n);
