@@ -109,11 +109,13 @@ __device__ __forceinline__ void split_range(int L, int splits, int split, int& p
 
 // Attention splits per KV head for the new row p (rows 0..p attend).
 __device__ __forceinline__ int attn_splits(const StepArgs& A, int p) {
-  // a split's cost grows with its q heads: with 4 or 8 per KV head the
-  // splits start at 128 or 64 rows
+  // a split's cost grows with its q heads: with 4 per KV head the splits
+  // start at 128 rows, with 8 at 32 rows, and then take 32 rows each (one
+  // group of four rows per warp)
   const int hpg = A.nq / A.nkv;
-  const int one = hpg <= 2 ? kRowsPerSplit : kRowsPerSplit * 2 / hpg;
-  const int s = p < one ? 1 : (p + kRowsPerSplitLong) / kRowsPerSplitLong;
+  const int one = hpg <= 2 ? kRowsPerSplit : hpg == 4 ? kRowsPerSplit / 2 : kRowsPerSplitLong / 2;
+  const int per = hpg >= 8 ? kRowsPerSplitLong / 2 : kRowsPerSplitLong;
+  const int s = p < one ? 1 : (p + per) / per;
   return s < A.max_splits ? s : A.max_splits;
 }
 
@@ -654,11 +656,12 @@ __device__ __noinline__ void attn_phase(const StepArgs& A, StepHdr& H, unsigned 
   }
 
   // Each warp keeps its own online softmax over the rows it takes (rows
-  // [8w, 8w + 8) of every tile), so the tiles need no CTA barrier; the warps
-  // merge once at the end.  Scores are in the base-2 domain (q carries
+  // [4w, 4w + 4) and [32 + 4w, 36 + 4w) of every tile: a tile of up to 32
+  // rows gives every warp one group), so the tiles need no CTA barrier; the
+  // warps merge once at the end.  Scores are in the base-2 domain (q carries
   // scale * log2 e), so every exponential is one ex2.
   unsigned char* ring = smem + A.off_ring;
-  const int r0 = warp * 8;  // this warp's rows of a tile
+  const int r0 = warp * 4;  // this warp's first row of a tile
   for (int t = 0; t < ntile; ++t) {
     const int t0 = p0 + t * kAT;
     const int tn = min(kAT, p1 - t0);
@@ -670,7 +673,7 @@ __device__ __noinline__ void attn_phase(const StepArgs& A, StepHdr& H, unsigned 
     if (ok && r0 < tn) {
 #pragma unroll 1
       for (int g2 = 0; g2 < 2; ++g2) {
-        const int rb = r0 + 4 * g2;                  // first row of this group of four
+        const int rb = r0 + 32 * g2;                 // first row of this group of four
         const int nr = min(4, tn - rb);             // rows of the group in the tile
         if (nr <= 0) break;
         // the new row is never copied into the ring: it is read from S.knew / S.vnew
