@@ -1368,9 +1368,12 @@ int step_make_plan(const StepShape& sh, int num_sms, int budget, StepPlan* plan)
     A.bits[m] = bits;
   }
   if (moe) {
-    // the router reads the gate|up phase's staged x: the same place
+    // the router reads the gate|up phase's staged x: the same place, and the
+    // same code width (int4 staging pre-scales a quarter of x for the upper
+    // nibble), else the model decodes through the kernel chain
     const PGeom &r = A.geo[kMatRouter], &g = A.geo[kMatGu];
-    if (r.off_x != g.off_x || r.off_zero != g.off_zero || r.off_xs != g.off_xs || r.xslot_bytes != g.xslot_bytes)
+    if (r.off_x != g.off_x || r.off_zero != g.off_zero || r.off_xs != g.off_xs || r.xslot_bytes != g.xslot_bytes ||
+        r.bits != g.bits)
       return -1;
     A.moe = 1;
     A.n_experts = sh.n_experts;

@@ -364,7 +364,7 @@ int emx_qwen3_is_compiled(emx_qwen3* m, int* compiled);
  * set_fused(m, 0) selects one kernel per operation.  Setting 1 fails with
  * EMX_ERR_INVALID when the model has no such plan (sharded, group size != 64,
  * head_dim != 128, more than 8 q heads per KV head, more than 256 experts or
- * top-16). */
+ * top-16, router and experts of different bit widths). */
 int emx_qwen3_set_fused(emx_qwen3* m, int fused);
 int emx_qwen3_is_fused(emx_qwen3* m, int* fused);
 int emx_qwen3_step_launches(emx_qwen3* m, int* n);

@@ -292,6 +292,23 @@ def test_moe_persistent_step(ctx, name):
     print(f"{name}: {same} of {len(forced)} steps bit-identical to the kernel chain")
 
 
+def test_moe_mixed_router_bits_use_kernel_chain(ctx):
+    """An 8-bit router over 4-bit experts has no persistent plan (the step
+    kernel stages one x for both): such a model decodes through the kernel
+    chain, against the oracle."""
+    import dataclasses
+
+    cfg = dataclasses.replace(MOE_CFG, router_bits=8)
+    m = emx.Qwen3(ctx, cfg)
+    assert not m.fused
+    with pytest.raises(emx.EmxError):
+        m.fused = True
+    m.close()
+    rng = np.random.default_rng(13)
+    prompt = rng.integers(0, cfg.vocab, 12).astype(np.int32)
+    _run_both(ctx, cfg, 23, prompt, 4, rng, "moe router int8")
+
+
 def test_greedy_decode_paths_agree(ctx):
     """decode (n graph replays, one sync) == n x decode_step == oracle greedy chain."""
     cfg = DEEP_CFG
