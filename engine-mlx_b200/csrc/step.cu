@@ -1324,9 +1324,10 @@ int step_make_plan(const StepShape& sh, int num_sms, int budget, StepPlan* plan)
   if (hpg != 1 && hpg != 2 && hpg != 4 && hpg != 8) return -1;
   const bool moe = sh.n_experts > 0;
   if (sh.H % 64 != 0 || (!moe && sh.I % 64 != 0)) return -1;
-  // MoE: routing by one warp (up to 256 experts), the top-k slots' indices in
-  // shared memory, expert widths in whole 64-wide groups
-  if (moe && (sh.n_experts > kStepMaxExperts || sh.n_experts % 16 != 0 || sh.top_k < 1 ||
+  // MoE: routing with one expert per consumer thread (up to 256, their
+  // probabilities in the H-wide residual buffer), the top-k slots' indices
+  // in shared memory, expert widths in whole 64-wide groups
+  if (moe && (sh.n_experts > kStepMaxExperts || sh.n_experts > sh.H || sh.n_experts % 16 != 0 || sh.top_k < 1 ||
               sh.top_k > kStepMaxTopK || sh.top_k > sh.n_experts || sh.moe_inter % 64 != 0))
     return -1;
   StepPlan P{};
